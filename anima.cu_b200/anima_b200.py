@@ -1,0 +1,220 @@
+"""Python binding of libanima_b200.so, the B200 (sm_100a) fused layer kernels of anima.cu.
+
+The library's interface is the C ABI in include/anima_b200.h; this module binds it with
+ctypes and adds thin wrappers that take torch CUDA tensors (torch supplies device memory
+and streams; it is not on the compute path). Every wrapper launches exactly one of the
+library's kernels on the current torch stream (or the stream given) and raises
+AnimaError on a non-zero status.
+
+There is no fallback: if the shared library is missing or fails to load, importing this
+module raises. Build it with `make -C anima.cu_b200` (or __graft_entry__.build()).
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+from ctypes import c_char_p, c_float, c_int, c_int64, c_void_p
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "libanima_b200.so")
+
+P, I32, I64, F32 = c_void_p, c_int, c_int64, c_float
+
+# name -> argument types (all return int status). Mirrors include/anima_b200.h.
+SIGNATURES = {
+    "anima_rms_norm_bf16": (P, P, P, I32, I32, F32, P),
+    "anima_layer_norm_bf16": (P, P, I32, I32, F32, P),
+    "anima_adaln_layernorm_bf16": (P, P, P, P, I32, I32, F32, P),
+    "anima_residual_gate_adaln_bf16": (P, P, P, P, P, P, I32, I32, F32, P),
+    "anima_adaln_rms_norm_bf16": (P, P, P, P, I32, I32, F32, P),
+    "anima_gemma_rms_norm_bf16": (P, P, P, I32, I32, F32, P),
+    "anima_gelu_tanh_bf16": (P, P, I64, P),
+    "anima_gelu_tanh_bias_bf16": (P, P, P, I64, I32, P),
+    "anima_silu_bf16": (P, P, I64, P),
+    "anima_silu_bias_bf16": (P, P, P, I64, I32, P),
+    "anima_add_bf16": (P, P, P, I64, P),
+    "anima_mul_bf16": (P, P, P, I64, P),
+    "anima_scale_shift_bcast_bf16": (P, P, P, P, I32, I32, P),
+    "anima_residual_gate_bcast_bf16": (P, P, P, P, I32, I32, P),
+    "anima_gated_gelu_bf16": (P, P, P, I64, P),
+    "anima_rope_cosmos_strided_bf16": (P, P, P, I32, I32, I32, I32, P),
+    "anima_rope_standard_bf16": (P, P, P, I32, I32, I32, P),
+    "anima_embedding_lookup_bf16": (P, P, P, I32, I32, I32, P, P),
+    "anima_rms_norm_channel_bf16": (P, P, P, I32, I32, I32, F32, P),
+    "anima_rms_norm_channel_silu_bf16": (P, P, P, I32, I32, I32, F32, P),
+    "anima_qk_norm_rope_bf16": (P, P, P, P, I32, I32, I32, I32, F32, P),
+    "anima_swiglu_bf16": (P, P, P, I64, P),
+    "anima_layer_norm_modulate_bf16": (P, P, P, P, I32, I32, F32, P),
+    "anima_timestep_embedding_bf16": (F32, P, P, P, I32, F32, P),
+}
+
+# Status codes (include/anima_b200.h)
+ANIMA_OK = 0
+ANIMA_ERR_NULL_POINTER = -1
+ANIMA_ERR_BAD_SHAPE = -2
+ANIMA_ERR_MISALIGNED = -3
+ANIMA_ERR_TOO_LARGE = -4
+ANIMA_ERR_OVERLAP = -5
+ANIMA_ERR_NO_DEVICE = -6
+
+
+class AnimaError(RuntimeError):
+    def __init__(self, fn: str, status: int, text: str):
+        super().__init__(f"{fn} failed with status {status}: {text}")
+        self.status = status
+
+
+def _load() -> ctypes.CDLL:
+    if not os.path.exists(LIB_PATH):
+        raise ImportError(f"{LIB_PATH} is missing: build it with `make -C {_HERE}`")
+    lib = ctypes.CDLL(LIB_PATH)
+    for name, argtypes in SIGNATURES.items():
+        fn = getattr(lib, name)
+        fn.argtypes = list(argtypes)
+        fn.restype = c_int
+    lib.anima_status_string.argtypes = [c_int]
+    lib.anima_status_string.restype = c_char_p
+    lib.anima_version.argtypes = []
+    lib.anima_version.restype = c_char_p
+    lib.anima_compat_last_error.argtypes = []
+    lib.anima_compat_last_error.restype = c_int
+    return lib
+
+
+lib = _load()
+
+
+def version() -> str:
+    return lib.anima_version().decode()
+
+
+def status_string(status: int) -> str:
+    return lib.anima_status_string(status).decode()
+
+
+def call(name: str, *args) -> None:
+    """Calls a C entry point with raw arguments and raises on a non-zero status."""
+    st = getattr(lib, name)(*args)
+    if st != ANIMA_OK:
+        raise AnimaError(name, st, status_string(st))
+
+
+# ------------------------------------------------------------------ torch wrappers
+def _ptr(t):
+    return None if t is None else t.data_ptr()
+
+
+def _stream(stream):
+    import torch
+
+    s = torch.cuda.current_stream() if stream is None else stream
+    return s.cuda_stream
+
+
+def rms_norm(x, weight, out, N, D, eps=1e-6, stream=None):
+    call("anima_rms_norm_bf16", _ptr(x), _ptr(weight), _ptr(out), N, D, eps, _stream(stream))
+
+
+def layer_norm(x, out, N, D, eps=1e-6, stream=None):
+    call("anima_layer_norm_bf16", _ptr(x), _ptr(out), N, D, eps, _stream(stream))
+
+
+def adaln_layernorm(x, scale, shift, out, N, D, eps=1e-6, stream=None):
+    call("anima_adaln_layernorm_bf16", _ptr(x), _ptr(scale), _ptr(shift), _ptr(out), N, D, eps,
+         _stream(stream))
+
+
+def residual_gate_adaln(hidden, sub_out, gate, scale, shift, normed, N, D, eps=1e-6, stream=None):
+    call("anima_residual_gate_adaln_bf16", _ptr(hidden), _ptr(sub_out), _ptr(gate), _ptr(scale),
+         _ptr(shift), _ptr(normed), N, D, eps, _stream(stream))
+
+
+def adaln_rms_norm(x, scale, shift, out, N, D, eps=1e-6, stream=None):
+    call("anima_adaln_rms_norm_bf16", _ptr(x), _ptr(scale), _ptr(shift), _ptr(out), N, D, eps,
+         _stream(stream))
+
+
+def gemma_rms_norm(x, weight, out, N, D, eps=1e-6, stream=None):
+    call("anima_gemma_rms_norm_bf16", _ptr(x), _ptr(weight), _ptr(out), N, D, eps, _stream(stream))
+
+
+def gelu_tanh(x, out, N, stream=None):
+    call("anima_gelu_tanh_bf16", _ptr(x), _ptr(out), N, _stream(stream))
+
+
+def gelu_tanh_bias(x, bias, out, N, D, stream=None):
+    call("anima_gelu_tanh_bias_bf16", _ptr(x), _ptr(bias), _ptr(out), N, D, _stream(stream))
+
+
+def silu(x, out, N, stream=None):
+    call("anima_silu_bf16", _ptr(x), _ptr(out), N, _stream(stream))
+
+
+def silu_bias(x, bias, out, N, D, stream=None):
+    call("anima_silu_bias_bf16", _ptr(x), _ptr(bias), _ptr(out), N, D, _stream(stream))
+
+
+def add(a, b, out, N, stream=None):
+    call("anima_add_bf16", _ptr(a), _ptr(b), _ptr(out), N, _stream(stream))
+
+
+def mul(a, b, out, N, stream=None):
+    call("anima_mul_bf16", _ptr(a), _ptr(b), _ptr(out), N, _stream(stream))
+
+
+def scale_shift_bcast(x, scale, shift, out, M, D, stream=None):
+    call("anima_scale_shift_bcast_bf16", _ptr(x), _ptr(scale), _ptr(shift), _ptr(out), M, D,
+         _stream(stream))
+
+
+def residual_gate_bcast(x, y, gate, out, M, D, stream=None):
+    call("anima_residual_gate_bcast_bf16", _ptr(x), _ptr(y), _ptr(gate), _ptr(out), M, D,
+         _stream(stream))
+
+
+def gated_gelu(gate, up, out, N, stream=None):
+    call("anima_gated_gelu_bf16", _ptr(gate), _ptr(up), _ptr(out), N, _stream(stream))
+
+
+def rope_cosmos_strided(x, cos_t, sin_t, B, S, H, HD, stream=None):
+    call("anima_rope_cosmos_strided_bf16", _ptr(x), _ptr(cos_t), _ptr(sin_t), B, S, H, HD,
+         _stream(stream))
+
+
+def rope_standard(x, cos_t, sin_t, total_rows, T, D, stream=None):
+    call("anima_rope_standard_bf16", _ptr(x), _ptr(cos_t), _ptr(sin_t), total_rows, T, D,
+         _stream(stream))
+
+
+def embedding_lookup(table, ids, out, T, D, vocab=0, bad_id_count=None, stream=None):
+    call("anima_embedding_lookup_bf16", _ptr(table), _ptr(ids), _ptr(out), T, D, vocab,
+         _ptr(bad_id_count), _stream(stream))
+
+
+def rms_norm_channel(x, gamma, out, B, C, spatial, eps=1e-6, stream=None):
+    call("anima_rms_norm_channel_bf16", _ptr(x), _ptr(gamma), _ptr(out), B, C, spatial, eps,
+         _stream(stream))
+
+
+def rms_norm_channel_silu(x, gamma, out, B, C, spatial, eps=1e-6, stream=None):
+    call("anima_rms_norm_channel_silu_bf16", _ptr(x), _ptr(gamma), _ptr(out), B, C, spatial, eps,
+         _stream(stream))
+
+
+def qk_norm_rope(x, weight, cos_t, sin_t, B, S, H, HD, eps=1e-6, stream=None):
+    call("anima_qk_norm_rope_bf16", _ptr(x), _ptr(weight), _ptr(cos_t), _ptr(sin_t), B, S, H, HD,
+         eps, _stream(stream))
+
+
+def swiglu(gate, up, out, N, stream=None):
+    call("anima_swiglu_bf16", _ptr(gate), _ptr(up), _ptr(out), N, _stream(stream))
+
+
+def layer_norm_modulate(x, scale, shift, out, N, D, eps=1e-6, stream=None):
+    call("anima_layer_norm_modulate_bf16", _ptr(x), _ptr(scale), _ptr(shift), _ptr(out), N, D, eps,
+         _stream(stream))
+
+
+def timestep_embedding(t, norm_weight, sinusoid_out, normed_out, dim, eps=1e-6, stream=None):
+    call("anima_timestep_embedding_bf16", float(t), _ptr(norm_weight), _ptr(sinusoid_out),
+         _ptr(normed_out), dim, eps, _stream(stream))

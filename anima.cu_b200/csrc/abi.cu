@@ -1,0 +1,59 @@
+// abi.cu -- library-wide host helpers of the C ABI: device properties, status strings.
+#include <atomic>
+
+#include "common.cuh"
+
+namespace anima {
+
+namespace {
+constexpr int kMaxDevices = 64;
+std::atomic<int> g_sm_count[kMaxDevices];          // 0 = not queried yet
+std::atomic<unsigned> g_smem_slots[kMaxDevices];   // bit i set = slot i configured
+}  // namespace
+
+int sm_count() {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0) return 148;
+    if (dev >= kMaxDevices) {
+        int n = 0;
+        return cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess && n > 0 ? n : 148;
+    }
+    int n = g_sm_count[dev].load(std::memory_order_relaxed);
+    if (n > 0) return n;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) {
+        cudaGetLastError();  // do not leave the query's error for launch_status() to report
+        return 148;
+    }
+    g_sm_count[dev].store(n, std::memory_order_relaxed);
+    return n;
+}
+
+int allow_dynamic_smem(const void *kernel, int bytes, int slot) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return ANIMA_ERR_NO_DEVICE;
+    const unsigned bit = 1u << slot;
+    if (dev < kMaxDevices && (g_smem_slots[dev].load(std::memory_order_acquire) & bit)) return ANIMA_OK;
+    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    if (e != cudaSuccess) return (int)e;
+    if (dev < kMaxDevices) g_smem_slots[dev].fetch_or(bit, std::memory_order_acq_rel);
+    return ANIMA_OK;
+}
+
+}  // namespace anima
+
+extern "C" const char *anima_status_string(int status) {
+    switch (status) {
+    case ANIMA_OK: return "ANIMA_OK";
+    case ANIMA_ERR_NULL_POINTER: return "ANIMA_ERR_NULL_POINTER: a required pointer is NULL";
+    case ANIMA_ERR_BAD_SHAPE: return "ANIMA_ERR_BAD_SHAPE: invalid size argument";
+    case ANIMA_ERR_MISALIGNED: return "ANIMA_ERR_MISALIGNED: pointer not aligned to its element size";
+    case ANIMA_ERR_TOO_LARGE: return "ANIMA_ERR_TOO_LARGE: size overflows the index arithmetic";
+    case ANIMA_ERR_OVERLAP: return "ANIMA_ERR_OVERLAP: output partially overlaps an input";
+    case ANIMA_ERR_NO_DEVICE: return "ANIMA_ERR_NO_DEVICE: no current CUDA device";
+    default:
+        if (status > 0) return cudaGetErrorString((cudaError_t)status);
+        return "unknown anima status";
+    }
+}
+
+extern "C" const char *anima_version(void) { return "anima_b200 0.1.0 sm_100a"; }

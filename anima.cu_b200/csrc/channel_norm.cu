@@ -1,0 +1,170 @@
+// channel_norm.cu -- VAE channel RMSNorm (+ optional fused SiLU) on NCHW bf16 (sm_100a).
+//
+// out[b,c,s] = x[b,c,s] * rsqrt(mean_c x[b,:,s]^2 + eps) * gamma[c]      (vae_kernels.cu:60-81)
+//
+// The reduction runs over channels, which sit `spatial` elements apart. The reference
+// gives each pixel a thread that walks the channels with 2-byte strided loads, twice
+// (once for the sum, once for the output), launched once per batch item.
+//
+// Here one 256-thread CTA owns a tile of 64 consecutive pixels x all C channels of one
+// image. The tile is staged into shared memory with 16-byte cp.async copies (each
+// channel contributes one contiguous 128-byte segment, so every warp request is four
+// full segments), then one thread per pixel walks the channels in order -- the
+// reference's own summation order, so the statistics and outputs match it bit for bit
+// -- and finally all threads scale the tile out of shared memory with 16-byte stores.
+// x crosses HBM once and out once. Shared memory per CTA is C*128 bytes (64 KB at
+// C = 512: three CTAs per SM keep ~190 KB of loads in flight).
+//
+// Tensors whose rows are not 16-byte aligned (spatial % 8 != 0) or whose tile would not
+// fit in shared memory use the generic kernel: one thread per pixel, the reference's
+// arithmetic, one launch for all batch items.
+#include "common.cuh"
+
+namespace anima {
+namespace {
+
+constexpr int kCnBlock = 256;
+constexpr int kCnPix = 64;                  // pixels per tile
+constexpr int kCnMaxSmem = 200 * 1024;      // tile bytes we allow per CTA
+
+__device__ __forceinline__ float ldb(const anima_bf16 *p) {
+    return __bfloat162float(*reinterpret_cast<const __nv_bfloat16 *>(p));
+}
+
+__device__ __forceinline__ float silu_f(float v) { return v / (1.0f + expf(-v)); }  // silu.cu:20-21
+
+__device__ __forceinline__ void cp_async16(void *smem, const void *gmem) {
+    const unsigned s = (unsigned)__cvta_generic_to_shared(smem);
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(s), "l"(gmem) : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() {
+    asm volatile("cp.async.commit_group;\ncp.async.wait_group 0;" ::: "memory");
+}
+
+struct CnArgs {
+    const anima_bf16 *x, *gamma;
+    anima_bf16 *out;
+    int C, spatial;
+    float eps;
+    int tiles_per_image;
+};
+
+template <bool kSilu>
+__global__ void __launch_bounds__(kCnBlock) channel_norm_tile(CnArgs a) {
+    extern __shared__ __align__(16) anima_bf16 tile[];  // [C][kCnPix]
+    __shared__ float rms_s[kCnPix];
+    const int b = blockIdx.x / a.tiles_per_image;
+    const int s_tile = (blockIdx.x - b * a.tiles_per_image) * kCnPix;
+    const int live_vecs = min(kCnPix, a.spatial - s_tile) / 8;  // spatial % 8 == 0
+    const int64_t img = (int64_t)b * a.C * a.spatial;
+    const int nchunks = a.C * (kCnPix / 8);
+
+    // Stage: chunk q = (channel q/8, pixel vector q%8).
+    for (int q = threadIdx.x; q < nchunks; q += kCnBlock) {
+        const int c = q >> 3, v = q & 7;
+        if (v < live_vecs)
+            cp_async16(tile + c * kCnPix + v * 8, a.x + img + (int64_t)c * a.spatial + s_tile + v * 8);
+    }
+    cp_async_wait_all();
+    __syncthreads();
+
+    // vae_kernels.cu:68-73: serial sum over channels, one thread per pixel.
+    if (threadIdx.x < kCnPix) {
+        const int p = threadIdx.x;
+        float q = 0.0f;
+        if (p < live_vecs * 8) {
+            const __nv_bfloat16 *col = reinterpret_cast<const __nv_bfloat16 *>(tile) + p;
+            for (int c = 0; c < a.C; ++c) {
+                const float f = __bfloat162float(col[c * kCnPix]);
+                q = __fmaf_rn(f, f, q);
+            }
+        }
+        rms_s[p] = rsqrtf(__fdiv_rn(q, (float)a.C) + a.eps);
+    }
+    __syncthreads();
+
+    // vae_kernels.cu:75-80: out = (x * rms) * gamma[c], from shared memory.
+    for (int q = threadIdx.x; q < nchunks; q += kCnBlock) {
+        const int c = q >> 3, v = q & 7;
+        if (v >= live_vecs) continue;
+        const Vec8 xv = *reinterpret_cast<const Vec8 *>(tile + c * kCnPix + v * 8);
+        const float gm = ldb(a.gamma + c);
+        float f[8];
+        unpack8(xv, f);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+            float o = (f[e] * rms_s[v * 8 + e]) * gm;
+            if constexpr (kSilu) o = silu_f(bf16_round(o));
+            f[e] = o;
+        }
+        st_vec(a.out + img + (int64_t)c * a.spatial + s_tile + v * 8, pack8(f));
+    }
+}
+
+// Reference-order kernel for any shape: one thread per (image, pixel).
+template <bool kSilu>
+__global__ void channel_norm_serial(CnArgs a, int64_t pixels) {
+    for (int64_t p = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; p < pixels;
+         p += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t b = p / a.spatial, s = p % a.spatial;
+        const anima_bf16 *xb = a.x + b * a.C * (int64_t)a.spatial;
+        anima_bf16 *ob = a.out + b * a.C * (int64_t)a.spatial;
+        float q = 0.0f;
+        for (int c = 0; c < a.C; ++c) {
+            const float f = ldb(xb + (int64_t)c * a.spatial + s);
+            q = __fmaf_rn(f, f, q);
+        }
+        const float r = rsqrtf(__fdiv_rn(q, (float)a.C) + a.eps);
+        for (int c = 0; c < a.C; ++c) {
+            const int64_t i = (int64_t)c * a.spatial + s;
+            float o = (ldb(xb + i) * r) * ldb(a.gamma + c);
+            if constexpr (kSilu) o = silu_f(bf16_round(o));
+            *reinterpret_cast<__nv_bfloat16 *>(ob + i) = __float2bfloat16_rn(o);
+        }
+    }
+}
+
+template <bool kSilu>
+int channel_norm(const anima_bf16 *x, const anima_bf16 *gamma, anima_bf16 *out, int B, int C,
+                 int spatial, float eps, cudaStream_t stream) {
+    if (B < 0 || C <= 0 || spatial < 0) return ANIMA_ERR_BAD_SHAPE;
+    const int64_t n = (int64_t)B * C * spatial;
+    if (n == 0) return ANIMA_OK;
+    if (!x || !gamma || !out) return ANIMA_ERR_NULL_POINTER;
+    if (!aligned_to(x, 2) || !aligned_to(gamma, 2) || !aligned_to(out, 2)) return ANIMA_ERR_MISALIGNED;
+    if (partial_overlap(x, n * 2, out, n * 2) || partial_overlap(gamma, (int64_t)C * 2, out, n * 2))
+        return ANIMA_ERR_OVERLAP;
+    CnArgs a{x, gamma, out, C, spatial, eps, (spatial + kCnPix - 1) / kCnPix};
+    const int64_t tiles = (int64_t)B * a.tiles_per_image;
+    const int64_t smem = (int64_t)C * kCnPix * 2;
+    if (spatial % 8 == 0 && aligned16(x) && aligned16(out) && smem <= kCnMaxSmem &&
+        tiles < 2147483647) {
+        auto kern = channel_norm_tile<kSilu>;
+        if (int e = allow_dynamic_smem((const void *)kern, kCnMaxSmem, kSilu ? 1 : 0)) return e;
+        kern<<<(unsigned)tiles, kCnBlock, (size_t)smem, stream>>>(a);
+    } else {
+        const int64_t pixels = (int64_t)B * spatial;
+        int64_t blocks = (pixels + 255) / 256;
+        const int64_t wave = (int64_t)sm_count() * 8;
+        if (blocks > wave) blocks = wave;
+        channel_norm_serial<kSilu><<<(unsigned)blocks, 256, 0, stream>>>(a, pixels);
+    }
+    return launch_status();
+}
+
+}  // namespace
+}  // namespace anima
+
+using namespace anima;
+
+extern "C" int anima_rms_norm_channel_bf16(const anima_bf16 *x, const anima_bf16 *gamma,
+                                           anima_bf16 *out, int B, int C, int spatial, float eps,
+                                           anima_stream_t stream) {
+    return channel_norm<false>(x, gamma, out, B, C, spatial, eps, stream);
+}
+
+extern "C" int anima_rms_norm_channel_silu_bf16(const anima_bf16 *x, const anima_bf16 *gamma,
+                                                anima_bf16 *out, int B, int C, int spatial,
+                                                float eps, anima_stream_t stream) {
+    return channel_norm<true>(x, gamma, out, B, C, spatial, eps, stream);
+}

@@ -1,0 +1,215 @@
+// common.cuh -- device helpers shared by the anima_b200 kernels (sm_100a).
+//
+// Memory: every hot kernel moves 16-byte vectors (8 bf16) with explicit PTX loads and
+// stores. Streamed tensors bypass L1 (L1::no_allocate); the small broadcast vectors
+// (scale/shift/gate/weights, RoPE tables) use the default cached path.
+//
+// Numerics: outputs must match the reference kernels' rounding. Pair sums and sums of
+// squares therefore go through `ref_pair_tree_sum`, which replays, in registers, the
+// exact addition tree of the reference's one-CTA-per-row reduction.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cuda_bf16.h>
+#include <stdint.h>
+
+#include "../../include/anima_b200.h"
+
+namespace anima {
+
+// ----------------------------------------------------------------- 16-byte I/O
+
+struct alignas(16) Vec8 {
+    uint32_t w[4];  // four packed bf16 pairs, element 2i in the low half of w[i]
+};
+
+// Streamed read: no L1 allocation (each byte is read once per kernel).
+__device__ __forceinline__ Vec8 ld_stream(const void *p) {
+    Vec8 r;
+    asm volatile("ld.global.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r.w[0]), "=r"(r.w[1]), "=r"(r.w[2]), "=r"(r.w[3])
+                 : "l"(p));
+    return r;
+}
+
+// Cached read for broadcast vectors and tables that many warps re-read.
+__device__ __forceinline__ Vec8 ld_cached(const void *p) {
+    Vec8 r;
+    asm volatile("ld.global.v4.u32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r.w[0]), "=r"(r.w[1]), "=r"(r.w[2]), "=r"(r.w[3])
+                 : "l"(p));
+    return r;
+}
+
+__device__ __forceinline__ void st_vec(void *p, const Vec8 &v) {
+    asm volatile("st.global.v4.u32 [%0], {%1,%2,%3,%4};" ::"l"(p), "r"(v.w[0]), "r"(v.w[1]),
+                 "r"(v.w[2]), "r"(v.w[3])
+                 : "memory");
+}
+
+__device__ __forceinline__ float bf_lo(uint32_t w) { return __uint_as_float(w << 16); }
+__device__ __forceinline__ float bf_hi(uint32_t w) { return __uint_as_float(w & 0xffff0000u); }
+
+// Round two floats to a packed bf16 pair (RNE), like __floats2bfloat162_rn.
+__device__ __forceinline__ uint32_t pack_bf2(float lo, float hi) {
+    __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
+    return *reinterpret_cast<uint32_t *>(&h);
+}
+
+__device__ __forceinline__ void unpack8(const Vec8 &v, float (&f)[8]) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        f[2 * i] = bf_lo(v.w[i]);
+        f[2 * i + 1] = bf_hi(v.w[i]);
+    }
+}
+
+__device__ __forceinline__ Vec8 pack8(const float (&f)[8]) {
+    Vec8 v;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) v.w[i] = pack_bf2(f[2 * i], f[2 * i + 1]);
+    return v;
+}
+
+__device__ __forceinline__ float bf16_round(float f) {
+    return __bfloat162float(__float2bfloat16_rn(f));
+}
+
+// ------------------------------------------------- reference reduction replay
+//
+// The reference reduces a row of D2 = D/2 bf16 pairs with one CTA of T = D2 threads
+// (D2 <= 1024 and a multiple of 32): thread t owns pair t, each warp reduces its 32
+// values with __shfl_down_sync offsets 16,8,4,2,1 (cuda_utils.cuh:46-50), warp 0 then
+// reduces the per-warp results the same way, padded with zeros to 32
+// (layer_norm.cu:7-19, rms_norm.cu:40-53). Floating-point addition is commutative but
+// not associative, so matching its bits means matching that tree.
+//
+// Here a row is owned by a "team" of LPR lanes (8, 16 or 32) of one warp. Lane l of the
+// team holds chunks c = l + LPR*k (k < K) of 8 elements, i.e. pairs p = 4c + j (j < 4).
+// Reference thread p sits in reference warp w = c/8 at reference lane r = 4(c%8) + j.
+// So reference offsets 16/8/4 are lane XORs 4/2/1 inside the team (c%8 = l%8 since
+// LPR % 8 == 0), and offsets 2/1 pair up j inside one lane. The warp-level tree runs as
+// a transposed butterfly: at each lane-XOR step a lane keeps half of its k values and
+// ships the other half to its partner, so K=8 costs 16+8+4 shuffles instead of 96.
+// After it, lane l holds the sum of reference warp w = (l>>3) + (LPR/8)*k*(l), and the
+// second-level tree over w maps each reference offset onto one more lane XOR.
+
+template <int N>
+struct Log2 {
+    static constexpr int value = 1 + Log2<N / 2>::value;
+};
+template <>
+struct Log2<1> {
+    static constexpr int value = 0;
+};
+
+// One lane-XOR step of the warp-level tree over values cur[M][4] (M = live k values).
+template <int M>
+struct TreeStep {
+    static constexpr int OUT = M > 1 ? M / 2 : 1;
+    __device__ __forceinline__ static void run(const float (&cur)[M][4], float (&nxt)[OUT][4],
+                                               int bit, int l, unsigned mask) {
+        if constexpr (M > 1) {
+            const bool upper = (l >> bit) & 1;
+#pragma unroll
+            for (int i = 0; i < M / 2; ++i)
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    float keep = upper ? cur[i + M / 2][j] : cur[i][j];
+                    float send = upper ? cur[i][j] : cur[i + M / 2][j];
+                    nxt[i][j] = keep + __shfl_xor_sync(mask, send, 1 << bit);
+                }
+        } else {
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+                nxt[0][j] = cur[0][j] + __shfl_xor_sync(mask, cur[0][j], 1 << bit);
+        }
+    }
+};
+
+// Full reference block sum of the row's pair values v[k][j]; every lane of the team
+// receives the result. LPR in {8,16,32}, K in {1,2,4,8}, D = 8*LPR*K <= 2048.
+template <int LPR, int K>
+__device__ __forceinline__ float ref_pair_tree_sum(const float (&v)[K][4], int l, unsigned mask) {
+    static_assert(LPR == 8 || LPR == 16 || LPR == 32, "team size");
+    static_assert(K == 1 || K == 2 || K == 4 || K == 8, "chunks per lane");
+    constexpr int M1 = TreeStep<K>::OUT;
+    constexpr int M2 = TreeStep<M1>::OUT;
+    constexpr int M3 = TreeStep<M2>::OUT;
+    float a[M1][4], b[M2][4], c[M3][4];
+    TreeStep<K>::run(v, a, 2, l, mask);   // reference offset 16
+    TreeStep<M1>::run(a, b, 1, l, mask);  // reference offset 8
+    TreeStep<M2>::run(b, c, 0, l, mask);  // reference offset 4
+    // reference offsets 2 and 1: pairs j^2, then j^1, inside the lane
+    float s = (c[0][0] + c[0][2]) + (c[0][1] + c[0][3]);
+
+    // Second level: reference warp 0 over w = (l>>3) + G*kstar, zero-padded to 32.
+    constexpr int LG_G = Log2<LPR / 8>::value;
+    constexpr int LG_K = Log2<K>::value;
+    constexpr int NW = (LPR / 8) * K;  // reference warps in the row
+#pragma unroll
+    for (int i = 4; i >= 0; --i) {
+        if ((1 << i) >= NW) continue;  // partner slot holds a padding zero: x + 0 == x
+        const int lane_bit = i < LG_G ? 3 + i : (i - LG_G) + 3 - LG_K;
+        s = s + __shfl_xor_sync(mask, s, 1 << lane_bit);
+    }
+    return s;
+}
+
+// The reference's CTA reduction itself (warp shfl_down tree, then warp 0 over the
+// per-warp sums), for the generic one-CTA-per-row kernels. `red` holds >= 32 floats.
+// Returns the total to every thread. Contains __syncthreads.
+__device__ __forceinline__ float ref_cta_sum(float v, float *red) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int nwarps = (blockDim.x + 31) >> 5;
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) v += __shfl_down_sync(0xffffffffu, v, off);
+    if (lane == 0) red[warp] = v;
+    __syncthreads();
+    if (warp == 0) {
+        v = lane < nwarps ? red[lane] : 0.0f;
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) v += __shfl_down_sync(0xffffffffu, v, off);
+        if (lane == 0) red[32] = v;
+    }
+    __syncthreads();
+    float total = red[32];
+    __syncthreads();  // red may be reused by the caller's next reduction
+    return total;
+}
+
+// Block size the reference launchers use for a row of D elements (rms_norm.cu:126-128).
+__host__ __device__ __forceinline__ int ref_row_threads(int D) {
+    int D2 = D / 2;
+    int t = (D2 <= 1024) ? ((D2 + 31) / 32 * 32) : 1024;
+    return t < 32 ? 32 : t;
+}
+
+// ------------------------------------------------------------------ host side
+
+// Number of SMs of the current device (cached per device ordinal).
+int sm_count();
+
+// Raises a kernel's dynamic shared-memory limit to `bytes` on the current device, once
+// per (device, slot); `slot` names the kernel (0..15). Returns ANIMA_OK or a cudaError_t.
+int allow_dynamic_smem(const void *kernel, int bytes, int slot);
+
+inline bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+inline bool aligned_to(const void *p, unsigned a) {
+    return (reinterpret_cast<uintptr_t>(p) & (a - 1)) == 0;
+}
+
+// True when [a, a+na) and [b, b+nb) overlap without being the same buffer start.
+inline bool partial_overlap(const void *a, int64_t na, const void *b, int64_t nb) {
+    uintptr_t x = reinterpret_cast<uintptr_t>(a), y = reinterpret_cast<uintptr_t>(b);
+    if (x == y) return false;
+    return x < y + (uintptr_t)nb && y < x + (uintptr_t)na;
+}
+
+// Status of the launch just issued (launch-configuration errors only; kernels run async).
+inline int launch_status() {
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? ANIMA_OK : (int)e;
+}
+
+}  // namespace anima

@@ -1,0 +1,277 @@
+// elementwise.cu -- GELU / SiLU / add / mul / broadcast modulate and gate kernels (sm_100a).
+//
+// One grid-stride kernel template covers them all: NS streamed bf16 inputs (1 or 2)
+// read as 16-byte chunks with L1-bypassing loads, NB broadcast vectors (0..2) indexed by
+// column (element % D, read through L1), and an Op that maps fp32 inputs to one fp32
+// output. Each thread keeps U chunks per input in flight. The grid is sized to one
+// resident wave (SMs x 2048 threads) and loops, so a launch costs the same at any size.
+// Elements past the last full chunk, and every element when a pointer is not 16-byte
+// aligned, take a scalar path inside the same launch.
+//
+// The per-element arithmetic is the reference's own expression for each op (file:line
+// at each Op), so results are bit-identical to the reference kernels.
+#include "common.cuh"
+
+namespace anima {
+namespace {
+
+constexpr int kEwBlock = 256;
+
+// gelu.cu:22-31: tanh-GELU with the reference's constants and fma placement.
+__device__ __forceinline__ float gelu_tanh_f(float v) {
+    const float inner = 0.7978845608028654f * __fmaf_rn(0.044715f * (v * v), v, v);
+    const float hv = 0.5f * v;
+    return __fmaf_rn(hv, tanhf(inner), hv);
+}
+
+// silu.cu:20-21
+__device__ __forceinline__ float silu_f(float v) { return v / (1.0f + expf(-v)); }
+
+struct OpGelu {  // gelu.cu:12-34
+    static constexpr int NS = 1, NB = 0;
+    __device__ float operator()(const float (&s)[2], const float (&)[2]) const { return gelu_tanh_f(s[0]); }
+};
+struct OpGeluBias {  // gelu.cu:37-64
+    static constexpr int NS = 1, NB = 1;
+    __device__ float operator()(const float (&s)[2], const float (&b)[2]) const {
+        return gelu_tanh_f(s[0] + b[0]);
+    }
+};
+struct OpSilu {  // silu.cu:7-24
+    static constexpr int NS = 1, NB = 0;
+    __device__ float operator()(const float (&s)[2], const float (&)[2]) const { return silu_f(s[0]); }
+};
+struct OpSiluBias {  // silu.cu:26-47
+    static constexpr int NS = 1, NB = 1;
+    __device__ float operator()(const float (&s)[2], const float (&b)[2]) const { return silu_f(s[0] + b[0]); }
+};
+struct OpAdd {  // elementwise.cu:37-53
+    static constexpr int NS = 2, NB = 0;
+    __device__ float operator()(const float (&s)[2], const float (&)[2]) const { return s[0] + s[1]; }
+};
+struct OpMul {  // elementwise.cu:125-141
+    static constexpr int NS = 2, NB = 0;
+    __device__ float operator()(const float (&s)[2], const float (&)[2]) const { return s[0] * s[1]; }
+};
+struct OpSwiGLU {  // silu.cu:7-24 on gate, rounded to bf16, then elementwise.cu:125-141
+    static constexpr int NS = 2, NB = 0;
+    __device__ float operator()(const float (&s)[2], const float (&)[2]) const {
+        return bf16_round(silu_f(s[0])) * s[1];
+    }
+};
+struct OpGatedGelu {  // gemma_ops.cu:5-22 (scalar formula; nvcc folds the cubic into an fma)
+    static constexpr int NS = 2, NB = 0;
+    __device__ float operator()(const float (&s)[2], const float (&)[2]) const {
+        const float g = s[0];
+        const float inner = 0.7978845608f * __fmaf_rn(0.044715f * g * g, g, g);
+        return (0.5f * g * (1.0f + tanhf(inner))) * s[1];
+    }
+};
+struct OpScaleShift {  // elementwise.cu:216-236: fma(x, 1+scale[d], shift[d])
+    static constexpr int NS = 1, NB = 2;
+    __device__ float operator()(const float (&s)[2], const float (&b)[2]) const {
+        return __fmaf_rn(s[0], 1.0f + b[0], b[1]);
+    }
+};
+struct OpResidualGate {  // elementwise.cu:249-269: fma(y, gate[d], x)
+    static constexpr int NS = 2, NB = 1;
+    __device__ float operator()(const float (&s)[2], const float (&b)[2]) const {
+        return __fmaf_rn(s[1], b[0], s[0]);
+    }
+};
+
+struct EwArgs {
+    const anima_bf16 *s0, *s1;  // streamed inputs
+    const anima_bf16 *b0, *b1;  // broadcast vectors [D]
+    anima_bf16 *out;
+    int64_t n;       // elements to process
+    int D;           // broadcast period (elements); 0 when NB == 0
+    bool vec;        // 16-byte path usable
+};
+
+__device__ __forceinline__ float ldb(const anima_bf16 *p) {
+    return __bfloat162float(*reinterpret_cast<const __nv_bfloat16 *>(p));
+}
+
+template <class Op, int U>
+__global__ void __launch_bounds__(kEwBlock) ew_kernel(EwArgs a, Op op) {
+    constexpr int NS = Op::NS, NB = Op::NB;
+    const int64_t tid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    int64_t done = 0;  // elements covered by the vector loop
+    if (a.vec) {
+        const int64_t nch = a.n >> 3;
+        done = nch << 3;
+        const uint32_t dch = NB ? (uint32_t)(a.D >> 3) : 1u;
+        for (int64_t base = tid; base < nch; base += stride * U) {
+            Vec8 in[U][NS > 1 ? 2 : 1];
+#pragma unroll
+            for (int u = 0; u < U; ++u) {
+                const int64_t i = base + u * stride;
+                if (i < nch) {
+                    in[u][0] = ld_stream(a.s0 + i * 8);
+                    if constexpr (NS > 1) in[u][NS - 1] = ld_stream(a.s1 + i * 8);
+                }
+            }
+#pragma unroll
+            for (int u = 0; u < U; ++u) {
+                const int64_t i = base + u * stride;
+                if (i >= nch) break;
+                float f0[8], f1[8], g0[8], g1[8];
+                unpack8(in[u][0], f0);
+                if constexpr (NS > 1) unpack8(in[u][NS - 1], f1);
+                if constexpr (NB > 0) {
+                    // column chunk of this chunk; chunk counts stay below 2^32 for any
+                    // tensor that fits in memory at 8 elements per chunk x 2 bytes
+                    const uint32_t c = (uint32_t)((uint64_t)i % dch);
+                    unpack8(ld_cached(a.b0 + (int64_t)c * 8), g0);
+                    if constexpr (NB > 1) unpack8(ld_cached(a.b1 + (int64_t)c * 8), g1);
+                }
+                float r[8];
+#pragma unroll
+                for (int e = 0; e < 8; ++e) {
+                    float s[2] = {f0[e], NS > 1 ? f1[e] : 0.0f};
+                    float b[2] = {NB > 0 ? g0[e] : 0.0f, NB > 1 ? g1[e] : 0.0f};
+                    r[e] = op(s, b);
+                }
+                st_vec(a.out + i * 8, pack8(r));
+            }
+        }
+    }
+    // Scalar path: the tail past the last full chunk, or everything when misaligned.
+    for (int64_t e = done + tid; e < a.n; e += stride) {
+        float s[2] = {ldb(a.s0 + e), NS > 1 ? ldb(a.s1 + e) : 0.0f};
+        float b[2] = {0.0f, 0.0f};
+        if constexpr (NB > 0) {
+            const int64_t d = e % a.D;
+            b[0] = ldb(a.b0 + d);
+            if constexpr (NB > 1) b[1] = ldb(a.b1 + d);
+        }
+        *reinterpret_cast<__nv_bfloat16 *>(a.out + e) = __float2bfloat16_rn(op(s, b));
+    }
+}
+
+template <class Op>
+int launch_ew(const EwArgs &a, cudaStream_t stream) {
+    if (a.n <= 0) return ANIMA_OK;
+    constexpr int U = Op::NS > 1 ? 2 : 4;
+    const int64_t work = a.vec ? ((a.n >> 3) + U - 1) / U : a.n;
+    int64_t blocks = (work + kEwBlock - 1) / kEwBlock;
+    const int64_t wave = (int64_t)sm_count() * (2048 / kEwBlock);
+    if (blocks > wave) blocks = wave;
+    if (blocks < 1) blocks = 1;
+    ew_kernel<Op, U><<<(unsigned)blocks, kEwBlock, 0, stream>>>(a, Op{});
+    return launch_status();
+}
+
+bool bf16_ok(const void *p) { return aligned_to(p, 2); }
+
+// Validates and launches a flat op over n elements (n = 2*floor(N/2), as the reference's
+// pair loop covers).
+template <class Op>
+int flat_op(const anima_bf16 *s0, const anima_bf16 *s1, const anima_bf16 *bias, anima_bf16 *out,
+            int64_t N, int D, cudaStream_t stream) {
+    constexpr int NS = Op::NS, NB = Op::NB;
+    if (N < 0) return ANIMA_ERR_BAD_SHAPE;
+    if (NB > 0 && (D <= 0 || (D & 1))) return ANIMA_ERR_BAD_SHAPE;
+    const int64_t n = N / 2 * 2;
+    if (n == 0) return ANIMA_OK;
+    if (!s0 || !out || (NS > 1 && !s1) || (NB > 0 && !bias)) return ANIMA_ERR_NULL_POINTER;
+    if (!bf16_ok(s0) || !bf16_ok(out) || (NS > 1 && !bf16_ok(s1)) || (NB > 0 && !bf16_ok(bias)))
+        return ANIMA_ERR_MISALIGNED;
+    if (n > INT64_MAX / 2) return ANIMA_ERR_TOO_LARGE;
+    if (partial_overlap(s0, n * 2, out, n * 2) || (NS > 1 && partial_overlap(s1, n * 2, out, n * 2)))
+        return ANIMA_ERR_OVERLAP;
+    EwArgs a{s0, NS > 1 ? s1 : nullptr, NB > 0 ? bias : nullptr, nullptr, out, n, NB > 0 ? D : 0, false};
+    a.vec = aligned16(s0) && aligned16(out) && (NS < 2 || aligned16(s1)) &&
+            (NB == 0 || (aligned16(bias) && D % 8 == 0));
+    return launch_ew<Op>(a, stream);
+}
+
+// Validates and launches a row-broadcast op over [M, D].
+template <class Op>
+int bcast_op(const anima_bf16 *x, const anima_bf16 *y, const anima_bf16 *b0, const anima_bf16 *b1,
+             anima_bf16 *out, int M, int D, cudaStream_t stream) {
+    constexpr int NS = Op::NS, NB = Op::NB;
+    if (M < 0 || D <= 0 || (D & 1)) return ANIMA_ERR_BAD_SHAPE;
+    const int64_t n = (int64_t)M * D;
+    if (n == 0) return ANIMA_OK;
+    if (!x || !out || (NS > 1 && !y) || !b0 || (NB > 1 && !b1)) return ANIMA_ERR_NULL_POINTER;
+    if (!bf16_ok(x) || !bf16_ok(out) || (NS > 1 && !bf16_ok(y)) || !bf16_ok(b0) ||
+        (NB > 1 && !bf16_ok(b1)))
+        return ANIMA_ERR_MISALIGNED;
+    if (partial_overlap(x, n * 2, out, n * 2) || (NS > 1 && partial_overlap(y, n * 2, out, n * 2)))
+        return ANIMA_ERR_OVERLAP;
+    EwArgs a{x, NS > 1 ? y : nullptr, b0, NB > 1 ? b1 : nullptr, out, n, D, false};
+    a.vec = D % 8 == 0 && aligned16(x) && aligned16(out) && (NS < 2 || aligned16(y)) &&
+            aligned16(b0) && (NB < 2 || aligned16(b1));
+    return launch_ew<Op>(a, stream);
+}
+
+}  // namespace
+}  // namespace anima
+
+using namespace anima;
+
+// ================================================================ C ABI
+
+extern "C" int anima_gelu_tanh_bf16(const anima_bf16 *x, anima_bf16 *out, int64_t N,
+                                    anima_stream_t stream) {
+    return flat_op<OpGelu>(x, nullptr, nullptr, out, N, 0, stream);
+}
+
+extern "C" int anima_gelu_tanh_bias_bf16(const anima_bf16 *x, const anima_bf16 *bias,
+                                         anima_bf16 *out, int64_t N, int D, anima_stream_t stream) {
+    return flat_op<OpGeluBias>(x, nullptr, bias, out, N, D, stream);
+}
+
+extern "C" int anima_silu_bf16(const anima_bf16 *x, anima_bf16 *out, int64_t N,
+                               anima_stream_t stream) {
+    return flat_op<OpSilu>(x, nullptr, nullptr, out, N, 0, stream);
+}
+
+extern "C" int anima_silu_bias_bf16(const anima_bf16 *x, const anima_bf16 *bias, anima_bf16 *out,
+                                    int64_t N, int D, anima_stream_t stream) {
+    return flat_op<OpSiluBias>(x, nullptr, bias, out, N, D, stream);
+}
+
+extern "C" int anima_add_bf16(const anima_bf16 *a, const anima_bf16 *b, anima_bf16 *out, int64_t N,
+                              anima_stream_t stream) {
+    return flat_op<OpAdd>(a, b, nullptr, out, N, 0, stream);
+}
+
+extern "C" int anima_mul_bf16(const anima_bf16 *a, const anima_bf16 *b, anima_bf16 *out, int64_t N,
+                              anima_stream_t stream) {
+    return flat_op<OpMul>(a, b, nullptr, out, N, 0, stream);
+}
+
+extern "C" int anima_swiglu_bf16(const anima_bf16 *gate, const anima_bf16 *up, anima_bf16 *out,
+                                 int64_t N, anima_stream_t stream) {
+    return flat_op<OpSwiGLU>(gate, up, nullptr, out, N, 0, stream);
+}
+
+extern "C" int anima_gated_gelu_bf16(const anima_bf16 *gate, const anima_bf16 *up, anima_bf16 *out,
+                                     int64_t N, anima_stream_t stream) {
+    // gemma_ops.cu:24-31 covers every element (no pair loop): process N, not 2*floor(N/2).
+    if (N < 0) return ANIMA_ERR_BAD_SHAPE;
+    if (N == 0) return ANIMA_OK;
+    if (!gate || !up || !out) return ANIMA_ERR_NULL_POINTER;
+    if (!bf16_ok(gate) || !bf16_ok(up) || !bf16_ok(out)) return ANIMA_ERR_MISALIGNED;
+    if (partial_overlap(gate, N * 2, out, N * 2) || partial_overlap(up, N * 2, out, N * 2))
+        return ANIMA_ERR_OVERLAP;
+    EwArgs a{gate, up, nullptr, nullptr, out, N, 0, false};
+    a.vec = aligned16(gate) && aligned16(up) && aligned16(out);
+    return launch_ew<OpGatedGelu>(a, stream);
+}
+
+extern "C" int anima_scale_shift_bcast_bf16(const anima_bf16 *x, const anima_bf16 *scale,
+                                            const anima_bf16 *shift, anima_bf16 *out, int M, int D,
+                                            anima_stream_t stream) {
+    return bcast_op<OpScaleShift>(x, nullptr, scale, shift, out, M, D, stream);
+}
+
+extern "C" int anima_residual_gate_bcast_bf16(const anima_bf16 *x, const anima_bf16 *y,
+                                              const anima_bf16 *gate, anima_bf16 *out, int M, int D,
+                                              anima_stream_t stream) {
+    return bcast_op<OpResidualGate>(x, y, gate, nullptr, out, M, D, stream);
+}

@@ -1,0 +1,310 @@
+// rope.cu -- rotary embeddings (sm_100a): Cosmos 3-axis half-split RoPE on the strided
+// [B*S, H*HD] layout, the standard half-split RoPE with fp32 tables, and the fused
+// per-head QK RMSNorm + Cosmos RoPE.
+//
+// Work unit = one 8-element chunk of the first half of one head of one row, plus the
+// matching chunk of the second half: two 16-byte streamed loads of x, 16-byte cached
+// loads of the cos/sin table row (shared by every head of a token, so it is read from
+// L1/L2, not HBM), two 16-byte stores. Two units per thread per step keep four
+// streamed loads in flight. The reference instead runs one thread per element pair
+// with scalar 2-byte accesses and 64-bit div/mod per thread (rope.cu:72-108).
+#include "common.cuh"
+
+namespace anima {
+namespace {
+
+constexpr int kRopeBlock = 256;
+constexpr int kRopeU = 2;
+
+__device__ __forceinline__ float ldb(const anima_bf16 *p) {
+    return __bfloat162float(*reinterpret_cast<const __nv_bfloat16 *>(p));
+}
+__device__ __forceinline__ void stb(anima_bf16 *p, float f) {
+    *reinterpret_cast<__nv_bfloat16 *>(p) = __float2bfloat16_rn(f);
+}
+
+// rope.cu:101-107. Every operand is a bf16 value, so both products are exact in fp32 and
+// the result has one rounding however the expression is contracted.
+__device__ __forceinline__ void rot_bf16(float xr, float xi, float c, float s, float &o_r, float &o_i) {
+    o_r = __fmaf_rn(xr, c, -(xi * s));
+    o_i = __fmaf_rn(xi, c, xr * s);
+}
+
+// gemma_ops.cu:81-85 with fp32 tables: x1*c - x2*s and x2*c + x1*s. nvcc contracts each
+// into one fma, folding the first product.
+__device__ __forceinline__ void rot_f32(float x1, float x2, float c, float s, float &o1, float &o2) {
+    o1 = __fmaf_rn(x1, c, -(x2 * s));
+    o2 = __fmaf_rn(x2, c, x1 * s);
+}
+
+struct CosmosArgs {
+    anima_bf16 *x;
+    const anima_bf16 *cos_t, *sin_t;
+    int S, H, HD;
+    int64_t units;   // rows * H * (HD/16)
+    uint32_t hc;     // chunks per half head = HD/16
+};
+
+__global__ void __launch_bounds__(kRopeBlock) rope_cosmos_vec(CosmosArgs a) {
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    const uint32_t per_row = (uint32_t)a.H * a.hc;
+    const int half = a.HD / 2;
+    for (int64_t base = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; base < a.units;
+         base += stride * kRopeU) {
+        Vec8 xr[kRopeU], xi[kRopeU], cv[kRopeU], sv[kRopeU];
+        anima_bf16 *p[kRopeU];
+#pragma unroll
+        for (int u = 0; u < kRopeU; ++u) {
+            const int64_t i = base + u * stride;
+            if (i >= a.units) break;
+            const int64_t row = i / per_row;
+            const uint32_t rem = (uint32_t)(i - row * per_row);
+            const uint32_t h = rem / a.hc, c = rem - h * a.hc;
+            const int64_t s = row % a.S;
+            p[u] = a.x + row * (int64_t)a.H * a.HD + (int64_t)h * a.HD + c * 8;
+            xr[u] = ld_stream(p[u]);
+            xi[u] = ld_stream(p[u] + half);
+            cv[u] = ld_cached(a.cos_t + s * a.HD + c * 8);
+            sv[u] = ld_cached(a.sin_t + s * a.HD + c * 8);
+        }
+#pragma unroll
+        for (int u = 0; u < kRopeU; ++u) {
+            if (base + u * stride >= a.units) break;
+            float r[8], im[8], c[8], s[8], o_r[8], o_i[8];
+            unpack8(xr[u], r);
+            unpack8(xi[u], im);
+            unpack8(cv[u], c);
+            unpack8(sv[u], s);
+#pragma unroll
+            for (int e = 0; e < 8; ++e) rot_bf16(r[e], im[e], c[e], s[e], o_r[e], o_i[e]);
+            st_vec(p[u], pack8(o_r));
+            st_vec(p[u] + half, pack8(o_i));
+        }
+    }
+}
+
+// One thread per element pair, scalar accesses (any even HD, any 2-byte alignment).
+__global__ void rope_cosmos_scalar(anima_bf16 *x, const anima_bf16 *cos_t, const anima_bf16 *sin_t,
+                                   int S, int H, int HD, int64_t pairs) {
+    const int half = HD / 2;
+    const int64_t per_row = (int64_t)H * half;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < pairs;
+         i += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t row = i / per_row, rem = i % per_row;
+        const int64_t h = rem / half, k = rem % half, s = row % S;
+        anima_bf16 *b = x + row * H * HD + h * HD;
+        float o_r, o_i;
+        rot_bf16(ldb(b + k), ldb(b + k + half), ldb(cos_t + s * HD + k), ldb(sin_t + s * HD + k), o_r, o_i);
+        stb(b + k, o_r);
+        stb(b + k + half, o_i);
+    }
+}
+
+struct StdArgs {
+    anima_bf16 *x;
+    const float *cos_t, *sin_t;
+    int T, D;
+    int64_t units;  // rows * (D/16)
+    uint32_t hc;    // chunks per half row = D/16
+};
+
+__global__ void __launch_bounds__(kRopeBlock) rope_standard_vec(StdArgs a) {
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    const int half = a.D / 2;
+    for (int64_t base = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; base < a.units;
+         base += stride * kRopeU) {
+        Vec8 x1[kRopeU], x2[kRopeU];
+        float4 cv[kRopeU][2], sv[kRopeU][2];
+        anima_bf16 *p[kRopeU];
+#pragma unroll
+        for (int u = 0; u < kRopeU; ++u) {
+            const int64_t i = base + u * stride;
+            if (i >= a.units) break;
+            const int64_t row = i / a.hc;
+            const uint32_t c = (uint32_t)(i - row * a.hc);
+            const int64_t t = row % a.T;
+            p[u] = a.x + row * a.D + c * 8;
+            x1[u] = ld_stream(p[u]);
+            x2[u] = ld_stream(p[u] + half);
+            const float4 *cp = reinterpret_cast<const float4 *>(a.cos_t + t * half + c * 8);
+            const float4 *sp = reinterpret_cast<const float4 *>(a.sin_t + t * half + c * 8);
+            cv[u][0] = __ldg(cp);
+            cv[u][1] = __ldg(cp + 1);
+            sv[u][0] = __ldg(sp);
+            sv[u][1] = __ldg(sp + 1);
+        }
+#pragma unroll
+        for (int u = 0; u < kRopeU; ++u) {
+            if (base + u * stride >= a.units) break;
+            float f1[8], f2[8], o1[8], o2[8];
+            unpack8(x1[u], f1);
+            unpack8(x2[u], f2);
+            const float c[8] = {cv[u][0].x, cv[u][0].y, cv[u][0].z, cv[u][0].w,
+                                cv[u][1].x, cv[u][1].y, cv[u][1].z, cv[u][1].w};
+            const float s[8] = {sv[u][0].x, sv[u][0].y, sv[u][0].z, sv[u][0].w,
+                                sv[u][1].x, sv[u][1].y, sv[u][1].z, sv[u][1].w};
+#pragma unroll
+            for (int e = 0; e < 8; ++e) rot_f32(f1[e], f2[e], c[e], s[e], o1[e], o2[e]);
+            st_vec(p[u], pack8(o1));
+            st_vec(p[u] + half, pack8(o2));
+        }
+    }
+}
+
+__global__ void rope_standard_scalar(anima_bf16 *x, const float *cos_t, const float *sin_t, int T,
+                                     int D, int64_t pairs) {
+    const int half = D / 2;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < pairs;
+         i += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t row = i / half, d = i % half, t = row % T;
+        anima_bf16 *b = x + row * D;
+        float o1, o2;
+        rot_f32(ldb(b + d), ldb(b + half + d), cos_t[t * half + d], sin_t[t * half + d], o1, o2);
+        stb(b + d, o1);
+        stb(b + half + d, o2);
+    }
+}
+
+// ----------------------------------------------- fused QK RMSNorm + Cosmos RoPE
+// One 8-lane team per (token row, head) with HD = 128: lane l holds chunk l (elements
+// 8l..8l+7 of the first half) and chunk l+8 (the second half), i.e. both members of its
+// rotation pairs. The RMS statistics replay the reference's reduction tree for a
+// 128-wide row (ref_pair_tree_sum<8,2>), the normalised values are rounded to bf16 as
+// rms_norm_bf16 stores them, then rotated exactly as rope_cosmos_strided_bf16 does.
+struct QkArgs {
+    anima_bf16 *x;
+    const anima_bf16 *w, *cos_t, *sin_t;
+    int S, H;
+    int64_t heads;  // B*S*H
+    float eps;
+};
+
+__global__ void __launch_bounds__(kRopeBlock) qk_norm_rope_128(QkArgs a) {
+    constexpr int LPR = 8, K = 2, HD = 128;
+    const int l = threadIdx.x & (LPR - 1);
+    const int64_t hid = (int64_t)blockIdx.x * (blockDim.x / LPR) + threadIdx.x / LPR;
+    const bool live = hid < a.heads;
+    const int64_t token = hid / a.H;
+    anima_bf16 *p = a.x + hid * HD + l * 8;
+    Vec8 v[K] = {Vec8{{0u, 0u, 0u, 0u}}, Vec8{{0u, 0u, 0u, 0u}}};
+    Vec8 w[K], cv, sv;
+    if (live) {
+        v[0] = ld_stream(p);
+        v[1] = ld_stream(p + 64);
+    }
+    w[0] = ld_cached(a.w + l * 8);
+    w[1] = ld_cached(a.w + 64 + l * 8);
+    const int64_t s = live ? token % a.S : 0;
+    cv = ld_cached(a.cos_t + s * HD + l * 8);
+    sv = ld_cached(a.sin_t + s * HD + l * 8);
+
+    float q[K][4];
+#pragma unroll
+    for (int k = 0; k < K; ++k)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const float lo = bf_lo(v[k].w[j]), hi = bf_hi(v[k].w[j]);
+            q[k][j] = __fmaf_rn(hi, hi, lo * lo);
+        }
+    const float sq = ref_pair_tree_sum<LPR, K>(q, l, 0xffffffffu);
+    const float r = rsqrtf(__fdiv_rn(sq, (float)HD) + a.eps);
+    if (!live) return;
+    float x0[8], x1[8], w0[8], w1[8], c[8], sn[8], o0[8], o1[8];
+    unpack8(v[0], x0);
+    unpack8(v[1], x1);
+    unpack8(w[0], w0);
+    unpack8(w[1], w1);
+    unpack8(cv, c);
+    unpack8(sv, sn);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+        const float n0 = bf16_round((x0[e] * r) * w0[e]);  // rms_norm.cu:62-64, stored as bf16
+        const float n1 = bf16_round((x1[e] * r) * w1[e]);
+        rot_bf16(n0, n1, c[e], sn[e], o0[e], o1[e]);
+    }
+    st_vec(p, pack8(o0));
+    st_vec(p + 64, pack8(o1));
+}
+
+unsigned grid_for(int64_t work, int block) {
+    int64_t blocks = (work + block - 1) / block;
+    const int64_t wave = (int64_t)sm_count() * (2048 / block);
+    if (blocks > wave) blocks = wave;
+    return (unsigned)(blocks < 1 ? 1 : blocks);
+}
+
+bool bf16_ok(const void *p) { return aligned_to(p, 2); }
+
+}  // namespace
+}  // namespace anima
+
+using namespace anima;
+
+// ================================================================ C ABI
+
+extern "C" int anima_rope_cosmos_strided_bf16(anima_bf16 *x, const anima_bf16 *cos_table,
+                                              const anima_bf16 *sin_table, int B, int S, int H,
+                                              int HD, anima_stream_t stream) {
+    if (B < 0 || S < 0 || H < 0 || HD <= 0 || (HD & 1)) return ANIMA_ERR_BAD_SHAPE;
+    const int64_t rows = (int64_t)B * S;
+    if (rows == 0 || H == 0) return ANIMA_OK;
+    if (!x || !cos_table || !sin_table) return ANIMA_ERR_NULL_POINTER;
+    if (!bf16_ok(x) || !bf16_ok(cos_table) || !bf16_ok(sin_table)) return ANIMA_ERR_MISALIGNED;
+    const int64_t nx = rows * H * HD * 2, nt = (int64_t)S * HD * 2;
+    if (partial_overlap(x, nx, cos_table, nt) || partial_overlap(x, nx, sin_table, nt) ||
+        x == cos_table || x == sin_table)
+        return ANIMA_ERR_OVERLAP;
+    if (HD % 16 == 0 && aligned16(x) && aligned16(cos_table) && aligned16(sin_table)) {
+        CosmosArgs a{x, cos_table, sin_table, S, H, HD, rows * H * (HD / 16), (uint32_t)(HD / 16)};
+        rope_cosmos_vec<<<grid_for((a.units + kRopeU - 1) / kRopeU, kRopeBlock), kRopeBlock, 0,
+                          stream>>>(a);
+    } else {
+        const int64_t pairs = rows * H * (HD / 2);
+        rope_cosmos_scalar<<<grid_for(pairs, kRopeBlock), kRopeBlock, 0, stream>>>(
+            x, cos_table, sin_table, S, H, HD, pairs);
+    }
+    return launch_status();
+}
+
+extern "C" int anima_rope_standard_bf16(anima_bf16 *x, const float *cos_table, const float *sin_table,
+                                        int total_rows, int T, int D, anima_stream_t stream) {
+    if (total_rows < 0 || T <= 0 || D <= 0 || (D & 1)) return ANIMA_ERR_BAD_SHAPE;
+    if (total_rows == 0) return ANIMA_OK;
+    if (!x || !cos_table || !sin_table) return ANIMA_ERR_NULL_POINTER;
+    if (!bf16_ok(x) || !aligned_to(cos_table, 4) || !aligned_to(sin_table, 4)) return ANIMA_ERR_MISALIGNED;
+    if (D % 16 == 0 && aligned16(x) && aligned16(cos_table) && aligned16(sin_table)) {
+        StdArgs a{x, cos_table, sin_table, T, D, (int64_t)total_rows * (D / 16), (uint32_t)(D / 16)};
+        rope_standard_vec<<<grid_for((a.units + kRopeU - 1) / kRopeU, kRopeBlock), kRopeBlock, 0,
+                            stream>>>(a);
+    } else {
+        const int64_t pairs = (int64_t)total_rows * (D / 2);
+        rope_standard_scalar<<<grid_for(pairs, kRopeBlock), kRopeBlock, 0, stream>>>(
+            x, cos_table, sin_table, T, D, pairs);
+    }
+    return launch_status();
+}
+
+extern "C" int anima_qk_norm_rope_bf16(anima_bf16 *x, const anima_bf16 *weight,
+                                       const anima_bf16 *cos_table, const anima_bf16 *sin_table,
+                                       int B, int S, int H, int HD, float eps, anima_stream_t stream) {
+    if (B < 0 || S < 0 || H < 0 || HD <= 0 || (HD & 1)) return ANIMA_ERR_BAD_SHAPE;
+    const int64_t heads = (int64_t)B * S * H;
+    if (heads == 0) return ANIMA_OK;
+    if (!x || !weight || !cos_table || !sin_table) return ANIMA_ERR_NULL_POINTER;
+    if (!bf16_ok(x) || !bf16_ok(weight) || !bf16_ok(cos_table) || !bf16_ok(sin_table))
+        return ANIMA_ERR_MISALIGNED;
+    if (HD == 128 && aligned16(x) && aligned16(weight) && aligned16(cos_table) && aligned16(sin_table)) {
+        const int64_t nx = heads * HD * 2, nt = (int64_t)S * HD * 2;
+        if (partial_overlap(x, nx, cos_table, nt) || partial_overlap(x, nx, sin_table, nt) ||
+            partial_overlap(x, nx, weight, HD * 2) || x == cos_table || x == sin_table || x == weight)
+            return ANIMA_ERR_OVERLAP;
+        QkArgs a{x, weight, cos_table, sin_table, S, H, heads, eps};
+        const int64_t per_block = kRopeBlock / 8;
+        qk_norm_rope_128<<<(unsigned)((heads + per_block - 1) / per_block), kRopeBlock, 0, stream>>>(a);
+        return launch_status();
+    }
+    // Other head sizes: the same two steps as the reference, back to back.
+    if (heads > 2147483647) return ANIMA_ERR_TOO_LARGE;
+    if (int e = anima_rms_norm_bf16(x, weight, x, (int)heads, HD, eps, stream)) return e;
+    return anima_rope_cosmos_strided_bf16(x, cos_table, sin_table, B, S, H, HD, stream);
+}

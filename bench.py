@@ -1,0 +1,590 @@
+#!/usr/bin/env python
+"""Benchmark of the anima.cu fused layer kernels on B200: one DiT denoising step's
+elementwise/normalisation chain at BASELINE config 2 (1024x1024 image -> 4096 tokens,
+CFG batch 2 -> 8192 rows x 2048 hidden, 16 heads x 128, MLP 8192, 512 text tokens,
+28 blocks with fresh modulation vectors, timestep embedding).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl anima|reference]
+
+One step = the timestep embedding + 28 x the block's chain as the reference wires it
+(transformer.cpp:381-466), with the DiT FFN's GELU as a standalone op as BASELINE's chain
+lists it:
+    3x add (mod += temb)  adaLN-LN  QK-RMSNorm q,k  RoPE q,k  residual-gate+adaLN
+    QK-RMSNorm q (cross) k (text)  residual-gate+adaLN  GELU [R,8192]  residual-gate
+GEMMs and attention are not part of the chain (they stay cuBLAS/cuDNN); their outputs
+(q, k, sub-layer outputs, FFN activations) are synthetic tensors resident in HBM.
+
+--impl anima      this library through its C ABI (include/anima_b200.h)
+--impl reference  the reference's own CUDA kernels (src/kernels/*.cu compiled unchanged
+                  for sm_100a, oracle/_ref) through their kernels.h launchers, with the
+                  reference's host-side timestep sinusoid + upload.
+
+Prints one JSON line (rank 0). Multi-GPU runs (torchrun, one rank per GPU) replicate the
+per-GPU workload (rows are independent; no collective on the data path) and report the
+aggregate over ranks with the max-over-ranks device time.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "anima.cu_b200"))
+
+METRIC = "fused-kernel HBM GB/s (% of B200 peak) at 4096×2048 bf16; DiT-step ms"
+
+# ---------------------------------------------------------------- workload (cfg2)
+CFG = dict(batch=2, pe=(1, 64, 64), hidden=2048, heads=16, head_dim=128, mlp=8192, text=512, blocks=28,
+           ts_dim=2048, eps=1e-6)
+NSETS = 4  # rotating activation buffer sets: ~1.4 GB touched per step, >> 126 MB L2
+
+
+def chain_bytes(c=CFG):
+    """Algorithmic HBM bytes of one step, per op type (each input read once, each output
+    written once, broadcast vectors counted once)."""
+    B, S = c["batch"], c["pe"][0] * c["pe"][1] * c["pe"][2]
+    R, D, H, HD, M, T = B * S, c["hidden"], c["heads"], c["head_dim"], c["mlp"], c["text"]
+    per_block = {
+        "add": 3 * (3 * 2 * 3 * D),                      # mod[3D] += temb[3D], three times
+        "adaln_layernorm": 4 * R * D + 4 * D,
+        "rms_norm_qk128": 2 * (4 * R * H * HD + 2 * HD) + (4 * R * H * HD + 2 * HD) + (4 * B * T * H * HD + 2 * HD),
+        "rope_cosmos_strided": 2 * (4 * R * H * HD + 2 * S * (HD // 2) * 2),
+        "residual_gate_adaln": 2 * (8 * R * D + 6 * D),
+        "gelu_tanh": 4 * R * M,
+        "residual_gate_bcast": 6 * R * D + 2 * D,
+    }
+    launches_per_block = {"add": 3, "adaln_layernorm": 1, "rms_norm_qk128": 4, "rope_cosmos_strided": 2,
+                          "residual_gate_adaln": 2, "gelu_tanh": 1, "residual_gate_bcast": 1}
+    ts = 2 * c["ts_dim"] + 4 * 2 * c["ts_dim"]            # sinusoid write; RMSNorm read+weight+write
+    total = c["blocks"] * sum(per_block.values()) + ts
+    return total, per_block, launches_per_block
+
+
+# ---------------------------------------------------------------- launchers
+class AnimaOps:
+    """The B200 library's C ABI, raw pointers, status checked on every call."""
+
+    kind = "anima"
+
+    def __init__(self):
+        import anima_b200
+
+        self.m = anima_b200
+        self.L = anima_b200.lib
+
+    def _ck(self, name, st):
+        if st != 0:
+            raise self.m.AnimaError(name, st, self.m.status_string(st))
+
+    def add(self, a, b, o, n, s):
+        self._ck("add", self.L.anima_add_bf16(a, b, o, n, s))
+
+    def adaln_layernorm(self, x, sc, sh, o, N, D, eps, s):
+        self._ck("adaln", self.L.anima_adaln_layernorm_bf16(x, sc, sh, o, N, D, eps, s))
+
+    def rms_norm(self, x, w, o, N, D, eps, s):
+        self._ck("rms", self.L.anima_rms_norm_bf16(x, w, o, N, D, eps, s))
+
+    def rope_cosmos_strided(self, x, c, sn, B, S, H, HD, s):
+        self._ck("rope", self.L.anima_rope_cosmos_strided_bf16(x, c, sn, B, S, H, HD, s))
+
+    def residual_gate_adaln(self, h, y, g, sc, sh, o, N, D, eps, s):
+        self._ck("resgate", self.L.anima_residual_gate_adaln_bf16(h, y, g, sc, sh, o, N, D, eps, s))
+
+    def gelu_tanh(self, x, o, n, s):
+        self._ck("gelu", self.L.anima_gelu_tanh_bf16(x, o, n, s))
+
+    def residual_gate_bcast(self, x, y, g, o, M, D, s):
+        self._ck("bcast", self.L.anima_residual_gate_bcast_bf16(x, y, g, o, M, D, s))
+
+    def timestep(self, t, w, sin_out, normed, dim, eps, s, host_buf=None):
+        self._ck("timestep", self.L.anima_timestep_embedding_bf16(t, w, sin_out, normed, dim, eps, s))
+
+
+class RefOps:
+    """The reference's kernels.h launchers from oracle/_ref (C++ linkage, void)."""
+
+    kind = "reference"
+
+    def __init__(self):
+        sys.path.insert(0, os.path.join(ROOT, "oracle"))
+        import oracle as O  # the reference's host sinusoid loop, restated in C
+        import refkernels
+
+        self.R = refkernels.load_reference()
+        self.O = O
+
+    def add(self, a, b, o, n, s):
+        self.R.add_bf16(a, b, o, n, s)
+
+    def adaln_layernorm(self, x, sc, sh, o, N, D, eps, s):
+        self.R.adaln_layernorm_bf16(x, sc, sh, o, N, D, eps, s)
+
+    def rms_norm(self, x, w, o, N, D, eps, s):
+        self.R.rms_norm_bf16(x, w, o, N, D, eps, s)
+
+    def rope_cosmos_strided(self, x, c, sn, B, S, H, HD, s):
+        self.R.rope_cosmos_strided_bf16(x, c, sn, B, S, H, HD, s)
+
+    def residual_gate_adaln(self, h, y, g, sc, sh, o, N, D, eps, s):
+        self.R.residual_gate_adaln_bf16(h, y, g, sc, sh, o, N, D, eps, s)
+
+    def gelu_tanh(self, x, o, n, s):
+        self.R.gelu_tanh_bf16(x, o, n, s)
+
+    def residual_gate_bcast(self, x, y, g, o, M, D, s):
+        self.R.residual_gate_bcast_bf16(x, y, g, o, M, D, s)
+
+    def timestep(self, t, w, sin_out, normed, dim, eps, s, host_buf=None):
+        # transformer.cpp:182-200: host sinusoid, bf16 upload, then rms_norm_bf16 on one row
+        host_buf.numpy()[:] = self.O.timestep_sinusoid(t, dim).view(np.int16)
+        self._sin_tensor.copy_(host_buf, non_blocking=False)  # synchronous, like the reference's cudaMemcpy
+        self.R.rms_norm_bf16(sin_out, w, normed, 1, dim, eps, s)
+
+
+# ---------------------------------------------------------------- device state
+class Chain:
+    def __init__(self, ops, device, seed=1234):
+        import torch
+
+        import tables
+
+        self.ops, self.dev = ops, device
+        c = CFG
+        self.B, self.S = c["batch"], c["pe"][0] * c["pe"][1] * c["pe"][2]
+        self.R, self.D, self.H, self.HD = self.B * self.S, c["hidden"], c["heads"], c["head_dim"]
+        self.M, self.T, self.NB, self.eps = c["mlp"], c["text"], c["blocks"], c["eps"]
+        g = torch.Generator(device=device).manual_seed(seed)
+
+        def randn(shape, mean=0.0, std=1.0):
+            return (torch.randn(shape, generator=g, device=device) * std + mean).to(torch.bfloat16)
+
+        R, D, H, HD = self.R, self.D, self.H, self.HD
+        self.sets = []
+        for _ in range(NSETS):
+            self.sets.append(dict(
+                hidden=randn((R, D)), normed=torch.empty((R, D), dtype=torch.bfloat16, device=device),
+                sub=randn((R, D)), q=randn((R, H * HD)), k=randn((R, H * HD)), qc=randn((R, H * HD)),
+                kc=randn((self.B * self.T, H * HD)), ff=randn((R, self.M))))
+        # fresh modulation per block (3 adaLN-Zero sets of shift|scale|gate) + temb
+        self.mod_raw = randn((self.NB, 3, 3 * D), std=0.1)
+        self.mod = torch.empty_like(self.mod_raw)
+        self.temb = randn((3 * D,), std=0.1)
+        self.qk_w = randn((self.NB, 4, HD), mean=1.0, std=0.02)
+        cos_t, sin_t = tables.cosmos_rope_tables(*c["pe"], HD)
+        self.cos = torch.from_numpy(cos_t.view(np.int16)).to(device)
+        self.sin = torch.from_numpy(sin_t.view(np.int16)).to(device)
+        self.ts_w = randn((c["ts_dim"],), mean=1.0, std=0.02)
+        self.ts_sin = torch.empty((c["ts_dim"],), dtype=torch.bfloat16, device=device)
+        self.ts_out = torch.empty((c["ts_dim"],), dtype=torch.bfloat16, device=device)
+        self.ts_host = torch.empty((c["ts_dim"],), dtype=torch.int16).pin_memory()
+        if isinstance(ops, RefOps):
+            ops._sin_tensor = self.ts_sin.view(torch.int16)
+        self.ts_rng = np.random.default_rng(seed)
+        self.launches_per_block = 14
+
+    def timestep(self, stream):
+        t = float(np.float32(self.ts_rng.uniform()) * np.float32(1000.0))
+        self.ops.timestep(t, self.ts_w.data_ptr(), self.ts_sin.data_ptr(), self.ts_out.data_ptr(), CFG["ts_dim"],
+                          self.eps, stream, host_buf=self.ts_host)
+
+    def block(self, i, stream, timers=None):
+        """One DiT block's chain; `timers` (op -> list of event pairs) times every launch."""
+        import torch
+
+        o, st = self.ops, stream
+        bs = self.sets[i % NSETS]
+        R, D, H, HD, B, S = self.R, self.D, self.H, self.HD, self.B, self.S
+        mod = [self.mod[i, j] for j in range(3)]
+        w = self.qk_w[i]
+        P = lambda t: t.data_ptr()  # noqa: E731
+
+        def run(name, fn, *args):
+            if timers is None:
+                fn(*args)
+                return
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            fn(*args)
+            b.record()
+            timers.setdefault(name, []).append((a, b))
+
+        for j in range(3):  # compute_adaln_zero's mod += temb (transformer.cpp:408)
+            run("add", o.add, P(self.mod_raw[i, j]), P(self.temb), P(mod[j]), 3 * D, st)
+        shift, scale, gate = (lambda m: (P(m), P(m) + 2 * D, P(m) + 4 * D))(mod[0])
+        run("adaln_layernorm", o.adaln_layernorm, P(bs["hidden"]), scale, shift, P(bs["normed"]), R, D, self.eps, st)
+        run("rms_norm_qk128", o.rms_norm, P(bs["q"]), P(w[0]), P(bs["q"]), R * H, HD, self.eps, st)
+        run("rms_norm_qk128", o.rms_norm, P(bs["k"]), P(w[1]), P(bs["k"]), R * H, HD, self.eps, st)
+        run("rope_cosmos_strided", o.rope_cosmos_strided, P(bs["q"]), P(self.cos), P(self.sin), B, S, H, HD, st)
+        run("rope_cosmos_strided", o.rope_cosmos_strided, P(bs["k"]), P(self.cos), P(self.sin), B, S, H, HD, st)
+        shift, scale, gate2 = (P(mod[1]), P(mod[1]) + 2 * D, P(mod[1]) + 4 * D)
+        run("residual_gate_adaln", o.residual_gate_adaln, P(bs["hidden"]), P(bs["sub"]), gate, scale, shift,
+            P(bs["normed"]), R, D, self.eps, st)
+        run("rms_norm_qk128", o.rms_norm, P(bs["qc"]), P(w[2]), P(bs["qc"]), R * H, HD, self.eps, st)
+        run("rms_norm_qk128", o.rms_norm, P(bs["kc"]), P(w[3]), P(bs["kc"]), B * self.T * H, HD, self.eps, st)
+        shift, scale, gate3 = (P(mod[2]), P(mod[2]) + 2 * D, P(mod[2]) + 4 * D)
+        run("residual_gate_adaln", o.residual_gate_adaln, P(bs["hidden"]), P(bs["sub"]), gate2, scale, shift,
+            P(bs["normed"]), R, D, self.eps, st)
+        run("gelu_tanh", o.gelu_tanh, P(bs["ff"]), P(bs["ff"]), R * self.M, st)
+        run("residual_gate_bcast", o.residual_gate_bcast, P(bs["hidden"]), P(bs["sub"]), gate3, P(bs["hidden"]), R,
+            D, st)
+
+    def blocks(self, stream, timers=None):
+        for i in range(self.NB):
+            self.block(i, stream, timers)
+
+
+# ---------------------------------------------------------------- clocks
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.gpu = gpu_index
+        self.proc = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"], "samples": 0}
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+            out, _ = self.proc.communicate()
+        sm, mx, reasons, power = [], [], set(), []
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in out.strip().splitlines():
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx.append(float(f[2]))
+                power.append(float(f[3]))
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "power_w_max": max(power) if power else None, "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ---------------------------------------------------------------- measurements
+def peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), "measured"
+    except (OSError, KeyError, ValueError):
+        return 6650.0, "fallback"
+
+
+def time_steps(chain, steps, stream_obj, graph, ts=True):
+    """Device time (ms) of `steps` steps on the current stream, events on both sides."""
+    import torch
+
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    a.record()
+    for _ in range(steps):
+        if ts:
+            chain.timestep(stream_obj.cuda_stream)
+        if graph is not None:
+            graph.replay()
+        else:
+            chain.blocks(stream_obj.cuda_stream)
+    b.record()
+    torch.cuda.synchronize()
+    return a.elapsed_time(b)
+
+
+def per_op_times(chain, steps, stream_obj):
+    """Eager pass with CUDA events around every launch: op -> (launches, mean ms)."""
+    import torch
+
+    timers = {}
+    for _ in range(steps):
+        chain.blocks(stream_obj.cuda_stream, timers)
+    torch.cuda.synchronize()
+    return {k: (len(v), statistics.mean(a.elapsed_time(b) for a, b in v)) for k, v in timers.items()}
+
+
+def headline_kernels(ops, device, peak, reps=50):
+    """Each row kernel at the headline [4096, 2048] (GELU at [4096, 8192]), cycling 8
+    buffer sets (> 4x L2) so every launch reads from HBM. Returns op -> GB/s, frac, us."""
+    import torch
+
+    N, D, M = 4096, 2048, 8192
+    sets = 8
+    x = [torch.randn((N, D), device=device).to(torch.bfloat16) for _ in range(sets)]
+    y = [torch.randn((N, D), device=device).to(torch.bfloat16) for _ in range(sets)]
+    o = [torch.empty((N, D), dtype=torch.bfloat16, device=device) for _ in range(sets)]
+    f = [torch.randn((N, M), device=device).to(torch.bfloat16) for _ in range(2)]
+    v = (torch.randn((3 * D,), device=device) * 0.1).to(torch.bfloat16)
+    sc, sh, g = v.data_ptr(), v.data_ptr() + 2 * D, v.data_ptr() + 4 * D
+    s = torch.cuda.current_stream().cuda_stream
+    eps = 1e-6
+    cases = {
+        "adaln_layernorm": (4 * N * D + 4 * D, lambda i: ops.adaln_layernorm(x[i].data_ptr(), sc, sh, o[i].data_ptr(), N, D, eps, s)),
+        "residual_gate_adaln": (8 * N * D + 6 * D, lambda i: ops.residual_gate_adaln(
+            x[i].data_ptr(), y[i].data_ptr(), g, sc, sh, o[i].data_ptr(), N, D, eps, s)),
+        "residual_gate_bcast": (6 * N * D + 2 * D, lambda i: ops.residual_gate_bcast(
+            x[i].data_ptr(), y[i].data_ptr(), g, x[i].data_ptr(), N, D, s)),
+        "rms_norm_qk128": (4 * N * D + 256, lambda i: ops.rms_norm(x[i].data_ptr(), v.data_ptr(), o[i].data_ptr(),
+                                                                   N * 16, 128, eps, s)),
+        "gelu_tanh_4096x8192": (4 * N * M, lambda i: ops.gelu_tanh(f[i % 2].data_ptr(), f[i % 2].data_ptr(), N * M, s)),
+    }
+    res = {}
+    for name, (nbytes, fn) in cases.items():
+        for i in range(4):
+            fn(i % sets)
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for i in range(reps):
+            fn(i % sets)
+        b.record()
+        torch.cuda.synchronize()
+        us = a.elapsed_time(b) * 1e3 / reps
+        gbs = nbytes / (us * 1e-6) / 1e9
+        res[name] = {"gbs": round(gbs, 1), "frac": round(gbs / peak, 3), "us": round(us, 2), "bytes": nbytes}
+    del x, y, o, f
+    torch.cuda.empty_cache()
+    return res
+
+
+def cpu_baseline_sample(blocks=2, rows=8192):
+    """The CPU restatement (oracle/, single thread) over `blocks` blocks of the same chain
+    at cfg2 shapes. Returns (GB/s, description)."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as O
+
+    rng = np.random.default_rng(5)
+    c = CFG
+    B, S = c["batch"], c["pe"][0] * c["pe"][1] * c["pe"][2]
+    R = rows
+    D, H, HD, M, T = c["hidden"], c["heads"], c["head_dim"], c["mlp"], c["text"]
+    hidden, sub = O.randn_bf16(rng, (R, D)), O.randn_bf16(rng, (R, D))
+    q, k, qc = (O.randn_bf16(rng, (R, H * HD)) for _ in range(3))
+    kc = O.randn_bf16(rng, (B * T, H * HD))
+    ff = O.randn_bf16(rng, R * M)
+    mod = O.randn_bf16(rng, (3, 3 * D), std=0.1)
+    temb = O.randn_bf16(rng, 3 * D, std=0.1)
+    w = O.randn_bf16(rng, HD, mean=1.0, std=0.02)
+    ct, st = O.cosmos_rope_tables(*c["pe"], HD)
+    t0 = time.perf_counter()
+    for _ in range(blocks):
+        m = [O.add(mod[j], temb) for j in range(3)]  # each [shift | scale | gate]
+        shift, scale, gate = ([mj[:D], mj[D:2 * D], mj[2 * D:]] for mj in m)
+        O.adaln_layernorm(hidden, scale[0], shift[0], R, D)
+        q = O.rms_norm(q.reshape(R * H, HD), w, R * H, HD)
+        k = O.rms_norm(k.reshape(R * H, HD), w, R * H, HD)
+        q = O.rope_cosmos_strided(q, ct, st, B, R // B, H, HD)
+        k = O.rope_cosmos_strided(k, ct, st, B, R // B, H, HD)
+        hidden, _ = O.residual_gate_adaln(hidden, sub, gate[0], scale[1], shift[1], R, D)
+        qc = O.rms_norm(qc.reshape(R * H, HD), w, R * H, HD)
+        kc = O.rms_norm(kc.reshape(B * T * H, HD), w, B * T * H, HD)
+        hidden, _ = O.residual_gate_adaln(hidden, sub, gate[1], scale[2], shift[2], R, D)
+        ff = O.gelu_tanh(ff)
+        hidden = O.residual_gate_bcast(hidden, sub, gate[2], R, D)
+    dt = time.perf_counter() - t0
+    _, per_block, _ = chain_bytes()
+    nbytes = blocks * sum(per_block.values()) * R / (B * S)
+    return nbytes / dt / 1e9, f"{blocks} of the 28 blocks of the cfg2 chain at {R} rows ({dt:.1f} s)"
+
+
+# ---------------------------------------------------------------- main
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=100)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["anima", "reference"], default="anima")
+    ap.add_argument("--eager", action="store_true", help="time eager launches instead of CUDA graph replay")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-headline", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference" and rank != 0:
+        return  # the reference is single-GPU code: rank 0 alone runs it
+
+    import torch
+
+    torch.cuda.set_device(local_rank)
+    device = torch.device("cuda", local_rank)
+    dist = None
+    if world > 1 and args.impl == "anima":
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=device)
+    n_gpus = world if dist is not None else 1
+
+    ops = AnimaOps() if args.impl == "anima" else RefOps()
+    chain = Chain(ops, device)
+    stream = torch.cuda.current_stream()
+    peak, peak_kind = peaks()
+    total_bytes, per_block, lpb = chain_bytes()
+
+    # warm-up (also initialises every kernel and the library's device caches)
+    for _ in range(args.warmup):
+        chain.timestep(stream.cuda_stream)
+        chain.blocks(stream.cuda_stream)
+    torch.cuda.synchronize()
+
+    graph = None
+    if not args.eager:
+        side = torch.cuda.Stream()
+        side.wait_stream(stream)
+        with torch.cuda.stream(side):
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph, stream=side):
+                chain.blocks(side.cuda_stream)
+        stream.wait_stream(side)
+        for _ in range(2):
+            graph.replay()
+        torch.cuda.synchronize()
+
+    # timed region: barrier + synchronize on both sides, device events, max over ranks
+    try:
+        smi_id = "GPU-" + str(torch.cuda.get_device_properties(device).uuid)
+    except Exception:
+        smi_id = str(local_rank)
+    clocks = ClockSampler(smi_id)
+    clocks.start()
+    if dist is not None:
+        dist.barrier()
+    torch.cuda.synchronize()
+    ms = time_steps(chain, args.steps, stream, graph)
+    if dist is not None:
+        t = torch.tensor([ms], device=device, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+        dist.barrier()
+    clk = clocks.stop()
+    ms_per_step = ms / args.steps
+    value = n_gpus * total_bytes * args.steps / (ms * 1e-3) / 1e9
+
+    # per-op device times (eager, CUDA events around every launch) -> roofline
+    ops_t = per_op_times(chain, min(args.steps, 10), stream)
+    kernels = {}
+    for name, (n, mean_ms) in ops_t.items():
+        per_launch = per_block[name] / lpb[name]
+        gbs = per_launch / (mean_ms * 1e-3) / 1e9
+        kernels[name] = {"launches_per_step": lpb[name] * CFG["blocks"], "us": round(mean_ms * 1e3, 2),
+                         "bytes_per_launch": int(per_launch), "gbs": round(gbs, 1), "frac": round(gbs / peak, 3),
+                         "share": None}
+    tot = sum(v["us"] * v["launches_per_step"] for v in kernels.values())
+    for v in kernels.values():
+        v["share"] = round(v["us"] * v["launches_per_step"] / tot, 3)
+    dom = max(kernels, key=lambda k: kernels[k]["share"])
+    dk = kernels[dom]
+
+    # end to end through the C ABI with host buffers: pinned hidden + modulation in, hidden out
+    h_in = torch.empty((chain.R, chain.D), dtype=torch.bfloat16).pin_memory()
+    m_in = torch.empty_like(chain.mod_raw, device="cpu").pin_memory()
+    h_out = torch.empty((chain.R, chain.D), dtype=torch.bfloat16).pin_memory()
+    h_in.copy_(chain.sets[0]["hidden"].cpu())
+    m_in.copy_(chain.mod_raw.cpu())
+    e2e_steps = max(3, min(args.steps, 20))
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(e2e_steps):
+        chain.sets[0]["hidden"].copy_(h_in, non_blocking=True)
+        chain.mod_raw.copy_(m_in, non_blocking=True)
+        chain.timestep(stream.cuda_stream)
+        if graph is not None:
+            graph.replay()
+        else:
+            chain.blocks(stream.cuda_stream)
+        h_out.copy_(chain.sets[(CFG["blocks"] - 1) % NSETS]["hidden"], non_blocking=True)
+    b.record()
+    torch.cuda.synchronize()
+    e2e_ms = a.elapsed_time(b) / e2e_steps
+    if dist is not None:
+        t = torch.tensor([e2e_ms], device=device, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+    h2d = h_in.numel() * 2 + m_in.numel() * 2 + (0 if args.impl == "anima" else CFG["ts_dim"] * 2)
+    d2h = h_out.numel() * 2
+
+    headline = None
+    if not args.no_headline and rank == 0:
+        headline = headline_kernels(ops, device, peak)
+
+    cpu = None
+    if not args.no_cpu_baseline and rank == 0:
+        v, sample = cpu_baseline_sample()
+        cpu = {"value": round(v, 3), "unit": "GB/s", "cores": 1, "kind": "port", "sample": sample,
+               "note": "CPU restatement of the reference kernels (oracle/oracle.c, -O2, one thread); the "
+                       "reference itself has no CPU implementation of these ops"}
+
+    if graph is not None:
+        del graph
+    launches_per_step = CFG["blocks"] * chain.launches_per_block + 1
+    line = {
+        "metric": METRIC, "value": round(value, 1), "unit": "GB/s", "n_gpus": n_gpus, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms_per_step, 4), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic: seeded N(0,1) activations, N(0,0.1) modulation and temb, 1+N(0,0.02) norm weights, "
+                "t~U(0,1)*1000; GEMM/attention outputs are resident synthetic tensors",
+        "config": {"workload": "cfg2: 1024x1024 image -> 4096 tokens x CFG 2, 28-block DiT elementwise chain",
+                   "rows": chain.R, "hidden": chain.D, "heads": chain.H, "head_dim": chain.HD, "mlp": chain.M,
+                   "text_tokens": chain.T, "blocks": chain.NB, "timestep_dim": CFG["ts_dim"],
+                   "algorithmic_bytes_per_step": total_bytes,
+                   "l2": f"{NSETS} rotating activation sets, ~1.4 GB touched per step > 126 MB L2 (no flush)",
+                   "timing": ("CUDA graph replay of the 28 blocks + eager timestep launch per step"
+                              if graph is not None else "eager launches"),
+                   "parallelism": f"replicas x{n_gpus} (rows independent; no collective on the data path)"},
+        "e2e": {"value": round(n_gpus * total_bytes / (e2e_ms * 1e-3) / 1e9, 1), "unit": "GB/s",
+                "ms_per_step": round(e2e_ms, 4), "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+        "gpu_launches": launches_per_step * args.steps if args.impl == "anima" else 0,
+        "roofline": {"bound": "hbm", "kernel": dom, "achieved": dk["gbs"], "peak": peak, "unit": "GB/s",
+                     "frac": dk["frac"], "peak_kind": peak_kind, "traffic": None,
+                     "bytes_per_launch": dk["bytes_per_launch"], "us_per_launch": dk["us"]},
+        "chain_frac_of_peak": round(value / n_gpus / peak, 3),
+        "cpu_baseline": cpu,
+        "clocks": clk,
+        "kernels": kernels,
+        "headline_4096x2048": headline,
+    }
+    if args.impl == "reference":
+        line["impl"] = "reference"
+        line["reference_kind"] = ("the reference's own CUDA kernels (src/kernels/*.cu compiled unchanged for sm_100a, "
+                                  "oracle/_ref) through their kernels.h launchers; host-side timestep sinusoid + "
+                                  "synchronous upload as transformer.cpp:182-200")
+        line["gpu_launches"] = 0
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,209 @@
+/*
+ * anima_b200.h -- C ABI of the B200 (sm_100a) fused layer kernels for anima.cu.
+ *
+ * Every entry point enqueues one kernel (or nothing, for empty inputs) on `stream`
+ * and returns without synchronising. The caller owns every buffer; the library
+ * allocates no device memory and keeps no per-call state. All pointers are device
+ * pointers unless stated otherwise. bf16 tensors are passed as uint16_t bit
+ * patterns, row-major and densely packed.
+ *
+ * Return value: ANIMA_OK (0); a negative ANIMA_ERR_* for an argument the library
+ * rejected before touching the GPU; or a positive cudaError_t from the launch.
+ * In-place use (input pointer == output pointer) is supported wherever the
+ * reference's callers use it; partially overlapping buffers are rejected.
+ *
+ * Reference: TheLegendOfKitty/anima.cu, src/kernels/kernels.h. Each declaration
+ * cites the launcher it replaces. A C++ shim in the same library also exports the
+ * reference's exact C++ signatures (see anima_kernels_compat.h), so the reference's
+ * model files link against this library unchanged.
+ */
+#ifndef ANIMA_B200_H
+#define ANIMA_B200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(__GNUC__)
+#define ANIMA_API __attribute__((visibility("default")))
+#else
+#define ANIMA_API
+#endif
+
+typedef uint16_t anima_bf16;               /* bf16 bit pattern */
+typedef struct CUstream_st *anima_stream_t; /* same type as cudaStream_t */
+
+enum {
+    ANIMA_OK = 0,
+    ANIMA_ERR_NULL_POINTER = -1,  /* a required pointer is NULL */
+    ANIMA_ERR_BAD_SHAPE = -2,     /* a size is negative, zero where it must not be, or odd where it must be even */
+    ANIMA_ERR_MISALIGNED = -3,    /* a bf16 pointer is not 2-byte aligned (fp32 / int32: 4-byte) */
+    ANIMA_ERR_TOO_LARGE = -4,     /* a size overflows the index arithmetic */
+    ANIMA_ERR_OVERLAP = -5,       /* an output partially overlaps an input */
+    ANIMA_ERR_NO_DEVICE = -6      /* no current CUDA device could be queried */
+};
+
+/* Human-readable name of a status code (static storage, never NULL). */
+ANIMA_API const char *anima_status_string(int status);
+
+/* Library version, e.g. "anima_b200 0.1.0 sm_100a". */
+ANIMA_API const char *anima_version(void);
+
+/* ------------------------------------------------------------------ row norms */
+
+/* out[n,:] = x[n,:] * rsqrt(mean(x[n,:]^2) + eps) * weight[:]; weight may be NULL.
+ * D even. Replaces rms_norm_bf16, kernels.h:9-11 (rms_norm.cu:118-131). */
+ANIMA_API int anima_rms_norm_bf16(const anima_bf16 *x, const anima_bf16 *weight, anima_bf16 *out,
+                        int N, int D, float eps, anima_stream_t stream);
+
+/* LayerNorm without affine. Replaces layer_norm_bf16, kernels.h:14-16 (layer_norm.cu:61-72). */
+ANIMA_API int anima_layer_norm_bf16(const anima_bf16 *x, anima_bf16 *out, int N, int D, float eps,
+                          anima_stream_t stream);
+
+/* out = LayerNorm(x) * (1 + scale[d]) + shift[d], scale/shift broadcast over rows.
+ * Replaces adaln_layernorm_bf16, kernels.h:19-22 (layer_norm.cu:127-135). */
+ANIMA_API int anima_adaln_layernorm_bf16(const anima_bf16 *x, const anima_bf16 *scale,
+                               const anima_bf16 *shift, anima_bf16 *out, int N, int D,
+                               float eps, anima_stream_t stream);
+
+/* hidden = hidden + sub_out * gate[d] (written back as bf16), then
+ * normed = LayerNorm(hidden) * (1 + scale[d]) + shift[d]. The statistics use the
+ * unrounded fp32 sum; the normalisation reads the bf16-rounded hidden, as the
+ * reference does. Replaces residual_gate_adaln_bf16, kernels.h:25-30 (layer_norm.cu:198-209). */
+ANIMA_API int anima_residual_gate_adaln_bf16(anima_bf16 *hidden, const anima_bf16 *sub_out,
+                                   const anima_bf16 *gate, const anima_bf16 *scale,
+                                   const anima_bf16 *shift, anima_bf16 *normed, int N, int D,
+                                   float eps, anima_stream_t stream);
+
+/* out = RMSNorm(x) * (1 + scale[n,d]) + shift[n,d] with per-row scale/shift.
+ * Replaces adaln_rms_norm_bf16, kernels.h:60-63 (adaln.cu:58-70). */
+ANIMA_API int anima_adaln_rms_norm_bf16(const anima_bf16 *x, const anima_bf16 *scale,
+                              const anima_bf16 *shift, anima_bf16 *out, int N, int D,
+                              float eps, anima_stream_t stream);
+
+/* out = RMSNorm(x) * (1 + weight[d]). Replaces gemma_rms_norm_bf16, kernels.h:151-153
+ * (gemma_ops.cu:170-177). */
+ANIMA_API int anima_gemma_rms_norm_bf16(const anima_bf16 *x, const anima_bf16 *weight, anima_bf16 *out,
+                              int N, int D, float eps, anima_stream_t stream);
+
+/* -------------------------------------------------------------- elementwise */
+
+/* tanh-GELU. The reference processes floor(N/2) element pairs and leaves an odd last
+ * element untouched; so does this. Replaces gelu_tanh_bf16, kernels.h:33 (gelu.cu:66-71). */
+ANIMA_API int anima_gelu_tanh_bf16(const anima_bf16 *x, anima_bf16 *out, int64_t N,
+                         anima_stream_t stream);
+
+/* gelu_tanh(x + bias[i % D]). Replaces gelu_tanh_bias_bf16, kernels.h:34-36 (gelu.cu:73-81). */
+ANIMA_API int anima_gelu_tanh_bias_bf16(const anima_bf16 *x, const anima_bf16 *bias, anima_bf16 *out,
+                              int64_t N, int D, anima_stream_t stream);
+
+/* x / (1 + exp(-x)). Replaces silu_bf16, kernels.h:39 (silu.cu:49-54). */
+ANIMA_API int anima_silu_bf16(const anima_bf16 *x, anima_bf16 *out, int64_t N, anima_stream_t stream);
+
+/* silu(x + bias[i % D]). Replaces silu_bias_bf16, kernels.h:40-42 (silu.cu:56-64). */
+ANIMA_API int anima_silu_bias_bf16(const anima_bf16 *x, const anima_bf16 *bias, anima_bf16 *out,
+                         int64_t N, int D, anima_stream_t stream);
+
+/* out = a + b. Replaces add_bf16, kernels.h:69-71 (elementwise.cu:55-64). */
+ANIMA_API int anima_add_bf16(const anima_bf16 *a, const anima_bf16 *b, anima_bf16 *out, int64_t N,
+                   anima_stream_t stream);
+
+/* out = a * b. Replaces mul_bf16, kernels.h:78-80 (elementwise.cu:143-152). */
+ANIMA_API int anima_mul_bf16(const anima_bf16 *a, const anima_bf16 *b, anima_bf16 *out, int64_t N,
+                   anima_stream_t stream);
+
+/* out[m,d] = x[m,d] * (1 + scale[d]) + shift[d]. Replaces scale_shift_bcast_bf16,
+ * kernels.h:87-89 (elementwise.cu:238-247). */
+ANIMA_API int anima_scale_shift_bcast_bf16(const anima_bf16 *x, const anima_bf16 *scale,
+                                 const anima_bf16 *shift, anima_bf16 *out, int M, int D,
+                                 anima_stream_t stream);
+
+/* out[m,d] = x[m,d] + y[m,d] * gate[d]. Replaces residual_gate_bcast_bf16, kernels.h:90-92
+ * (elementwise.cu:271-280). */
+ANIMA_API int anima_residual_gate_bcast_bf16(const anima_bf16 *x, const anima_bf16 *y,
+                                   const anima_bf16 *gate, anima_bf16 *out, int M, int D,
+                                   anima_stream_t stream);
+
+/* out = gelu_tanh(gate) * up (scalar formula of the reference). Replaces gated_gelu_bf16,
+ * kernels.h:138-140 (gemma_ops.cu:24-31). */
+ANIMA_API int anima_gated_gelu_bf16(const anima_bf16 *gate, const anima_bf16 *up, anima_bf16 *out,
+                          int64_t N, anima_stream_t stream);
+
+/* --------------------------------------------------------------------- RoPE */
+
+/* In-place Cosmos half-split rotation on x[B*S, H*HD]: for i < HD/2,
+ * (x_i, x_{i+HD/2}) <- (x_i c - x_{i+HD/2} s, x_{i+HD/2} c + x_i s), with c, s read
+ * from the bf16 tables cos/sin [S, HD] at [s_pos, i]. Replaces rope_cosmos_strided_bf16,
+ * kernels.h:51-53 (rope.cu:110-121). */
+ANIMA_API int anima_rope_cosmos_strided_bf16(anima_bf16 *x, const anima_bf16 *cos_table,
+                                   const anima_bf16 *sin_table, int B, int S, int H, int HD,
+                                   anima_stream_t stream);
+
+/* In-place half-split rotation on rows of x[total_rows, D] with t = row % T and fp32
+ * tables cos/sin [T, D/2]. Replaces rope_standard_bf16, kernels.h:145-147 (gemma_ops.cu:89-97). */
+ANIMA_API int anima_rope_standard_bf16(anima_bf16 *x, const float *cos_table, const float *sin_table,
+                             int total_rows, int T, int D, anima_stream_t stream);
+
+/* ------------------------------------------------------------------- gather */
+
+/* out[t,:] = table[ids[t],:], bit-exact. ids outside [0, vocab) produce a zero row and,
+ * when bad_id_count is non-NULL, increment *bad_id_count (a device int the caller
+ * zeroes). vocab <= 0 disables the check (the reference's behaviour).
+ * Replaces embedding_lookup_bf16, kernels.h:142-144 (gemma_ops.cu:47-53), which takes
+ * no vocabulary size. */
+ANIMA_API int anima_embedding_lookup_bf16(const anima_bf16 *table, const int32_t *ids, anima_bf16 *out,
+                                int T, int D, int vocab, int32_t *bad_id_count,
+                                anima_stream_t stream);
+
+/* ----------------------------------------------------------- VAE channel norm */
+
+/* NCHW: out[b,c,s] = x[b,c,s] * rsqrt(mean_c x[b,:,s]^2 + eps) * gamma[c], one launch
+ * for all B. Replaces rms_norm_channel_bf16, kernels.h:177-180 (vae_kernels.cu:83-98). */
+ANIMA_API int anima_rms_norm_channel_bf16(const anima_bf16 *x, const anima_bf16 *gamma, anima_bf16 *out,
+                                int B, int C, int spatial, float eps, anima_stream_t stream);
+
+/* ------------------------------------------------ new entry points (additive)
+ * These have no single reference launcher: each replaces a short chain of reference
+ * calls with one kernel and produces the same bits as that chain (the intermediate
+ * bf16 rounding is kept). */
+
+/* silu(rms_norm_channel(x)) in one pass: the chain rms_norm_channel_bf16 + silu_bf16 at
+ * vae.cpp:148,184 (and :189, :457-458). */
+ANIMA_API int anima_rms_norm_channel_silu_bf16(const anima_bf16 *x, const anima_bf16 *gamma,
+                                     anima_bf16 *out, int B, int C, int spatial, float eps,
+                                     anima_stream_t stream);
+
+/* Per-head RMSNorm with weight followed by the Cosmos rotation, in place on
+ * x[B*S, H*HD]: the chain rms_norm_bf16 + rope_cosmos_strided_bf16 at
+ * transformer.cpp:350-358. */
+ANIMA_API int anima_qk_norm_rope_bf16(anima_bf16 *x, const anima_bf16 *weight,
+                            const anima_bf16 *cos_table, const anima_bf16 *sin_table, int B,
+                            int S, int H, int HD, float eps, anima_stream_t stream);
+
+/* out = silu(gate) * up with silu rounded to bf16 first: the chain silu_bf16 + mul_bf16 at
+ * qwen3.cpp:248-250. out may alias gate or up. */
+ANIMA_API int anima_swiglu_bf16(const anima_bf16 *gate, const anima_bf16 *up, anima_bf16 *out, int64_t N,
+                      anima_stream_t stream);
+
+/* out = LayerNorm(x) rounded to bf16, then * (1 + scale[d]) + shift[d]: the chain
+ * layer_norm_bf16 + scale_shift_bcast_bf16 at transformer.cpp:563-564. */
+ANIMA_API int anima_layer_norm_modulate_bf16(const anima_bf16 *x, const anima_bf16 *scale,
+                                   const anima_bf16 *shift, anima_bf16 *out, int N, int D,
+                                   float eps, anima_stream_t stream);
+
+/* Timestep embedding on the GPU: writes the flip_sin_to_cos sinusoid of `timestep`
+ * (cos of t*f_i in [0, dim/2), sin in [dim/2, dim), f_i = exp(-ln(1e4) i / (dim/2)))
+ * as bf16 to sinusoid_out[dim], and, when normed_out is non-NULL, its RMSNorm times
+ * norm_weight (nullable) to normed_out[dim]. The reference builds the sinusoid on the
+ * host and uploads it (transformer.cpp:182-197) before rms_norm_bf16 (:200). dim even. */
+ANIMA_API int anima_timestep_embedding_bf16(float timestep, const anima_bf16 *norm_weight,
+                                  anima_bf16 *sinusoid_out, anima_bf16 *normed_out, int dim,
+                                  float eps, anima_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* ANIMA_B200_H */

@@ -1,0 +1,502 @@
+/*
+ * oracle.c -- TEST INFRASTRUCTURE ONLY: CPU restatement of anima.cu's fused layer
+ * kernels, used as the parity checker. Compiled with -ffp-contract=off so that every
+ * fused multiply-add below is one the reference's CUDA source spells out (or that nvcc
+ * is known to form there); see oracle.h for the contract and the mode parameters.
+ */
+#include "oracle.h"
+
+#include <math.h>
+#include <stdlib.h>
+#include <string.h>
+
+/* ------------------------------------------------------------------ bf16 helpers */
+
+float oracle_bf16_to_f32(uint16_t b) {
+    uint32_t u = (uint32_t)b << 16;
+    float f;
+    memcpy(&f, &u, sizeof f);
+    return f;
+}
+
+uint16_t oracle_f32_to_bf16(float f) {
+    uint32_t u;
+    memcpy(&u, &f, sizeof u);
+    if ((u & 0x7fffffffu) > 0x7f800000u) return 0x7fff; /* NaN */
+    u += 0x7fffu + ((u >> 16) & 1u);                      /* round to nearest even */
+    return (uint16_t)(u >> 16);
+}
+
+#define B2F oracle_bf16_to_f32
+#define F2B oracle_f32_to_bf16
+
+/* ------------------------------------------------------- reference reductions */
+
+/* warp_reduce_sum, src/cuda_utils.cuh:46-50: __shfl_down_sync with offsets 16..1;
+ * the value that matters is lane 0's. */
+static float ref_warp_sum(float v[32]) {
+    for (int off = 16; off > 0; off >>= 1)
+        for (int l = 0; l < off; ++l) v[l] = v[l] + v[l + off];
+    return v[0];
+}
+
+/* cta_reduce_sum, src/kernels/layer_norm.cu:7-19 (the same tree is inlined at
+ * rms_norm.cu:40-53, adaln.cu:418-431, gemma_ops.cu:148-161). */
+float oracle_ref_block_sum(const float *per_thread, int nthreads) {
+    int nwarps = (nthreads + 31) / 32;
+    float warp_sums[32];
+    for (int w = 0; w < nwarps; ++w) {
+        float v[32];
+        for (int l = 0; l < 32; ++l) {
+            int t = w * 32 + l;
+            v[l] = t < nthreads ? per_thread[t] : 0.0f;
+        }
+        warp_sums[w] = ref_warp_sum(v);
+    }
+    float v[32];
+    for (int l = 0; l < 32; ++l) v[l] = l < nwarps ? warp_sums[l] : 0.0f;
+    return ref_warp_sum(v);
+}
+
+/* layer_norm.cu:68-70, :132-133, :205-206; rms_norm.cu:126-128; adaln.cu:453-454 */
+int oracle_ref_row_threads(int D) {
+    int D2 = D / 2;
+    int threads = (D2 <= 1024) ? ((D2 + 31) / 32 * 32) : 1024;
+    if (threads < 32) threads = 32;
+    return threads;
+}
+
+/* var = sum_sq/D - mean*mean (layer_norm.cu:49,107,179); mode 0 = contracted to an fma. */
+static float ref_var(float q_over_d, float mean, int var_mode) {
+    return var_mode == 0 ? fmaf(-mean, mean, q_over_d) : q_over_d - mean * mean;
+}
+
+/* ------------------------------------------------------------------ LayerNorm */
+
+/* layer_norm.cu:26-59 */
+void oracle_layer_norm(const uint16_t *x, uint16_t *out, int N, int D, float eps,
+                       int var_mode) {
+    int D2 = D / 2, T = oracle_ref_row_threads(D);
+    float *ps = calloc((size_t)T, sizeof(float)), *pq = calloc((size_t)T, sizeof(float));
+    for (int n = 0; n < N; ++n) {
+        const uint16_t *xr = x + (int64_t)n * D;
+        uint16_t *yr = out + (int64_t)n * D;
+        for (int t = 0; t < T; ++t) {
+            float s = 0.0f, q = 0.0f;
+            for (int i = t; i < D2; i += T) {
+                float v0 = B2F(xr[2 * i]), v1 = B2F(xr[2 * i + 1]);
+                s += v0 + v1;
+                q = fmaf(v0, v0, q);
+                q = fmaf(v1, v1, q);
+            }
+            ps[t] = s;
+            pq[t] = q;
+        }
+        float mean = oracle_ref_block_sum(ps, T) / (float)D;
+        float var = ref_var(oracle_ref_block_sum(pq, T) / (float)D, mean, var_mode);
+        float inv_std = 1.0f / sqrtf(var + eps);
+        for (int i = 0; i < D2; ++i) {
+            float v0 = (B2F(xr[2 * i]) - mean) * inv_std;
+            float v1 = (B2F(xr[2 * i + 1]) - mean) * inv_std;
+            yr[2 * i] = F2B(v0);
+            yr[2 * i + 1] = F2B(v1);
+        }
+    }
+    free(ps);
+    free(pq);
+}
+
+/* layer_norm.cu:83-125 */
+void oracle_adaln_layernorm(const uint16_t *x, const uint16_t *scale, const uint16_t *shift,
+                            uint16_t *out, int N, int D, float eps, int var_mode) {
+    int D2 = D / 2, T = oracle_ref_row_threads(D);
+    float *ps = calloc((size_t)T, sizeof(float)), *pq = calloc((size_t)T, sizeof(float));
+    for (int n = 0; n < N; ++n) {
+        const uint16_t *xr = x + (int64_t)n * D;
+        uint16_t *yr = out + (int64_t)n * D;
+        for (int t = 0; t < T; ++t) {
+            float s = 0.0f, q = 0.0f;
+            for (int i = t; i < D2; i += T) {
+                float v0 = B2F(xr[2 * i]), v1 = B2F(xr[2 * i + 1]);
+                s += v0 + v1;
+                q += v0 * v0 + v1 * v1; /* bf16 squares are exact: no contraction choice */
+            }
+            ps[t] = s;
+            pq[t] = q;
+        }
+        float mean = oracle_ref_block_sum(ps, T) / (float)D;
+        float var = ref_var(oracle_ref_block_sum(pq, T) / (float)D, mean, var_mode);
+        float inv_std = 1.0f / sqrtf(var + eps);
+        for (int e = 0; e < 2 * D2; ++e) {
+            float xv = B2F(xr[e]), sv = B2F(scale[e]), hv = B2F(shift[e]);
+            yr[e] = F2B(fmaf((xv - mean) * inv_std, 1.0f + sv, hv));
+        }
+    }
+    free(ps);
+    free(pq);
+}
+
+static float sq_pair(float h0, float h1, int sq_mode) {
+    switch (sq_mode) {
+    case 0: return fmaf(h0, h0, h1 * h1);
+    case 1: return fmaf(h1, h1, h0 * h0);
+    default: return h0 * h0 + h1 * h1;
+    }
+}
+
+/* layer_norm.cu:146-196 */
+void oracle_residual_gate_adaln(uint16_t *hidden, const uint16_t *sub_out,
+                                const uint16_t *gate, const uint16_t *scale,
+                                const uint16_t *shift, uint16_t *normed, int N, int D,
+                                float eps, int sq_mode, int var_mode) {
+    int D2 = D / 2, T = oracle_ref_row_threads(D);
+    float *ps = calloc((size_t)T, sizeof(float)), *pq = calloc((size_t)T, sizeof(float));
+    for (int n = 0; n < N; ++n) {
+        uint16_t *hr = hidden + (int64_t)n * D;
+        const uint16_t *yr = sub_out + (int64_t)n * D;
+        uint16_t *nr = normed + (int64_t)n * D;
+        for (int t = 0; t < T; ++t) {
+            float s = 0.0f, q = 0.0f;
+            for (int i = t; i < D2; i += T) {
+                float h0 = fmaf(B2F(yr[2 * i]), B2F(gate[2 * i]), B2F(hr[2 * i]));
+                float h1 = fmaf(B2F(yr[2 * i + 1]), B2F(gate[2 * i + 1]), B2F(hr[2 * i + 1]));
+                hr[2 * i] = F2B(h0);
+                hr[2 * i + 1] = F2B(h1);
+                s += h0 + h1;
+                q += sq_pair(h0, h1, sq_mode);
+            }
+            ps[t] = s;
+            pq[t] = q;
+        }
+        float mean = oracle_ref_block_sum(ps, T) / (float)D;
+        float var = ref_var(oracle_ref_block_sum(pq, T) / (float)D, mean, var_mode);
+        float inv_std = 1.0f / sqrtf(var + eps);
+        for (int e = 0; e < 2 * D2; ++e) {
+            float hv = B2F(hr[e]), sv = B2F(scale[e]), shv = B2F(shift[e]);
+            nr[e] = F2B(fmaf((hv - mean) * inv_std, 1.0f + sv, shv));
+        }
+    }
+    free(ps);
+    free(pq);
+}
+
+/* -------------------------------------------------------------------- RMSNorm */
+
+/* rms_norm.cu:9-67 */
+void oracle_rms_norm(const uint16_t *x, const uint16_t *weight, uint16_t *out, int N, int D,
+                     float eps) {
+    int D2 = D / 2, T = oracle_ref_row_threads(D);
+    float *pq = calloc((size_t)T, sizeof(float));
+    for (int n = 0; n < N; ++n) {
+        const uint16_t *xr = x + (int64_t)n * D;
+        uint16_t *yr = out + (int64_t)n * D;
+        for (int t = 0; t < T; ++t) {
+            float q = 0.0f;
+            for (int i = t; i < D2; i += T) {
+                float v0 = B2F(xr[2 * i]), v1 = B2F(xr[2 * i + 1]);
+                q = fmaf(v0, v0, q);
+                q = fmaf(v1, v1, q);
+            }
+            pq[t] = q;
+        }
+        float rms_inv = 1.0f / sqrtf(oracle_ref_block_sum(pq, T) / (float)D + eps);
+        for (int e = 0; e < 2 * D2; ++e) {
+            float v = B2F(xr[e]) * rms_inv;
+            if (weight) v = v * B2F(weight[e]);
+            yr[e] = F2B(v);
+        }
+    }
+    free(pq);
+}
+
+/* adaln.cu:11-58 */
+void oracle_adaln_rms_norm(const uint16_t *x, const uint16_t *scale, const uint16_t *shift,
+                           uint16_t *out, int N, int D, float eps) {
+    int D2 = D / 2, T = oracle_ref_row_threads(D);
+    float *pq = calloc((size_t)T, sizeof(float));
+    for (int n = 0; n < N; ++n) {
+        const uint16_t *xr = x + (int64_t)n * D;
+        const uint16_t *sr = scale + (int64_t)n * D, *hr = shift + (int64_t)n * D;
+        uint16_t *yr = out + (int64_t)n * D;
+        for (int t = 0; t < T; ++t) {
+            float q = 0.0f;
+            for (int i = t; i < D2; i += T) {
+                float v0 = B2F(xr[2 * i]), v1 = B2F(xr[2 * i + 1]);
+                q = fmaf(v0, v0, q);
+                q = fmaf(v1, v1, q);
+            }
+            pq[t] = q;
+        }
+        float rms_inv = 1.0f / sqrtf(oracle_ref_block_sum(pq, T) / (float)D + eps);
+        for (int e = 0; e < 2 * D2; ++e) {
+            float v = B2F(xr[e]) * rms_inv;
+            yr[e] = F2B(fmaf(v, 1.0f + B2F(sr[e]), B2F(hr[e])));
+        }
+    }
+    free(pq);
+}
+
+/* gemma_ops.cu:132-177: scalar loop over D, block of min(roundup32(D), 1024) threads */
+void oracle_gemma_rms_norm(const uint16_t *x, const uint16_t *weight, uint16_t *out, int N,
+                           int D, float eps) {
+    int T = (D <= 1024) ? ((D + 31) / 32 * 32) : 1024;
+    if (T < 32) T = 32;
+    float *pq = calloc((size_t)T, sizeof(float));
+    for (int n = 0; n < N; ++n) {
+        const uint16_t *xr = x + (int64_t)n * D;
+        uint16_t *yr = out + (int64_t)n * D;
+        for (int t = 0; t < T; ++t) {
+            float q = 0.0f;
+            for (int i = t; i < D; i += T) {
+                float v = B2F(xr[i]);
+                q += v * v;
+            }
+            pq[t] = q;
+        }
+        float rms_inv = 1.0f / sqrtf(oracle_ref_block_sum(pq, T) / (float)D + eps);
+        for (int i = 0; i < D; ++i) {
+            float v = B2F(xr[i]) * rms_inv;
+            yr[i] = F2B(v * (1.0f + B2F(weight[i])));
+        }
+    }
+    free(pq);
+}
+
+/* ---------------------------------------------------------------- activations */
+
+static const float kSqrt2OverPi = 0.7978845608028654f; /* gelu.cu:8 */
+static const float kGeluCoeff = 0.044715f;             /* gelu.cu:9 */
+
+/* gelu.cu:22-31 */
+static float gelu_tanh_f(float v) {
+    float inner = kSqrt2OverPi * fmaf(kGeluCoeff * (v * v), v, v);
+    float half_v = 0.5f * v;
+    return fmaf(half_v, tanhf(inner), half_v);
+}
+
+/* gelu.cu:12-34 (bias NULL) and :37-64 */
+void oracle_gelu_tanh(const uint16_t *x, const uint16_t *bias, uint16_t *out, int64_t N, int D) {
+    int64_t N2 = N / 2;
+    for (int64_t e = 0; e < 2 * N2; ++e) {
+        float v = B2F(x[e]);
+        if (bias) v = v + B2F(bias[e % D]);
+        out[e] = F2B(gelu_tanh_f(v));
+    }
+}
+
+/* silu.cu:7-24 (bias NULL) and :26-47 */
+void oracle_silu(const uint16_t *x, const uint16_t *bias, uint16_t *out, int64_t N, int D) {
+    int64_t N2 = N / 2;
+    for (int64_t e = 0; e < 2 * N2; ++e) {
+        float v = B2F(x[e]);
+        if (bias) v = v + B2F(bias[e % D]);
+        out[e] = F2B(v / (1.0f + expf(-v)));
+    }
+}
+
+/* gemma_ops.cu:5-22: inner = c1*(g + c2*g*g*g), nvcc folds the add into an fma */
+void oracle_gated_gelu(const uint16_t *gate, const uint16_t *up, uint16_t *out, int64_t N) {
+    for (int64_t i = 0; i < N; ++i) {
+        float g = B2F(gate[i]), u = B2F(up[i]);
+        float inner = 0.7978845608f * fmaf(0.044715f * g * g, g, g);
+        float gelu_g = 0.5f * g * (1.0f + tanhf(inner));
+        out[i] = F2B(gelu_g * u);
+    }
+}
+
+/* ---------------------------------------------------------------- elementwise */
+
+/* elementwise.cu:37-53 */
+void oracle_add(const uint16_t *a, const uint16_t *b, uint16_t *out, int64_t N) {
+    for (int64_t i = 0; i < N / 2 * 2; ++i) out[i] = F2B(B2F(a[i]) + B2F(b[i]));
+}
+
+/* elementwise.cu:125-141 */
+void oracle_mul(const uint16_t *a, const uint16_t *b, uint16_t *out, int64_t N) {
+    for (int64_t i = 0; i < N / 2 * 2; ++i) out[i] = F2B(B2F(a[i]) * B2F(b[i]));
+}
+
+/* elementwise.cu:216-236 */
+void oracle_scale_shift_bcast(const uint16_t *x, const uint16_t *scale, const uint16_t *shift,
+                              uint16_t *out, int M, int D) {
+    int D2 = D / 2;
+    for (int64_t m = 0; m < M; ++m)
+        for (int d = 0; d < 2 * D2; ++d) {
+            int64_t e = m * (2 * D2) + d;
+            out[e] = F2B(fmaf(B2F(x[e]), 1.0f + B2F(scale[d]), B2F(shift[d])));
+        }
+}
+
+/* elementwise.cu:249-269 */
+void oracle_residual_gate_bcast(const uint16_t *x, const uint16_t *y, const uint16_t *gate,
+                                uint16_t *out, int M, int D) {
+    int D2 = D / 2;
+    for (int64_t m = 0; m < M; ++m)
+        for (int d = 0; d < 2 * D2; ++d) {
+            int64_t e = m * (2 * D2) + d;
+            out[e] = F2B(fmaf(B2F(y[e]), B2F(gate[d]), B2F(x[e])));
+        }
+}
+
+/* ----------------------------------------------------------------------- RoPE */
+
+/* rope.cu:72-108. bf16 x bf16 products are exact in fp32, so the rotation has a
+ * single rounding whichever way nvcc contracts it. */
+void oracle_rope_cosmos_strided(uint16_t *x, const uint16_t *cos_t, const uint16_t *sin_t,
+                                int B, int S, int H, int HD) {
+    int half = HD / 2;
+    for (int64_t row = 0; row < (int64_t)B * S; ++row) {
+        int s = (int)(row % S);
+        for (int h = 0; h < H; ++h) {
+            uint16_t *base = x + row * H * HD + (int64_t)h * HD;
+            for (int i = 0; i < half; ++i) {
+                float xr = B2F(base[i]), xi = B2F(base[i + half]);
+                float c = B2F(cos_t[(int64_t)s * HD + i]), sn = B2F(sin_t[(int64_t)s * HD + i]);
+                base[i] = F2B(xr * c - xi * sn);
+                base[i + half] = F2B(xi * c + xr * sn);
+            }
+        }
+    }
+}
+
+static float rot2(float a, float b, float c, float d, int mode, float sign) {
+    /* a*b + sign*(c*d), with the contraction choice `mode` */
+    switch (mode) {
+    case 0: return fmaf(a, b, sign * (c * d));
+    case 1: return fmaf(sign * c, d, a * b);
+    default: return a * b + sign * (c * d);
+    }
+}
+
+/* gemma_ops.cu:62-87 */
+void oracle_rope_standard(uint16_t *x, const float *cos_t, const float *sin_t,
+                          int total_rows, int T, int D, int mode_a, int mode_b) {
+    int half = D / 2;
+    for (int64_t row = 0; row < total_rows; ++row) {
+        int t = (int)(row % T);
+        for (int d = 0; d < half; ++d) {
+            float c = cos_t[(int64_t)t * half + d], s = sin_t[(int64_t)t * half + d];
+            int64_t i1 = row * D + d, i2 = row * D + half + d;
+            float x1 = B2F(x[i1]), x2 = B2F(x[i2]);
+            float o1 = rot2(x1, c, x2, s, mode_a, -1.0f);
+            float o2 = rot2(x2, c, x1, s, mode_b, 1.0f);
+            x[i1] = F2B(o1);
+            x[i2] = F2B(o2);
+        }
+    }
+}
+
+/* ------------------------------------------------------------------ gather */
+
+/* gemma_ops.cu:34-45 */
+void oracle_embedding_lookup(const uint16_t *table, const int32_t *ids, uint16_t *out, int T,
+                             int D, int vocab) {
+    for (int t = 0; t < T; ++t) {
+        int id = ids[t];
+        if (id < 0 || id >= vocab)
+            memset(out + (int64_t)t * D, 0, (size_t)D * 2);
+        else
+            memcpy(out + (int64_t)t * D, table + (int64_t)id * D, (size_t)D * 2);
+    }
+}
+
+/* ------------------------------------------------------------- VAE channel norm */
+
+/* vae_kernels.cu:60-81, launched per batch item at :83-98 */
+void oracle_rms_norm_channel(const uint16_t *x, const uint16_t *gamma, uint16_t *out, int B,
+                             int C, int spatial, float eps) {
+    for (int b = 0; b < B; ++b) {
+        const uint16_t *xb = x + (int64_t)b * C * spatial;
+        uint16_t *ob = out + (int64_t)b * C * spatial;
+        for (int s = 0; s < spatial; ++s) {
+            float q = 0.0f;
+            for (int c = 0; c < C; ++c) {
+                float v = B2F(xb[(int64_t)c * spatial + s]);
+                q += v * v;
+            }
+            float rms = 1.0f / sqrtf(q / (float)C + eps);
+            for (int c = 0; c < C; ++c) {
+                int64_t i = (int64_t)c * spatial + s;
+                ob[i] = F2B((B2F(xb[i]) * rms) * B2F(gamma[c]));
+            }
+        }
+    }
+}
+
+/* ------------------------------------------------------------- host tables */
+
+/* transformer.cpp:182-197 */
+void oracle_timestep_sinusoid(float t, int dim, uint16_t *out) {
+    int half = dim / 2;
+    for (int i = 0; i < half; ++i) {
+        float freq = expf(-logf(10000.0f) * (float)i / (float)half);
+        float angle = t * freq;
+        out[i] = F2B(cosf(angle));
+        out[half + i] = F2B(sinf(angle));
+    }
+}
+
+static void axis_freqs(int dim, float theta, float *freqs) {
+    for (int i = 0; i < dim / 2; ++i) freqs[i] = 1.0f / powf(theta, (float)(2 * i) / (float)dim);
+}
+
+/* transformer.cpp:213-318 */
+void oracle_cosmos_rope_tables(int pe_t, int pe_h, int pe_w, int HD, uint16_t *cos_out,
+                               uint16_t *sin_out) {
+    int dim_h = (HD / 6) * 2, dim_w = (HD / 6) * 2, dim_t = HD - dim_h - dim_w;
+    float h_ntk = powf(4.0f, (float)dim_h / (float)(dim_h - 2));
+    float w_ntk = powf(4.0f, (float)dim_w / (float)(dim_w - 2));
+    float t_ntk = powf(1.0f, (float)dim_t / (float)(dim_t - 2));
+    float *ft = malloc(sizeof(float) * (size_t)(dim_t / 2 + 1));
+    float *fh = malloc(sizeof(float) * (size_t)(dim_h / 2 + 1));
+    float *fw = malloc(sizeof(float) * (size_t)(dim_w / 2 + 1));
+    axis_freqs(dim_t, 10000.0f * t_ntk, ft);
+    axis_freqs(dim_h, 10000.0f * h_ntk, fh);
+    axis_freqs(dim_w, 10000.0f * w_ntk, fw);
+    float *crow = malloc(sizeof(float) * (size_t)HD), *srow = malloc(sizeof(float) * (size_t)HD);
+    for (int a = 0; a < pe_t; ++a)
+        for (int b = 0; b < pe_h; ++b)
+            for (int c = 0; c < pe_w; ++c) {
+                int idx = (a * pe_h + b) * pe_w + c, off = 0;
+                for (int d = 0; d < dim_t / 2; ++d, ++off) {
+                    float ang = (float)a * ft[d];
+                    crow[off] = cosf(ang);
+                    srow[off] = sinf(ang);
+                }
+                for (int d = 0; d < dim_h / 2; ++d, ++off) {
+                    float ang = (float)b * fh[d];
+                    crow[off] = cosf(ang);
+                    srow[off] = sinf(ang);
+                }
+                for (int d = 0; d < dim_w / 2; ++d, ++off) {
+                    float ang = (float)c * fw[d];
+                    crow[off] = cosf(ang);
+                    srow[off] = sinf(ang);
+                }
+                for (int d = 0; d < off; ++d) {
+                    crow[off + d] = crow[d];
+                    srow[off + d] = srow[d];
+                }
+                for (int d = 0; d < HD; ++d) {
+                    cos_out[(int64_t)idx * HD + d] = F2B(crow[d]);
+                    sin_out[(int64_t)idx * HD + d] = F2B(srow[d]);
+                }
+            }
+    free(ft);
+    free(fh);
+    free(fw);
+    free(crow);
+    free(srow);
+}
+
+/* qwen3.cpp:12-23, llm_adapter.cpp:11-22 */
+void oracle_standard_rope_tables(int T, int HD, float theta, float *cos_out, float *sin_out) {
+    int half = HD / 2;
+    for (int t = 0; t < T; ++t)
+        for (int d = 0; d < half; ++d) {
+            float freq = 1.0f / powf(theta, (float)(2 * d) / (float)HD);
+            float angle = (float)t * freq;
+            cos_out[t * half + d] = cosf(angle);
+            sin_out[t * half + d] = sinf(angle);
+        }
+}

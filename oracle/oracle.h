@@ -1,0 +1,124 @@
+/*
+ * oracle.h -- TEST INFRASTRUCTURE ONLY.
+ *
+ * A plain-C restatement of the arithmetic of anima.cu's fused layer kernels
+ * (the .cu files under src/kernels) and of the host-side table builders that feed them. It is
+ * the checker the parity tests compare the CUDA library against; nothing in the
+ * product links or calls it. Only tests/, __graft_entry__.smoke() and the
+ * cpu_baseline leg of bench.py load it.
+ *
+ * bf16 values travel as uint16_t bit patterns. Each function names the
+ * reference file:line whose arithmetic it follows. Where the reference's
+ * floating-point result depends on its CUDA thread layout (block reductions),
+ * the restatement reproduces that layout: per-thread strided partial sums, the
+ * warp shfl_down tree (src/cuda_utils.cuh:46-50) and the cross-warp tree
+ * through shared memory (src/kernels/layer_norm.cu:7-19).
+ *
+ * The reference's per-element expressions leave a few fused-multiply-add
+ * contractions to nvcc. Those choices are parameters here ("mode" arguments);
+ * the parity tests pin them against the reference kernels' own outputs.
+ */
+#ifndef ANIMA_ORACLE_H
+#define ANIMA_ORACLE_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* bf16 <-> f32, round-to-nearest-even with NaN -> 0x7fff (cuda_bf16 host semantics). */
+float    oracle_bf16_to_f32(uint16_t b);
+uint16_t oracle_f32_to_bf16(float f);
+
+/* The reference's CTA reduction of per-thread partials (layer_norm.cu:7-19,
+ * rms_norm.cu:40-53): nthreads is the launched block size. */
+float oracle_ref_block_sum(const float *per_thread, int nthreads);
+
+/* Block size the reference launchers pick for a row of D elements
+ * (layer_norm.cu:68-70, rms_norm.cu:126-128). */
+int oracle_ref_row_threads(int D);
+
+/* layer_norm.cu:26-72 -- LayerNorm without affine. */
+void oracle_layer_norm(const uint16_t *x, uint16_t *out, int N, int D, float eps,
+                       int var_mode);
+
+/* layer_norm.cu:83-135 -- LN(x)*(1+scale[d])+shift[d]. */
+void oracle_adaln_layernorm(const uint16_t *x, const uint16_t *scale, const uint16_t *shift,
+                            uint16_t *out, int N, int D, float eps, int var_mode);
+
+/* layer_norm.cu:146-209 -- hidden = x + y*gate[d] (in place, bf16);
+ * normed = LN(hidden)*(1+scale)+shift. Stats from the fp32 h, pass 2 from bf16(h).
+ * sq_mode: 0 fma(h0,h0,h1*h1), 1 fma(h1,h1,h0*h0), 2 h0*h0+h1*h1 unfused. */
+void oracle_residual_gate_adaln(uint16_t *hidden, const uint16_t *sub_out,
+                                const uint16_t *gate, const uint16_t *scale,
+                                const uint16_t *shift, uint16_t *normed, int N, int D,
+                                float eps, int sq_mode, int var_mode);
+
+/* rms_norm.cu:9-67,118-131 -- x*rsqrt(mean x^2+eps)*w[d]; weight may be NULL. */
+void oracle_rms_norm(const uint16_t *x, const uint16_t *weight, uint16_t *out, int N, int D,
+                     float eps);
+
+/* adaln.cu:11-58 -- RMS(x)*(1+scale[n,d])+shift[n,d] with per-row scale/shift. */
+void oracle_adaln_rms_norm(const uint16_t *x, const uint16_t *scale, const uint16_t *shift,
+                           uint16_t *out, int N, int D, float eps);
+
+/* gemma_ops.cu:132-177 -- RMS(x)*(1+w[d]), scalar loop, block over D. */
+void oracle_gemma_rms_norm(const uint16_t *x, const uint16_t *weight, uint16_t *out, int N,
+                           int D, float eps);
+
+/* gelu.cu:12-34 / :37-64 -- tanh GELU, optionally of x+bias[d]. bias may be NULL. */
+void oracle_gelu_tanh(const uint16_t *x, const uint16_t *bias, uint16_t *out, int64_t N, int D);
+
+/* silu.cu:7-24 / :26-47 -- x/(1+exp(-x)), optionally of x+bias[d]. bias may be NULL. */
+void oracle_silu(const uint16_t *x, const uint16_t *bias, uint16_t *out, int64_t N, int D);
+
+/* gemma_ops.cu:5-22 -- gelu_tanh(gate)*up, scalar formula. */
+void oracle_gated_gelu(const uint16_t *gate, const uint16_t *up, uint16_t *out, int64_t N);
+
+/* elementwise.cu:37-53 (add), :125-141 (mul). */
+void oracle_add(const uint16_t *a, const uint16_t *b, uint16_t *out, int64_t N);
+void oracle_mul(const uint16_t *a, const uint16_t *b, uint16_t *out, int64_t N);
+
+/* elementwise.cu:216-236 -- fma(x, 1+scale[d], shift[d]). */
+void oracle_scale_shift_bcast(const uint16_t *x, const uint16_t *scale, const uint16_t *shift,
+                              uint16_t *out, int M, int D);
+
+/* elementwise.cu:249-269 -- fma(y, gate[d], x). */
+void oracle_residual_gate_bcast(const uint16_t *x, const uint16_t *y, const uint16_t *gate,
+                                uint16_t *out, int M, int D);
+
+/* rope.cu:72-108 -- in-place half-split rotation on [B*S, H*HD] with bf16 [S,HD] tables. */
+void oracle_rope_cosmos_strided(uint16_t *x, const uint16_t *cos_t, const uint16_t *sin_t,
+                                int B, int S, int H, int HD);
+
+/* gemma_ops.cu:62-87 -- in-place half-split rotation on rows of [rows, D], t = row % T,
+ * fp32 tables [T, D/2]. mode_a picks the contraction of x1*c - x2*s, mode_b that of
+ * x2*c + x1*s: 0 fma(first product, ., -second), 1 fma(second, ., first), 2 unfused. */
+void oracle_rope_standard(uint16_t *x, const float *cos_t, const float *sin_t,
+                          int total_rows, int T, int D, int mode_a, int mode_b);
+
+/* gemma_ops.cu:34-45 -- out[t,:] = table[ids[t],:]. Out-of-range ids produce zeros
+ * here (the reference does not check them). */
+void oracle_embedding_lookup(const uint16_t *table, const int32_t *ids, uint16_t *out, int T,
+                             int D, int vocab);
+
+/* vae_kernels.cu:60-98 -- NCHW channel RMSNorm times gamma[c]; sequential sum over c. */
+void oracle_rms_norm_channel(const uint16_t *x, const uint16_t *gamma, uint16_t *out, int B,
+                             int C, int spatial, float eps);
+
+/* transformer.cpp:182-197 -- flip_sin_to_cos sinusoid of one timestep, bf16 [dim]. */
+void oracle_timestep_sinusoid(float t, int dim, uint16_t *out);
+
+/* transformer.cpp:213-318 -- Cosmos 3-axis RoPE tables, bf16 [pe_t*pe_h*pe_w, HD]. */
+void oracle_cosmos_rope_tables(int pe_t, int pe_h, int pe_w, int HD, uint16_t *cos_out,
+                               uint16_t *sin_out);
+
+/* qwen3.cpp:12-23 (theta 1e6) and llm_adapter.cpp:11-22 (theta 1e4) -- fp32 [T, HD/2]. */
+void oracle_standard_rope_tables(int T, int HD, float theta, float *cos_out, float *sin_out);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif

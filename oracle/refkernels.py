@@ -1,0 +1,83 @@
+"""TEST INFRASTRUCTURE ONLY: ctypes access to the reference's C++ kernel launchers.
+
+`load_reference()` opens oracle/_ref/libref_kernels.so, the reference's own
+src/kernels/*.cu compiled unchanged for sm_100a (oracle/Makefile). It is the GPU-side
+oracle of the parity tests and the kernels that `bench.py --impl reference` times.
+
+The launchers have C++ linkage, so they are resolved by their mangled names
+(src/kernels/kernels.h). libanima_b200.so exports the same mangled names through its
+compatibility shim; `load_launchers(path)` binds either library the same way, which is
+how the tests check that the shim forwards correctly.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+from ctypes import c_float, c_int, c_int64, c_void_p
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+REF_LIB_PATH = os.path.join(_HERE, "_ref", "libref_kernels.so")
+
+P, I32, I64, F32 = c_void_p, c_int, c_int64, c_float
+
+# launcher -> (mangled symbol, argument types); kernels.h line ranges in comments.
+LAUNCHERS = {
+    "rms_norm_bf16": ("_Z13rms_norm_bf16PK13__nv_bfloat16S1_PS_iifP11CUstream_st", (P, P, P, I32, I32, F32, P)),  # :9-11
+    "layer_norm_bf16": ("_Z15layer_norm_bf16PK13__nv_bfloat16PS_iifP11CUstream_st", (P, P, I32, I32, F32, P)),  # :14-16
+    "adaln_layernorm_bf16": ("_Z20adaln_layernorm_bf16PK13__nv_bfloat16S1_S1_PS_iifP11CUstream_st",
+                             (P, P, P, P, I32, I32, F32, P)),  # :19-22
+    "residual_gate_adaln_bf16": ("_Z24residual_gate_adaln_bf16P13__nv_bfloat16PKS_S2_S2_S2_S0_iifP11CUstream_st",
+                                 (P, P, P, P, P, P, I32, I32, F32, P)),  # :25-30
+    "gelu_tanh_bf16": ("_Z14gelu_tanh_bf16PK13__nv_bfloat16PS_lP11CUstream_st", (P, P, I64, P)),  # :33
+    "gelu_tanh_bias_bf16": ("_Z19gelu_tanh_bias_bf16PK13__nv_bfloat16S1_PS_liP11CUstream_st",
+                            (P, P, P, I64, I32, P)),  # :34-36
+    "silu_bf16": ("_Z9silu_bf16PK13__nv_bfloat16PS_lP11CUstream_st", (P, P, I64, P)),  # :39
+    "silu_bias_bf16": ("_Z14silu_bias_bf16PK13__nv_bfloat16S1_PS_liP11CUstream_st", (P, P, P, I64, I32, P)),  # :40-42
+    "rope_cosmos_strided_bf16": ("_Z24rope_cosmos_strided_bf16P13__nv_bfloat16PKS_S2_iiiiP11CUstream_st",
+                                 (P, P, P, I32, I32, I32, I32, P)),  # :51-53
+    "adaln_rms_norm_bf16": ("_Z19adaln_rms_norm_bf16PK13__nv_bfloat16S1_S1_PS_iifP11CUstream_st",
+                            (P, P, P, P, I32, I32, F32, P)),  # :60-63
+    "add_bf16": ("_Z8add_bf16PK13__nv_bfloat16S1_PS_lP11CUstream_st", (P, P, P, I64, P)),  # :69-71
+    "mul_bf16": ("_Z8mul_bf16PK13__nv_bfloat16S1_PS_lP11CUstream_st", (P, P, P, I64, P)),  # :78-80
+    "scale_shift_bcast_bf16": ("_Z22scale_shift_bcast_bf16PK13__nv_bfloat16S1_S1_PS_iiP11CUstream_st",
+                               (P, P, P, P, I32, I32, P)),  # :87-89
+    "residual_gate_bcast_bf16": ("_Z24residual_gate_bcast_bf16PK13__nv_bfloat16S1_S1_PS_iiP11CUstream_st",
+                                 (P, P, P, P, I32, I32, P)),  # :90-92
+    "gated_gelu_bf16": ("_Z15gated_gelu_bf16PK13__nv_bfloat16S1_PS_lP11CUstream_st", (P, P, P, I64, P)),  # :138-140
+    "embedding_lookup_bf16": ("_Z21embedding_lookup_bf16PK13__nv_bfloat16PKiPS_iiP11CUstream_st",
+                              (P, P, P, I32, I32, P)),  # :142-144
+    "rope_standard_bf16": ("_Z18rope_standard_bf16P13__nv_bfloat16PKfS2_iiiP11CUstream_st",
+                           (P, P, P, I32, I32, I32, P)),  # :145-147
+    "gemma_rms_norm_bf16": ("_Z19gemma_rms_norm_bf16PK13__nv_bfloat16S1_PS_iifP11CUstream_st",
+                            (P, P, P, I32, I32, F32, P)),  # :151-153
+    "rms_norm_channel_bf16": ("_Z21rms_norm_channel_bf16PK13__nv_bfloat16S1_PS_iiifP11CUstream_st",
+                              (P, P, P, I32, I32, I32, F32, P)),  # :177-180
+}
+
+
+class Launchers:
+    """Attribute access to the launchers of one library: `L.rms_norm_bf16(...)`."""
+
+    def __init__(self, path: str):
+        if not os.path.exists(path):
+            raise ImportError(f"{path} is missing")
+        # RTLD_LOCAL: the reference and the B200 library export the same C++ names.
+        self.cdll = ctypes.CDLL(path, mode=os.RTLD_LOCAL | os.RTLD_NOW)
+        self.path = path
+        for name, (sym, argtypes) in LAUNCHERS.items():
+            fn = getattr(self.cdll, sym)
+            fn.argtypes = list(argtypes)
+            fn.restype = None
+            setattr(self, name, fn)
+
+
+def load_launchers(path: str) -> Launchers:
+    return Launchers(path)
+
+
+def load_reference() -> Launchers:
+    return Launchers(REF_LIB_PATH)
+
+
+def reference_available() -> bool:
+    return os.path.exists(REF_LIB_PATH)

@@ -1,0 +1,161 @@
+"""Generates the golden fixtures in this directory by running the REFERENCE's own CUDA
+kernels (src/kernels/*.cu compiled unchanged for sm_100a into oracle/_ref) on small
+seeded inputs. Needs a GPU and oracle/_ref/libref_kernels.so; run on a B200 box:
+
+    python tests/golden/make_golden.py --out tests/golden
+
+Each fixture is an .npz of uint16 bf16 bit patterns (fp32 / int32 arrays where the
+launcher takes them) holding the inputs and the reference outputs. The CPU test
+tests/test_cpu_golden.py pins the CPU restatement in oracle/ against them.
+"""
+import argparse
+import os
+import sys
+
+import numpy as np
+import torch
+
+ROOT = os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+sys.path.insert(0, os.path.join(ROOT, "oracle"))
+
+import oracle as O  # noqa: E402  (inputs, tables and bf16 helpers only)
+import refkernels  # noqa: E402
+
+
+def dev(a):
+    a = np.ascontiguousarray(a)
+    if a.dtype == np.uint16:
+        a = a.view(np.int16)
+    return torch.from_numpy(a).cuda()
+
+
+def host(t, dtype=np.uint16):
+    return t.cpu().numpy().view(dtype)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--out", default=os.path.dirname(os.path.abspath(__file__)))
+    args = ap.parse_args()
+    os.makedirs(args.out, exist_ok=True)
+    R = refkernels.load_reference()
+    s = torch.cuda.current_stream().cuda_stream
+    rng = np.random.default_rng(20261201)
+    fx = {}
+
+    def put(name, **arrays):
+        fx[name] = arrays
+
+    # ---- row norms (layer_norm.cu, rms_norm.cu, adaln.cu, gemma_ops.cu)
+    for N, D in [(8, 2048), (3, 96), (2, 4096), (16, 128)]:
+        x = O.randn_bf16(rng, (N, D), mean=0.2)
+        out = torch.empty((N, D), dtype=torch.int16, device="cuda")
+        R.layer_norm_bf16(dev(x).data_ptr(), out.data_ptr(), N, D, 1e-6, s)
+        torch.cuda.synchronize()
+        put(f"layer_norm_{N}x{D}", x=x, out=host(out))
+    for N, D in [(8, 2048), (4, 128), (2, 4096)]:
+        x, sc, sh = O.randn_bf16(rng, (N, D)), O.randn_bf16(rng, D, std=0.1), O.randn_bf16(rng, D, std=0.1)
+        out = torch.empty((N, D), dtype=torch.int16, device="cuda")
+        R.adaln_layernorm_bf16(dev(x).data_ptr(), dev(sc).data_ptr(), dev(sh).data_ptr(), out.data_ptr(), N, D,
+                               1e-6, s)
+        torch.cuda.synchronize()
+        put(f"adaln_layernorm_{N}x{D}", x=x, scale=sc, shift=sh, out=host(out))
+    for N, D in [(8, 2048), (2, 4096), (4, 96)]:
+        x, y = O.randn_bf16(rng, (N, D)), O.randn_bf16(rng, (N, D))
+        g, sc, sh = (O.randn_bf16(rng, D, std=0.1) for _ in range(3))
+        h = dev(x)
+        out = torch.empty((N, D), dtype=torch.int16, device="cuda")
+        R.residual_gate_adaln_bf16(h.data_ptr(), dev(y).data_ptr(), dev(g).data_ptr(), dev(sc).data_ptr(),
+                                   dev(sh).data_ptr(), out.data_ptr(), N, D, 1e-6, s)
+        torch.cuda.synchronize()
+        put(f"residual_gate_adaln_{N}x{D}", x=x, y=y, gate=g, scale=sc, shift=sh, hidden=host(h), normed=host(out))
+    for N, D, weighted in [(64, 128, True), (8, 1024, True), (4, 2048, False), (2, 4096, True), (3, 64, True)]:
+        x, w = O.randn_bf16(rng, (N, D)), O.randn_bf16(rng, D, mean=1.0, std=0.02)
+        out = torch.empty((N, D), dtype=torch.int16, device="cuda")
+        dw = dev(w) if weighted else None
+        R.rms_norm_bf16(dev(x).data_ptr(), dw.data_ptr() if weighted else None, out.data_ptr(), N, D, 1e-6, s)
+        torch.cuda.synchronize()
+        put(f"rms_norm_{N}x{D}_{'w' if weighted else 'nw'}", x=x, weight=w if weighted else np.zeros(0, np.uint16),
+            out=host(out))
+    N, D = 4, 2048
+    x, sc, sh = O.randn_bf16(rng, (N, D)), O.randn_bf16(rng, (N, D), std=0.1), O.randn_bf16(rng, (N, D), std=0.1)
+    out = torch.empty((N, D), dtype=torch.int16, device="cuda")
+    R.adaln_rms_norm_bf16(dev(x).data_ptr(), dev(sc).data_ptr(), dev(sh).data_ptr(), out.data_ptr(), N, D, 1e-6, s)
+    torch.cuda.synchronize()
+    put("adaln_rms_norm_4x2048", x=x, scale=sc, shift=sh, out=host(out))
+    N, D = 4, 1024
+    x, w = O.randn_bf16(rng, (N, D)), O.randn_bf16(rng, D, std=0.1)
+    out = torch.empty((N, D), dtype=torch.int16, device="cuda")
+    R.gemma_rms_norm_bf16(dev(x).data_ptr(), dev(w).data_ptr(), out.data_ptr(), N, D, 1e-6, s)
+    torch.cuda.synchronize()
+    put("gemma_rms_norm_4x1024", x=x, weight=w, out=host(out))
+
+    # ---- activations and elementwise (gelu.cu, silu.cu, elementwise.cu, gemma_ops.cu)
+    ext = O.f32_to_bf16(np.array([0, -0.0, 1e-30, 3, -3, 8, -8, 20, -20, 88, -88, 3e38, -3e38], np.float32))
+    for op in ("gelu_tanh", "silu"):
+        x = np.concatenate([O.randn_bf16(rng, 8190, std=3.0), ext])
+        out = torch.zeros(x.size, dtype=torch.int16, device="cuda")
+        getattr(R, op + "_bf16")(dev(x).data_ptr(), out.data_ptr(), x.size, s)
+        M, Db = 16, 96
+        xb, b = O.randn_bf16(rng, (M, Db), std=2.0), O.randn_bf16(rng, Db, std=0.5)
+        outb = torch.zeros(M * Db, dtype=torch.int16, device="cuda")
+        getattr(R, op + "_bias_bf16")(dev(xb).data_ptr(), dev(b).data_ptr(), outb.data_ptr(), M * Db, Db, s)
+        torch.cuda.synchronize()
+        put(op, x=x, out=host(out))
+        put(op + "_bias", x=xb, bias=b, out=host(outb))
+    for op in ("add", "mul", "gated_gelu"):
+        a, b = O.randn_bf16(rng, 4096, std=2.0), O.randn_bf16(rng, 4096)
+        out = torch.zeros(4096, dtype=torch.int16, device="cuda")
+        getattr(R, op + "_bf16")(dev(a).data_ptr(), dev(b).data_ptr(), out.data_ptr(), 4096, s)
+        torch.cuda.synchronize()
+        put(op, a=a, b=b, out=host(out))
+    M, D = 8, 2048
+    x, sc, sh, y = (O.randn_bf16(rng, (M, D)), O.randn_bf16(rng, D, std=0.1), O.randn_bf16(rng, D, std=0.1),
+                    O.randn_bf16(rng, (M, D)))
+    out = torch.empty((M, D), dtype=torch.int16, device="cuda")
+    R.scale_shift_bcast_bf16(dev(x).data_ptr(), dev(sc).data_ptr(), dev(sh).data_ptr(), out.data_ptr(), M, D, s)
+    out2 = torch.empty((M, D), dtype=torch.int16, device="cuda")
+    R.residual_gate_bcast_bf16(dev(x).data_ptr(), dev(y).data_ptr(), dev(sc).data_ptr(), out2.data_ptr(), M, D, s)
+    torch.cuda.synchronize()
+    put("scale_shift_bcast", x=x, scale=sc, shift=sh, out=host(out))
+    put("residual_gate_bcast", x=x, y=y, gate=sc, out=host(out2))
+
+    # ---- RoPE (rope.cu, gemma_ops.cu); tables from the restated host builders
+    B, pe, H, HD = 2, (1, 4, 4), 4, 128
+    S = 16
+    ct, st = O.cosmos_rope_tables(*pe, HD=HD)
+    x = O.randn_bf16(rng, (B * S, H * HD))
+    xd = dev(x)
+    R.rope_cosmos_strided_bf16(xd.data_ptr(), dev(ct).data_ptr(), dev(st).data_ptr(), B, S, H, HD, s)
+    torch.cuda.synchronize()
+    put("rope_cosmos_strided", x=x, cos=ct, sin=st, out=host(xd), shape=np.array([B, S, H, HD], np.int32))
+    for heads, T, HD, theta in [(4, 16, 128, 1e6), (2, 9, 64, 1e4)]:
+        ct, st = O.standard_rope_tables(T, HD, theta)
+        x = O.randn_bf16(rng, (heads * T, HD))
+        xd = dev(x)
+        R.rope_standard_bf16(xd.data_ptr(), torch.from_numpy(ct).cuda().data_ptr(),
+                             torch.from_numpy(st).cuda().data_ptr(), heads * T, T, HD, s)
+        torch.cuda.synchronize()
+        put(f"rope_standard_{HD}", x=x, cos=ct, sin=st, out=host(xd), shape=np.array([heads * T, T, HD], np.int32))
+
+    # ---- gather and VAE channel norm (gemma_ops.cu, vae_kernels.cu)
+    V, D, T = 1000, 64, 32
+    table, ids = O.randn_bf16(rng, (V, D), std=0.02), rng.integers(0, V, T, dtype=np.int32)
+    out = torch.empty((T, D), dtype=torch.int16, device="cuda")
+    R.embedding_lookup_bf16(dev(table).data_ptr(), torch.from_numpy(ids).cuda().data_ptr(), out.data_ptr(), T, D, s)
+    torch.cuda.synchronize()
+    put("embedding_lookup", table=table, ids=ids, out=host(out))
+    for B, C, sp in [(1, 96, 64), (2, 32, 40)]:
+        x, g = O.randn_bf16(rng, (B, C, sp)), O.randn_bf16(rng, C, mean=1.0, std=0.02)
+        out = torch.empty((B, C, sp), dtype=torch.int16, device="cuda")
+        R.rms_norm_channel_bf16(dev(x).data_ptr(), dev(g).data_ptr(), out.data_ptr(), B, C, sp, 1e-6, s)
+        torch.cuda.synchronize()
+        put(f"rms_norm_channel_{B}x{C}x{sp}", x=x, gamma=g, out=host(out))
+
+    for name, arrays in fx.items():
+        np.savez_compressed(os.path.join(args.out, name + ".npz"), **arrays)
+    print(f"wrote {len(fx)} fixtures to {args.out}")
+
+
+if __name__ == "__main__":
+    main()

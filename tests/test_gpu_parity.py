@@ -1,0 +1,428 @@
+"""Parity of the B200 kernels (called through the C ABI) with
+  (1) the reference's own CUDA kernels, compiled unchanged for sm_100a -- expected
+      bit-exact, since the B200 kernels reproduce the reference's reduction order and
+      per-element expressions; and
+  (2) the CPU restatement in oracle/ -- within one bf16 ulp of the result, judged at
+      max(|result|, 2^-12) (the CPU's 1/sqrtf and libm tanhf/expf differ from the GPU's
+      rsqrtf/tanhf/expf in the last fp32 bits).
+Edge cases follow what the reference's callers exercise: in-place aliasing, N = 1, widths
+outside the fast paths (generic kernels), unaligned sub-buffers, odd lengths, tails.
+"""
+import numpy as np
+import pytest
+import torch
+
+import oracle as O
+from gpu_util import assert_bit_exact, assert_one_ulp, dev, empty_bf16, host, stream_ptr
+
+pytestmark = pytest.mark.gpu
+
+ORACLE_MAX_ELEMS = 1 << 21  # the CPU restatement runs on inputs up to this size
+
+
+def _modvec(rng, D, std=0.1):
+    return O.randn_bf16(rng, D, std=std)
+
+
+def _weight(rng, D):
+    return O.randn_bf16(rng, D, mean=1.0, std=0.02)
+
+
+ROW_SHAPES = [(1, 2048), (37, 2048), (4096, 2048), (5, 1024), (300, 1024), (1, 128), (2049, 128),
+              (3, 64), (17, 256), (9, 512), (3, 96), (4, 2050), (2, 4096), (2, 6)]
+
+
+# ---------------------------------------------------------------- row norms
+@pytest.mark.parametrize("N,D", ROW_SHAPES)
+@pytest.mark.parametrize("weighted", [True, False])
+def test_rms_norm(anima, ref, rng, N, D, weighted):
+    x = O.randn_bf16(rng, (N, D))
+    w = _weight(rng, D) if weighted else None
+    dx = dev(x)
+    dw = dev(w) if weighted else None
+    out, out_ref = empty_bf16((N, D)), empty_bf16((N, D))
+    anima.rms_norm(dx, dw, out, N, D, 1e-6)
+    ref.rms_norm_bf16(dx.data_ptr(), dw.data_ptr() if weighted else None, out_ref.data_ptr(), N, D, 1e-6, stream_ptr())
+    # in place, as the DiT QK norm calls it (transformer.cpp:350)
+    xi = dev(x)
+    anima.rms_norm(xi, dw, xi, N, D, 1e-6)
+    torch.cuda.synchronize()
+    assert_bit_exact(host(out), host(out_ref), "rms_norm vs reference")
+    assert_bit_exact(host(xi), host(out_ref), "rms_norm in place")
+    if N * D <= ORACLE_MAX_ELEMS:
+        assert_one_ulp(host(out), O.rms_norm(x, w, N, D), "rms_norm vs oracle")
+
+
+@pytest.mark.parametrize("N,D", ROW_SHAPES)
+def test_layer_norm(anima, ref, rng, N, D):
+    x = O.randn_bf16(rng, (N, D), mean=0.3)
+    dx = dev(x)
+    out, out_ref = empty_bf16((N, D)), empty_bf16((N, D))
+    anima.layer_norm(dx, out, N, D, 1e-6)
+    ref.layer_norm_bf16(dx.data_ptr(), out_ref.data_ptr(), N, D, 1e-6, stream_ptr())
+    xi = dev(x)
+    anima.layer_norm(xi, xi, N, D, 1e-6)  # in place (transformer.cpp:563)
+    torch.cuda.synchronize()
+    assert_bit_exact(host(out), host(out_ref), "layer_norm vs reference")
+    assert_bit_exact(host(xi), host(out_ref), "layer_norm in place")
+    if N * D <= ORACLE_MAX_ELEMS:
+        assert_one_ulp(host(out), O.layer_norm(x, N, D), "layer_norm vs oracle")
+
+
+@pytest.mark.parametrize("N,D", ROW_SHAPES)
+def test_adaln_layernorm(anima, ref, rng, N, D):
+    x = O.randn_bf16(rng, (N, D))
+    sc, sh = _modvec(rng, D), _modvec(rng, D)
+    dx, dsc, dsh = dev(x), dev(sc), dev(sh)
+    out, out_ref = empty_bf16((N, D)), empty_bf16((N, D))
+    anima.adaln_layernorm(dx, dsc, dsh, out, N, D, 1e-6)
+    ref.adaln_layernorm_bf16(dx.data_ptr(), dsc.data_ptr(), dsh.data_ptr(), out_ref.data_ptr(), N, D, 1e-6,
+                             stream_ptr())
+    torch.cuda.synchronize()
+    assert_bit_exact(host(out), host(out_ref), "adaln_layernorm vs reference")
+    if N * D <= ORACLE_MAX_ELEMS:
+        assert_one_ulp(host(out), O.adaln_layernorm(x, sc, sh, N, D), "adaln_layernorm vs oracle")
+
+
+@pytest.mark.parametrize("N,D", ROW_SHAPES)
+def test_residual_gate_adaln(anima, ref, rng, N, D):
+    x, y = O.randn_bf16(rng, (N, D)), O.randn_bf16(rng, (N, D))
+    g, sc, sh = _modvec(rng, D), _modvec(rng, D), _modvec(rng, D)
+    dg, dsc, dsh, dy = dev(g), dev(sc), dev(sh), dev(y)
+    h, h_ref = dev(x), dev(x)
+    out, out_ref = empty_bf16((N, D)), empty_bf16((N, D))
+    anima.residual_gate_adaln(h, dy, dg, dsc, dsh, out, N, D, 1e-6)
+    ref.residual_gate_adaln_bf16(h_ref.data_ptr(), dy.data_ptr(), dg.data_ptr(), dsc.data_ptr(), dsh.data_ptr(),
+                                 out_ref.data_ptr(), N, D, 1e-6, stream_ptr())
+    torch.cuda.synchronize()
+    assert_bit_exact(host(h), host(h_ref), "residual_gate_adaln hidden vs reference")
+    assert_bit_exact(host(out), host(out_ref), "residual_gate_adaln normed vs reference")
+    if N * D <= ORACLE_MAX_ELEMS:
+        oh, on = O.residual_gate_adaln(x, y, g, sc, sh, N, D)
+        assert_bit_exact(host(h), oh, "residual_gate_adaln hidden vs oracle")
+        assert_one_ulp(host(out), on, "residual_gate_adaln normed vs oracle")
+
+
+@pytest.mark.parametrize("N,D", [(1, 2048), (65, 2048), (7, 128), (3, 96)])
+def test_adaln_rms_norm(anima, ref, rng, N, D):
+    x = O.randn_bf16(rng, (N, D))
+    sc, sh = O.randn_bf16(rng, (N, D), std=0.1), O.randn_bf16(rng, (N, D), std=0.1)
+    dx, dsc, dsh = dev(x), dev(sc), dev(sh)
+    out, out_ref = empty_bf16((N, D)), empty_bf16((N, D))
+    anima.adaln_rms_norm(dx, dsc, dsh, out, N, D, 1e-6)
+    ref.adaln_rms_norm_bf16(dx.data_ptr(), dsc.data_ptr(), dsh.data_ptr(), out_ref.data_ptr(), N, D, 1e-6,
+                            stream_ptr())
+    torch.cuda.synchronize()
+    assert_bit_exact(host(out), host(out_ref), "adaln_rms_norm vs reference")
+    assert_one_ulp(host(out), O.adaln_rms_norm(x, sc, sh, N, D), "adaln_rms_norm vs oracle")
+
+
+@pytest.mark.parametrize("N,D", [(4, 1024), (3, 2048), (5, 100)])
+def test_gemma_rms_norm(anima, ref, rng, N, D):
+    x, w = O.randn_bf16(rng, (N, D)), O.randn_bf16(rng, D, std=0.1)
+    dx, dw = dev(x), dev(w)
+    out, out_ref = empty_bf16((N, D)), empty_bf16((N, D))
+    anima.gemma_rms_norm(dx, dw, out, N, D, 1e-6)
+    ref.gemma_rms_norm_bf16(dx.data_ptr(), dw.data_ptr(), out_ref.data_ptr(), N, D, 1e-6, stream_ptr())
+    torch.cuda.synchronize()
+    assert_bit_exact(host(out), host(out_ref), "gemma_rms_norm vs reference")
+    assert_one_ulp(host(out), O.gemma_rms_norm(x, w, N, D), "gemma_rms_norm vs oracle")
+
+
+def test_row_norm_unaligned_subbuffer(anima, ref, rng):
+    """A row block starting one element into an allocation takes the generic path."""
+    N, D = 8, 2048
+    base = O.randn_bf16(rng, N * D + 8)
+    d = dev(base)
+    sc, sh = dev(_modvec(rng, D)), dev(_modvec(rng, D))
+    out, out_ref = empty_bf16(N * D + 8), empty_bf16(N * D + 8)
+    x_ptr, o_ptr, r_ptr = d.data_ptr() + 2, out.data_ptr() + 2, out_ref.data_ptr() + 2
+    from anima_b200 import call
+
+    call("anima_adaln_layernorm_bf16", x_ptr, sc.data_ptr(), sh.data_ptr(), o_ptr, N, D, 1e-6, stream_ptr())
+    ref.adaln_layernorm_bf16(x_ptr, sc.data_ptr(), sh.data_ptr(), r_ptr, N, D, 1e-6, stream_ptr())
+    torch.cuda.synchronize()
+    assert_bit_exact(host(out)[1:1 + N * D], host(out_ref)[1:1 + N * D], "unaligned adaln")
+
+
+# ---------------------------------------------------------------- elementwise
+FLAT_SIZES = [2, 8, 9, 1000, 4097, 8 * 8192 * 9 + 6, 1 << 20]
+
+
+@pytest.mark.parametrize("N", FLAT_SIZES)
+@pytest.mark.parametrize("op", ["gelu_tanh", "silu"])
+def test_unary(anima, ref, rng, N, op):
+    x = O.randn_bf16(rng, N, std=2.0)
+    dx = dev(x)
+    out, out_ref = dev(np.zeros(N, np.uint16)), dev(np.zeros(N, np.uint16))
+    getattr(anima, op)(dx, out, N)
+    getattr(ref, op + "_bf16")(dx.data_ptr(), out_ref.data_ptr(), N, stream_ptr())
+    xi = dev(x)
+    getattr(anima, op)(xi, xi, N)  # in place (vae.cpp:184, llm_adapter.cpp:301)
+    torch.cuda.synchronize()
+    assert_bit_exact(host(out), host(out_ref), f"{op} vs reference")
+    got_inplace = host(xi)
+    assert_bit_exact(got_inplace[: N // 2 * 2], host(out_ref)[: N // 2 * 2], f"{op} in place")
+    if N % 2:
+        assert got_inplace[-1] == x[-1], "odd last element must stay untouched, as in the reference"
+    if N <= ORACLE_MAX_ELEMS:
+        want = getattr(O, op)(x)
+        assert_one_ulp(host(out)[: N // 2 * 2], want[: N // 2 * 2], f"{op} vs oracle")
+
+
+@pytest.mark.parametrize("op", ["gelu_tanh", "silu"])
+def test_unary_extreme_inputs(anima, ref, op):
+    """Saturation, overflow of exp and tiny values go through the same arithmetic."""
+    v = np.array([0.0, -0.0, 1e-30, -1e-30, 3.0, -3.0, 8.0, -8.0, 20.0, -20.0, 88.0, -88.0, 100.0, -100.0,
+                  3.0e38, -3.0e38, np.inf, -np.inf], np.float32)
+    x = O.f32_to_bf16(np.concatenate([v, np.linspace(-12, 12, 4096, dtype=np.float32)]))
+    N = x.size
+    dx = dev(x)
+    out, out_ref = empty_bf16(N), empty_bf16(N)
+    getattr(anima, op)(dx, out, N)
+    getattr(ref, op + "_bf16")(dx.data_ptr(), out_ref.data_ptr(), N, stream_ptr())
+    torch.cuda.synchronize()
+    assert_bit_exact(host(out), host(out_ref), f"{op} extremes vs reference")
+
+
+@pytest.mark.parametrize("op", ["gelu_tanh_bias", "silu_bias"])
+@pytest.mark.parametrize("M,D", [(3, 6144), (1000, 8), (7, 10)])
+def test_unary_bias(anima, ref, rng, op, M, D):
+    x, b = O.randn_bf16(rng, (M, D)), O.randn_bf16(rng, D, std=0.5)
+    dx, db = dev(x), dev(b)
+    N = M * D
+    out, out_ref = empty_bf16(N), empty_bf16(N)
+    getattr(anima, op)(dx, db, out, N, D)
+    getattr(ref, op + "_bf16")(dx.data_ptr(), db.data_ptr(), out_ref.data_ptr(), N, D, stream_ptr())
+    torch.cuda.synchronize()
+    assert_bit_exact(host(out), host(out_ref), f"{op} vs reference")
+    base = op.replace("_bias", "")
+    assert_one_ulp(host(out), getattr(O, base)(x.reshape(-1), b, D), f"{op} vs oracle")
+
+
+@pytest.mark.parametrize("N", [2, 6144, 4097, 512 * 3072, 1 << 22])
+@pytest.mark.parametrize("op", ["add", "mul"])
+def test_binary(anima, ref, rng, N, op):
+    a, b = O.randn_bf16(rng, N), O.randn_bf16(rng, N)
+    da, db = dev(a), dev(b)
+    out, out_ref = empty_bf16(N), empty_bf16(N)
+    getattr(anima, op)(da, db, out, N)
+    getattr(ref, op + "_bf16")(da.data_ptr(), db.data_ptr(), out_ref.data_ptr(), N, stream_ptr())
+    ai = dev(a)
+    getattr(anima, op)(ai, db, ai, N)  # out == a (qwen3.cpp:249, transformer.cpp:408)
+    torch.cuda.synchronize()
+    assert_bit_exact(host(out)[: N // 2 * 2], host(out_ref)[: N // 2 * 2], f"{op} vs reference")
+    assert_bit_exact(host(ai)[: N // 2 * 2], host(out_ref)[: N // 2 * 2], f"{op} in place")
+    if N <= ORACLE_MAX_ELEMS:
+        assert_bit_exact(host(out)[: N // 2 * 2], getattr(O, op)(a, b)[: N // 2 * 2], f"{op} vs oracle")
+
+
+def test_binary_unaligned(anima, ref, rng):
+    N = 10001
+    a, b = O.randn_bf16(rng, N + 1), O.randn_bf16(rng, N + 1)
+    da, db = dev(a), dev(b)
+    out, out_ref = empty_bf16(N + 1), empty_bf16(N + 1)
+    from anima_b200 import call
+
+    call("anima_add_bf16", da.data_ptr() + 2, db.data_ptr(), out.data_ptr() + 2, N - 1, stream_ptr())
+    ref.add_bf16(da.data_ptr() + 2, db.data_ptr(), out_ref.data_ptr() + 2, N - 1, stream_ptr())
+    torch.cuda.synchronize()
+    assert_bit_exact(host(out)[1:N - 1], host(out_ref)[1:N - 1], "unaligned add")
+
+
+@pytest.mark.parametrize("N", [8, 512 * 3072, 4099])
+def test_swiglu_matches_reference_chain(anima, ref, rng, N):
+    g, u = O.randn_bf16(rng, N, std=2.0), O.randn_bf16(rng, N)
+    dg, du = dev(g), dev(u)
+    out = empty_bf16(N)
+    anima.swiglu(dg, du, out, N)
+    gr = dev(g)  # qwen3.cpp:248-250: silu in place, then mul into the gate buffer
+    ref.silu_bf16(gr.data_ptr(), gr.data_ptr(), N, stream_ptr())
+    ref.mul_bf16(gr.data_ptr(), du.data_ptr(), gr.data_ptr(), N, stream_ptr())
+    torch.cuda.synchronize()
+    assert_bit_exact(host(out)[: N // 2 * 2], host(gr)[: N // 2 * 2], "swiglu vs silu+mul")
+
+
+@pytest.mark.parametrize("N", [1, 9, 100003])
+def test_gated_gelu(anima, ref, rng, N):
+    g, u = O.randn_bf16(rng, N, std=2.0), O.randn_bf16(rng, N)
+    dg, du = dev(g), dev(u)
+    out, out_ref = empty_bf16(N), empty_bf16(N)
+    anima.gated_gelu(dg, du, out, N)
+    ref.gated_gelu_bf16(dg.data_ptr(), du.data_ptr(), out_ref.data_ptr(), N, stream_ptr())
+    torch.cuda.synchronize()
+    assert_bit_exact(host(out), host(out_ref), "gated_gelu vs reference")
+    assert_one_ulp(host(out), O.gated_gelu(g, u), "gated_gelu vs oracle")
+
+
+@pytest.mark.parametrize("M,D", [(1, 2048), (8192, 2048), (33, 96), (5, 10)])
+def test_scale_shift_bcast(anima, ref, rng, M, D):
+    x, sc, sh = O.randn_bf16(rng, (M, D)), _modvec(rng, D), _modvec(rng, D)
+    dx, dsc, dsh = dev(x), dev(sc), dev(sh)
+    out, out_ref = empty_bf16((M, D)), empty_bf16((M, D))
+    anima.scale_shift_bcast(dx, dsc, dsh, out, M, D)
+    ref.scale_shift_bcast_bf16(dx.data_ptr(), dsc.data_ptr(), dsh.data_ptr(), out_ref.data_ptr(), M, D, stream_ptr())
+    xi = dev(x)
+    anima.scale_shift_bcast(xi, dsc, dsh, xi, M, D)  # in place (transformer.cpp:564)
+    torch.cuda.synchronize()
+    assert_bit_exact(host(out), host(out_ref), "scale_shift_bcast vs reference")
+    assert_bit_exact(host(xi), host(out_ref), "scale_shift_bcast in place")
+    if M * D <= ORACLE_MAX_ELEMS:
+        assert_bit_exact(host(out), O.scale_shift_bcast(x, sc, sh, M, D), "scale_shift_bcast vs oracle")
+
+
+@pytest.mark.parametrize("M,D", [(1, 2048), (8192, 2048), (33, 96), (5, 10)])
+def test_residual_gate_bcast(anima, ref, rng, M, D):
+    x, y, g = O.randn_bf16(rng, (M, D)), O.randn_bf16(rng, (M, D)), _modvec(rng, D)
+    dx, dy, dg = dev(x), dev(y), dev(g)
+    out, out_ref = empty_bf16((M, D)), empty_bf16((M, D))
+    anima.residual_gate_bcast(dx, dy, dg, out, M, D)
+    ref.residual_gate_bcast_bf16(dx.data_ptr(), dy.data_ptr(), dg.data_ptr(), out_ref.data_ptr(), M, D, stream_ptr())
+    xi = dev(x)
+    anima.residual_gate_bcast(xi, dy, dg, xi, M, D)  # out == x (transformer.cpp:464)
+    torch.cuda.synchronize()
+    assert_bit_exact(host(out), host(out_ref), "residual_gate_bcast vs reference")
+    assert_bit_exact(host(xi), host(out_ref), "residual_gate_bcast in place")
+    if M * D <= ORACLE_MAX_ELEMS:
+        assert_bit_exact(host(out), O.residual_gate_bcast(x, y, g, M, D), "residual_gate_bcast vs oracle")
+
+
+# ---------------------------------------------------------------- RoPE
+@pytest.mark.parametrize("B,pe,H,HD", [(2, (1, 32, 32), 16, 128), (1, (1, 8, 8), 16, 128), (3, (1, 4, 6), 2, 64),
+                                       (2, (1, 3, 5), 3, 12)])
+def test_rope_cosmos_strided(anima, ref, rng, B, pe, H, HD):
+    S = pe[0] * pe[1] * pe[2]
+    cos_t, sin_t = O.cosmos_rope_tables(*pe, HD=HD)
+    x = O.randn_bf16(rng, (B * S, H * HD))
+    dc, ds = dev(cos_t), dev(sin_t)
+    a, r = dev(x), dev(x)
+    anima.rope_cosmos_strided(a, dc, ds, B, S, H, HD)
+    ref.rope_cosmos_strided_bf16(r.data_ptr(), dc.data_ptr(), ds.data_ptr(), B, S, H, HD, stream_ptr())
+    torch.cuda.synchronize()
+    assert_bit_exact(host(a), host(r), "rope_cosmos_strided vs reference")
+    assert_bit_exact(host(a), O.rope_cosmos_strided(x, cos_t, sin_t, B, S, H, HD), "rope_cosmos_strided vs oracle")
+
+
+@pytest.mark.parametrize("heads,T,HD,theta", [(16, 512, 128, 1e6), (8, 512, 128, 1e6), (16, 77, 64, 1e4),
+                                              (2, 5, 20, 1e4)])
+def test_rope_standard(anima, ref, rng, heads, T, HD, theta):
+    cos_t, sin_t = O.standard_rope_tables(T, HD, theta)
+    rows = heads * T
+    x = O.randn_bf16(rng, (rows, HD))
+    dc, ds = dev(cos_t), dev(sin_t)
+    a, r = dev(x), dev(x)
+    anima.rope_standard(a, dc, ds, rows, T, HD)
+    ref.rope_standard_bf16(r.data_ptr(), dc.data_ptr(), ds.data_ptr(), rows, T, HD, stream_ptr())
+    torch.cuda.synchronize()
+    assert_bit_exact(host(a), host(r), "rope_standard vs reference")
+    assert_one_ulp(host(a), O.rope_standard(x, cos_t, sin_t, rows, T, HD), "rope_standard vs oracle")
+
+
+@pytest.mark.parametrize("B,pe,H,HD", [(2, (1, 32, 32), 16, 128), (1, (1, 3, 5), 4, 128), (2, (1, 4, 4), 2, 64)])
+def test_qk_norm_rope_matches_reference_chain(anima, ref, rng, B, pe, H, HD):
+    S = pe[0] * pe[1] * pe[2]
+    cos_t, sin_t = O.cosmos_rope_tables(*pe, HD=HD)
+    x, w = O.randn_bf16(rng, (B * S, H * HD)), _weight(rng, HD)
+    dc, ds, dw = dev(cos_t), dev(sin_t), dev(w)
+    a, r = dev(x), dev(x)
+    anima.qk_norm_rope(a, dw, dc, ds, B, S, H, HD, 1e-6)
+    ref.rms_norm_bf16(r.data_ptr(), dw.data_ptr(), r.data_ptr(), B * S * H, HD, 1e-6, stream_ptr())
+    ref.rope_cosmos_strided_bf16(r.data_ptr(), dc.data_ptr(), ds.data_ptr(), B, S, H, HD, stream_ptr())
+    torch.cuda.synchronize()
+    assert_bit_exact(host(a), host(r), "qk_norm_rope vs rms_norm + rope_cosmos_strided")
+
+
+# ---------------------------------------------------------------- gather
+def test_embedding_lookup_qwen3(anima, ref, rng):
+    V, D, T = 151936, 1024, 512
+    table = O.randn_bf16(rng, (V, D), std=0.02)
+    ids = rng.integers(0, V, T, dtype=np.int32)
+    ids[:4] = [0, V - 1, 7, 7]
+    dt, di = dev(table), dev(ids)
+    out, out_ref = empty_bf16((T, D)), empty_bf16((T, D))
+    anima.embedding_lookup(dt, di, out, T, D, V)
+    ref.embedding_lookup_bf16(dt.data_ptr(), di.data_ptr(), out_ref.data_ptr(), T, D, stream_ptr())
+    torch.cuda.synchronize()
+    got = host(out)
+    assert_bit_exact(got, host(out_ref), "embedding_lookup vs reference")
+    assert np.array_equal(got, table[ids]), "embedding_lookup vs table[ids]"
+
+
+@pytest.mark.parametrize("D", [1024, 64, 6])
+def test_embedding_lookup_bad_ids(anima, rng, D):
+    V, T = 100, 9
+    table = O.randn_bf16(rng, (V, D))
+    ids = np.array([0, 99, 100, -1, 5, 2**31 - 1, -(2**31), 50, 100], np.int32)
+    dt, di = dev(table), dev(ids)
+    out = dev(np.full((T, D), 0x3F80, np.uint16))
+    bad = torch.zeros(1, dtype=torch.int32, device="cuda")
+    anima.embedding_lookup(dt, di, out, T, D, V, bad)
+    torch.cuda.synchronize()
+    got = host(out)
+    assert int(bad.item()) == 5
+    want = O.embedding_lookup(table, ids, T, D, V)
+    assert np.array_equal(got, want)
+
+
+# ---------------------------------------------------------------- VAE channel norm
+@pytest.mark.parametrize("B,C,H,W", [(1, 512, 32, 32), (2, 96, 16, 16), (1, 128, 8, 12), (1, 100, 5, 7),
+                                     (3, 16, 4, 4), (1, 1536, 8, 8)])
+def test_rms_norm_channel(anima, ref, rng, B, C, H, W):
+    sp = H * W
+    x, g = O.randn_bf16(rng, (B, C, sp)), _weight(rng, C)
+    dx, dg = dev(x), dev(g)
+    out, out_ref = empty_bf16((B, C, sp)), empty_bf16((B, C, sp))
+    anima.rms_norm_channel(dx, dg, out, B, C, sp, 1e-6)
+    ref.rms_norm_channel_bf16(dx.data_ptr(), dg.data_ptr(), out_ref.data_ptr(), B, C, sp, 1e-6, stream_ptr())
+    xi = dev(x)
+    anima.rms_norm_channel(xi, dg, xi, B, C, sp, 1e-6)  # in place (vae.cpp:148)
+    torch.cuda.synchronize()
+    assert_bit_exact(host(out), host(out_ref), "rms_norm_channel vs reference")
+    assert_bit_exact(host(xi), host(out_ref), "rms_norm_channel in place")
+    if x.size <= ORACLE_MAX_ELEMS:
+        assert_one_ulp(host(out), O.rms_norm_channel(x, g, B, C, sp), "rms_norm_channel vs oracle")
+
+
+@pytest.mark.parametrize("B,C,H,W", [(1, 512, 32, 32), (1, 96, 10, 10)])
+def test_rms_norm_channel_silu_matches_reference_chain(anima, ref, rng, B, C, H, W):
+    sp = H * W
+    x, g = O.randn_bf16(rng, (B, C, sp)), _weight(rng, C)
+    dx, dg = dev(x), dev(g)
+    out = empty_bf16((B, C, sp))
+    anima.rms_norm_channel_silu(dx, dg, out, B, C, sp, 1e-6)
+    r = dev(x)  # vae.cpp:148 then :184
+    ref.rms_norm_channel_bf16(r.data_ptr(), dg.data_ptr(), r.data_ptr(), B, C, sp, 1e-6, stream_ptr())
+    ref.silu_bf16(r.data_ptr(), r.data_ptr(), B * C * sp, stream_ptr())
+    torch.cuda.synchronize()
+    assert_bit_exact(host(out), host(r), "rms_norm_channel_silu vs rms_norm_channel + silu")
+
+
+# ---------------------------------------------------------------- fused LN + modulate
+@pytest.mark.parametrize("N,D", [(1024, 2048), (3, 96)])
+def test_layer_norm_modulate_matches_reference_chain(anima, ref, rng, N, D):
+    x, sc, sh = O.randn_bf16(rng, (N, D)), _modvec(rng, D), _modvec(rng, D)
+    dx, dsc, dsh = dev(x), dev(sc), dev(sh)
+    out = empty_bf16((N, D))
+    anima.layer_norm_modulate(dx, dsc, dsh, out, N, D, 1e-6)
+    r = dev(x)  # transformer.cpp:563-564, both in place
+    ref.layer_norm_bf16(r.data_ptr(), r.data_ptr(), N, D, 1e-6, stream_ptr())
+    ref.scale_shift_bcast_bf16(r.data_ptr(), dsc.data_ptr(), dsh.data_ptr(), r.data_ptr(), N, D, stream_ptr())
+    torch.cuda.synchronize()
+    assert_bit_exact(host(out), host(r), "layer_norm_modulate vs layer_norm + scale_shift_bcast")
+
+
+# ---------------------------------------------------------------- timestep embedding
+@pytest.mark.parametrize("dim", [256, 2048])
+def test_timestep_embedding(anima, ref, rng, dim):
+    w = _weight(rng, dim)
+    dw = dev(w)
+    ts = list(rng.uniform(0.0, 1.0, 12).astype(np.float32) * np.float32(1000.0)) + [0.0, 1.0, 999.0, 0.0313]
+    for t in ts:
+        sin_out, normed = empty_bf16(dim), empty_bf16(dim)
+        anima.timestep_embedding(float(t), dw, sin_out, normed, dim, 1e-6)
+        normed_ref = empty_bf16(dim)
+        ref.rms_norm_bf16(sin_out.data_ptr(), dw.data_ptr(), normed_ref.data_ptr(), 1, dim, 1e-6, stream_ptr())
+        torch.cuda.synchronize()
+        # the host loop of transformer.cpp:182-197, restated in oracle.c
+        assert_one_ulp(host(sin_out), O.timestep_sinusoid(t, dim), f"sinusoid t={t}")
+        assert_bit_exact(host(normed), host(normed_ref), f"timestep rms_norm t={t}")
