@@ -30,11 +30,12 @@ __device__ __forceinline__ void rot_bf16(float xr, float xi, float c, float s, f
     o_i = __fmaf_rn(xi, c, xr * s);
 }
 
-// gemma_ops.cu:81-85 with fp32 tables: x1*c - x2*s and x2*c + x1*s. nvcc contracts each
-// into one fma, folding the first product.
+// gemma_ops.cu:84-85 with fp32 tables: x1*c - x2*s and x2*c + x1*s. The reference build
+// contracts each into one fma: the first folds x1*c, the second folds x1*s (pinned
+// against the reference kernels' outputs on the GPU).
 __device__ __forceinline__ void rot_f32(float x1, float x2, float c, float s, float &o1, float &o2) {
     o1 = __fmaf_rn(x1, c, -(x2 * s));
-    o2 = __fmaf_rn(x2, c, x1 * s);
+    o2 = __fmaf_rn(x1, s, x2 * c);
 }
 
 struct CosmosArgs {

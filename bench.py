@@ -195,10 +195,8 @@ class Chain:
         self.ops.timestep(t, self.ts_w.data_ptr(), self.ts_sin.data_ptr(), self.ts_out.data_ptr(), CFG["ts_dim"],
                           self.eps, stream, host_buf=self.ts_host)
 
-    def block(self, i, stream, timers=None):
-        """One DiT block's chain; `timers` (op -> list of event pairs) times every launch."""
-        import torch
-
+    def block(self, i, stream, only=None):
+        """One DiT block's chain; `only` restricts it to one op type (for per-op timing)."""
         o, st = self.ops, stream
         bs = self.sets[i % NSETS]
         R, D, H, HD, B, S = self.R, self.D, self.H, self.HD, self.B, self.S
@@ -207,14 +205,8 @@ class Chain:
         P = lambda t: t.data_ptr()  # noqa: E731
 
         def run(name, fn, *args):
-            if timers is None:
+            if only is None or only == name:
                 fn(*args)
-                return
-            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            a.record()
-            fn(*args)
-            b.record()
-            timers.setdefault(name, []).append((a, b))
 
         for j in range(3):  # compute_adaln_zero's mod += temb (transformer.cpp:408)
             run("add", o.add, P(self.mod_raw[i, j]), P(self.temb), P(mod[j]), 3 * D, st)
@@ -236,14 +228,14 @@ class Chain:
         run("residual_gate_bcast", o.residual_gate_bcast, P(bs["hidden"]), P(bs["sub"]), gate3, P(bs["hidden"]), R,
             D, st)
 
-    def blocks(self, stream, timers=None):
+    def blocks(self, stream, only=None):
         for i in range(self.NB):
-            self.block(i, stream, timers)
+            self.block(i, stream, only)
 
 
 # ---------------------------------------------------------------- clocks
 class ClockSampler:
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+    FIELDS = ("timestamp,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
@@ -259,7 +251,15 @@ class ClockSampler:
         except OSError:
             self.proc = None
 
-    def stop(self):
+    def mark(self):
+        """Wall-clock bounds of the timed region (samples outside it are dropped)."""
+        import datetime
+
+        return datetime.datetime.now()
+
+    def stop(self, t0=None, t1=None):
+        import datetime
+
         if self.proc is None:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"], "samples": 0}
         self.proc.terminate()
@@ -273,6 +273,12 @@ class ClockSampler:
         for line in out.strip().splitlines():
             f = [x.strip() for x in line.split(",")]
             if len(f) < 9:
+                continue
+            try:
+                ts = datetime.datetime.strptime(f[0], "%Y/%m/%d %H:%M:%S.%f")
+            except ValueError:
+                ts = None
+            if t0 is not None and ts is not None and not (t0 <= ts <= t1):
                 continue
             try:
                 sm.append(float(f[1]))
@@ -316,15 +322,40 @@ def time_steps(chain, steps, stream_obj, graph, ts=True):
     return a.elapsed_time(b)
 
 
-def per_op_times(chain, steps, stream_obj):
-    """Eager pass with CUDA events around every launch: op -> (launches, mean ms)."""
+def capture(fn):
+    """CUDA graph of the launches `fn(stream_handle)` makes (on a side stream)."""
     import torch
 
-    timers = {}
-    for _ in range(steps):
-        chain.blocks(stream_obj.cuda_stream, timers)
-    torch.cuda.synchronize()
-    return {k: (len(v), statistics.mean(a.elapsed_time(b) for a, b in v)) for k, v in timers.items()}
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(side):
+        with torch.cuda.graph(g, stream=side):
+            fn(side.cuda_stream)
+    torch.cuda.current_stream().wait_stream(side)
+    return g
+
+
+def per_op_times(chain, ops, reps):
+    """Device time per launch of each op type: a CUDA graph holding only that op's launches
+    of one step (its real arguments, so it cycles the same >L2 buffer sets), replayed
+    `reps` times between CUDA events. Returns op -> mean ms per launch."""
+    import torch
+
+    out = {}
+    for name, per_step in ops.items():
+        g = capture(lambda s: chain.blocks(s, only=name))
+        g.replay()
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(reps):
+            g.replay()
+        b.record()
+        torch.cuda.synchronize()
+        out[name] = a.elapsed_time(b) / (reps * per_step)
+        del g
+    return out
 
 
 def headline_kernels(ops, device, peak, reps=50):
@@ -458,13 +489,7 @@ def main():
 
     graph = None
     if not args.eager:
-        side = torch.cuda.Stream()
-        side.wait_stream(stream)
-        with torch.cuda.stream(side):
-            graph = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(graph, stream=side):
-                chain.blocks(side.cuda_stream)
-        stream.wait_stream(side)
+        graph = capture(lambda s: chain.blocks(s))
         for _ in range(2):
             graph.replay()
         torch.cuda.synchronize()
@@ -476,23 +501,26 @@ def main():
         smi_id = str(local_rank)
     clocks = ClockSampler(smi_id)
     clocks.start()
+    time.sleep(0.3)  # let nvidia-smi start sampling
     if dist is not None:
         dist.barrier()
     torch.cuda.synchronize()
+    t_begin = clocks.mark()
     ms = time_steps(chain, args.steps, stream, graph)
+    t_end = clocks.mark()
     if dist is not None:
         t = torch.tensor([ms], device=device, dtype=torch.float64)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = float(t.item())
         dist.barrier()
-    clk = clocks.stop()
+    clk = clocks.stop(t_begin, t_end)
     ms_per_step = ms / args.steps
     value = n_gpus * total_bytes * args.steps / (ms * 1e-3) / 1e9
 
-    # per-op device times (eager, CUDA events around every launch) -> roofline
-    ops_t = per_op_times(chain, min(args.steps, 10), stream)
+    # per-op device times (graph replay of each op type alone) -> roofline
+    ops_t = per_op_times(chain, {k: v * CFG["blocks"] for k, v in lpb.items()}, max(3, min(args.steps, 20)))
     kernels = {}
-    for name, (n, mean_ms) in ops_t.items():
+    for name, mean_ms in ops_t.items():
         per_launch = per_block[name] / lpb[name]
         gbs = per_launch / (mean_ms * 1e-3) / 1e9
         kernels[name] = {"launches_per_step": lpb[name] * CFG["blocks"], "us": round(mean_ms * 1e3, 2),
@@ -544,8 +572,8 @@ def main():
                "note": "CPU restatement of the reference kernels (oracle/oracle.c, -O2, one thread); the "
                        "reference itself has no CPU implementation of these ops"}
 
-    if graph is not None:
-        del graph
+    used_graph = graph is not None
+    del graph  # release the captured graph before the process group goes away
     launches_per_step = CFG["blocks"] * chain.launches_per_block + 1
     line = {
         "metric": METRIC, "value": round(value, 1), "unit": "GB/s", "n_gpus": n_gpus, "steps": args.steps,
@@ -559,7 +587,7 @@ def main():
                    "algorithmic_bytes_per_step": total_bytes,
                    "l2": f"{NSETS} rotating activation sets, ~1.4 GB touched per step > 126 MB L2 (no flush)",
                    "timing": ("CUDA graph replay of the 28 blocks + eager timestep launch per step"
-                              if graph is not None else "eager launches"),
+                              if used_graph else "eager launches"),
                    "parallelism": f"replicas x{n_gpus} (rows independent; no collective on the data path)"},
         "e2e": {"value": round(n_gpus * total_bytes / (e2e_ms * 1e-3) / 1e9, 1), "unit": "GB/s",
                 "ms_per_step": round(e2e_ms, 4), "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},

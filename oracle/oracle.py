@@ -56,7 +56,7 @@ lib = _load()
 # own outputs (tests/golden): see oracle.h for what each mode means.
 VAR_MODE = 0          # var = fma(-mean, mean, sum_sq/D)
 RESID_SQ_MODE = 0     # sum_sq += fma(h0, h0, h1*h1)
-ROPE_STD_MODES = (0, 0)  # fma(x1, c, -(x2*s)), fma(x2, c, x1*s)
+ROPE_STD_MODES = (0, 1)  # fma(x1, c, -(x2*s)), fma(x1, s, x2*c)
 
 
 # ------------------------------------------------------------------ bf16 helpers

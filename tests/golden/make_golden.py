@@ -22,15 +22,60 @@ import oracle as O  # noqa: E402  (inputs, tables and bf16 helpers only)
 import refkernels  # noqa: E402
 
 
+_KEEP = []  # every device tensor stays alive until exit: a temporary's block could be
+            # handed to the next allocation before the kernel that reads it has run
+
+
 def dev(a):
     a = np.ascontiguousarray(a)
     if a.dtype == np.uint16:
         a = a.view(np.int16)
-    return torch.from_numpy(a).cuda()
+    t = torch.from_numpy(a).cuda()
+    _KEEP.append(t)
+    return t
 
 
 def host(t, dtype=np.uint16):
     return t.cpu().numpy().view(dtype)
+
+
+def craft_rope_standard_pin(rng):
+    """Inputs on which the nine ways of contracting x1*c - x2*s and x2*c + x1*s into fmas
+    give pairwise different bf16 outputs, so the reference's choice can be read off its
+    result. Each pair's exact result is placed next to a bf16 rounding midpoint (solving
+    for s), and only elements whose rounding depends on the contraction are kept: 400
+    for each pair of choices of either product. Layout: 64 rows x 128 (64 pairs), T = 64,
+    each row with its own table row."""
+    import itertools
+
+    def candidates(n, target):
+        x1 = O.bf16_to_f32(O.f32_to_bf16(rng.uniform(0.5, 1.0, n).astype(np.float32)))
+        x2 = O.bf16_to_f32(O.f32_to_bf16(rng.uniform(0.5, 1.0, n).astype(np.float32)))
+        c = rng.uniform(0.5, 1.0, n).astype(np.float32)
+        m = np.float64(0.5) + (rng.integers(0, 64, n) + 0.5) * 2.0 ** -8
+        if target == 0:
+            s = ((x1.astype(np.float64) * c - m) / x2).astype(np.float32)
+        else:
+            s = ((m - x2.astype(np.float64) * c) / x1).astype(np.float32)
+        return x1, x2, c, s
+
+    picked = []
+    for target in (0, 1):
+        x1, x2, c, s = candidates(1 << 20, target)
+        n = x1.size
+        x = np.stack([O.f32_to_bf16(x1), O.f32_to_bf16(x2)], 1)
+        outs = [O.rope_standard(x, c.reshape(n, 1), s.reshape(n, 1), n, n, 2,
+                                modes=(m, 0) if target == 0 else (0, m))[:, target] for m in range(3)]
+        for p, q in itertools.combinations(range(3), 2):
+            idx = np.nonzero(outs[p] != outs[q])[0][:400]
+            picked.append(np.stack([x1[idx], x2[idx], c[idx], s[idx]], 1))
+    P = np.concatenate(picked)
+    fill = np.stack(candidates(64 * 64 - len(P), 0), 1)
+    P = np.concatenate([P, fill])[rng.permutation(64 * 64)]
+    x = np.zeros((64, 128), np.uint16)
+    x[:, :64] = O.f32_to_bf16(P[:, 0]).reshape(64, 64)
+    x[:, 64:] = O.f32_to_bf16(P[:, 1]).reshape(64, 64)
+    return x, P[:, 2].reshape(64, 64).astype(np.float32), P[:, 3].reshape(64, 64).astype(np.float32)
 
 
 def main():
@@ -133,16 +178,22 @@ def main():
         ct, st = O.standard_rope_tables(T, HD, theta)
         x = O.randn_bf16(rng, (heads * T, HD))
         xd = dev(x)
-        R.rope_standard_bf16(xd.data_ptr(), torch.from_numpy(ct).cuda().data_ptr(),
-                             torch.from_numpy(st).cuda().data_ptr(), heads * T, T, HD, s)
+        R.rope_standard_bf16(xd.data_ptr(), dev(ct).data_ptr(),
+                             dev(st).data_ptr(), heads * T, T, HD, s)
         torch.cuda.synchronize()
         put(f"rope_standard_{HD}", x=x, cos=ct, sin=st, out=host(xd), shape=np.array([heads * T, T, HD], np.int32))
+
+    x, ct, st = craft_rope_standard_pin(rng)
+    xd = dev(x)
+    R.rope_standard_bf16(xd.data_ptr(), dev(ct).data_ptr(), dev(st).data_ptr(), 64, 64, 128, s)
+    torch.cuda.synchronize()
+    put("rope_standard_pin", x=x, cos=ct, sin=st, out=host(xd), shape=np.array([64, 64, 128], np.int32))
 
     # ---- gather and VAE channel norm (gemma_ops.cu, vae_kernels.cu)
     V, D, T = 1000, 64, 32
     table, ids = O.randn_bf16(rng, (V, D), std=0.02), rng.integers(0, V, T, dtype=np.int32)
     out = torch.empty((T, D), dtype=torch.int16, device="cuda")
-    R.embedding_lookup_bf16(dev(table).data_ptr(), torch.from_numpy(ids).cuda().data_ptr(), out.data_ptr(), T, D, s)
+    R.embedding_lookup_bf16(dev(table).data_ptr(), dev(ids).data_ptr(), out.data_ptr(), T, D, s)
     torch.cuda.synchronize()
     put("embedding_lookup", table=table, ids=ids, out=host(out))
     for B, C, sp in [(1, 96, 64), (2, 32, 40)]:

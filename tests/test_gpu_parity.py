@@ -130,19 +130,33 @@ def test_gemma_rms_norm(anima, ref, rng, N, D):
 
 
 def test_row_norm_unaligned_subbuffer(anima, ref, rng):
-    """A row block starting one element into an allocation takes the generic path."""
+    """Row blocks that start 2 or 4 bytes into an allocation take the generic path.
+
+    The reference kernels load bf16 pairs (4-byte accesses, layer_norm.cu:99), so they
+    are only ever given 4-byte-aligned pointers here; the 2-byte offset is checked
+    against the CPU restatement alone.
+    """
     N, D = 8, 2048
     base = O.randn_bf16(rng, N * D + 8)
     d = dev(base)
-    sc, sh = dev(_modvec(rng, D)), dev(_modvec(rng, D))
-    out, out_ref = empty_bf16(N * D + 8), empty_bf16(N * D + 8)
-    x_ptr, o_ptr, r_ptr = d.data_ptr() + 2, out.data_ptr() + 2, out_ref.data_ptr() + 2
+    scv, shv = _modvec(rng, D), _modvec(rng, D)
+    sc, sh = dev(scv), dev(shv)
     from anima_b200 import call
 
-    call("anima_adaln_layernorm_bf16", x_ptr, sc.data_ptr(), sh.data_ptr(), o_ptr, N, D, 1e-6, stream_ptr())
-    ref.adaln_layernorm_bf16(x_ptr, sc.data_ptr(), sh.data_ptr(), r_ptr, N, D, 1e-6, stream_ptr())
-    torch.cuda.synchronize()
-    assert_bit_exact(host(out)[1:1 + N * D], host(out_ref)[1:1 + N * D], "unaligned adaln")
+    for off in (2, 4):  # bytes
+        e = off // 2
+        out, out_ref = empty_bf16(N * D + 8), empty_bf16(N * D + 8)
+        call("anima_adaln_layernorm_bf16", d.data_ptr() + off, sc.data_ptr(), sh.data_ptr(), out.data_ptr() + off, N,
+             D, 1e-6, stream_ptr())
+        if off % 4 == 0:
+            ref.adaln_layernorm_bf16(d.data_ptr() + off, sc.data_ptr(), sh.data_ptr(), out_ref.data_ptr() + off, N, D,
+                                     1e-6, stream_ptr())
+        torch.cuda.synchronize()
+        got = host(out)[e:e + N * D]
+        if off % 4 == 0:
+            assert_bit_exact(got, host(out_ref)[e:e + N * D], f"adaln at +{off} B vs reference")
+        want = O.adaln_layernorm(np.ascontiguousarray(base[e:e + N * D]), scv, shv, N, D)
+        assert_one_ulp(got, want, f"adaln at +{off} B vs oracle")
 
 
 # ---------------------------------------------------------------- elementwise
@@ -218,16 +232,26 @@ def test_binary(anima, ref, rng, N, op):
 
 
 def test_binary_unaligned(anima, ref, rng):
+    """Unaligned sub-buffers take the scalar path. The reference's bf16-pair loads need
+    4-byte alignment (elementwise.cu:45-49), so it only sees the 4-byte offset."""
     N = 10001
-    a, b = O.randn_bf16(rng, N + 1), O.randn_bf16(rng, N + 1)
+    a, b = O.randn_bf16(rng, N + 2), O.randn_bf16(rng, N + 2)
     da, db = dev(a), dev(b)
-    out, out_ref = empty_bf16(N + 1), empty_bf16(N + 1)
     from anima_b200 import call
 
-    call("anima_add_bf16", da.data_ptr() + 2, db.data_ptr(), out.data_ptr() + 2, N - 1, stream_ptr())
-    ref.add_bf16(da.data_ptr() + 2, db.data_ptr(), out_ref.data_ptr() + 2, N - 1, stream_ptr())
-    torch.cuda.synchronize()
-    assert_bit_exact(host(out)[1:N - 1], host(out_ref)[1:N - 1], "unaligned add")
+    for off in (2, 4):
+        e = off // 2
+        out, out_ref = empty_bf16(N + 2), empty_bf16(N + 2)
+        call("anima_add_bf16", da.data_ptr() + off, db.data_ptr(), out.data_ptr() + off, N - 1, stream_ptr())
+        if off % 4 == 0:
+            ref.add_bf16(da.data_ptr() + off, db.data_ptr(), out_ref.data_ptr() + off, N - 1, stream_ptr())
+        torch.cuda.synchronize()
+        n = (N - 1) // 2 * 2
+        got = host(out)[e:e + n]
+        if off % 4 == 0:
+            assert_bit_exact(got, host(out_ref)[e:e + n], f"add at +{off} B vs reference")
+        assert_bit_exact(got, O.add(np.ascontiguousarray(a[e:e + n]), np.ascontiguousarray(b[:n])),
+                         f"add at +{off} B vs oracle")
 
 
 @pytest.mark.parametrize("N", [8, 512 * 3072, 4099])
