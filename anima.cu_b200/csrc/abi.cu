@@ -1,5 +1,7 @@
 // abi.cu -- library-wide host helpers of the C ABI: device properties, status strings.
 #include <atomic>
+#include <mutex>
+#include <vector>
 
 #include "common.cuh"
 
@@ -37,6 +39,43 @@ int allow_dynamic_smem(const void *kernel, int bytes, int slot) {
     if (e != cudaSuccess) return (int)e;
     if (dev < kMaxDevices) g_smem_slots[dev].fetch_or(bit, std::memory_order_acq_rel);
     return ANIMA_OK;
+}
+
+namespace {
+struct OccEntry {
+    int dev;
+    const void *kernel;
+    int block, smem, ctas;
+};
+std::mutex g_occ_mu;
+std::vector<OccEntry> g_occ;
+}  // namespace
+
+int resident_ctas(const void *kernel, int block, int smem, int *err) {
+    *err = ANIMA_OK;
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) {
+        cudaGetLastError();
+        *err = ANIMA_ERR_NO_DEVICE;
+        return 0;
+    }
+    {
+        std::lock_guard<std::mutex> lock(g_occ_mu);
+        for (const OccEntry &e : g_occ)
+            if (e.dev == dev && e.kernel == kernel && e.block == block && e.smem == smem) return e.ctas;
+    }
+    cudaError_t e = cudaSuccess;
+    if (smem > 48 * 1024) e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    int n = 0;
+    if (e == cudaSuccess) e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kernel, block, (size_t)smem);
+    if (e != cudaSuccess || n <= 0) {
+        cudaGetLastError();
+        *err = e != cudaSuccess ? (int)e : (int)cudaErrorInvalidConfiguration;
+        return 0;
+    }
+    std::lock_guard<std::mutex> lock(g_occ_mu);
+    g_occ.push_back(OccEntry{dev, kernel, block, smem, n});
+    return n;
 }
 
 }  // namespace anima

@@ -194,6 +194,12 @@ int sm_count();
 // per (device, slot); `slot` names the kernel (0..15). Returns ANIMA_OK or a cudaError_t.
 int allow_dynamic_smem(const void *kernel, int bytes, int slot);
 
+// Resident CTAs per SM of `kernel` launched with `block` threads and `smem` bytes of
+// dynamic shared memory on the current device, raising the kernel's dynamic shared-memory
+// limit first when smem > 48 KB. Cached per (device, kernel, smem). On failure returns 0
+// and stores the status in *err.
+int resident_ctas(const void *kernel, int block, int smem, int *err);
+
 inline bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 inline bool aligned_to(const void *p, unsigned a) {
     return (reinterpret_cast<uintptr_t>(p) & (a - 1)) == 0;

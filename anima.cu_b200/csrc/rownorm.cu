@@ -1,17 +1,14 @@
 // rownorm.cu -- LayerNorm / adaLN / residual-gate adaLN / RMSNorm row kernels (sm_100a).
 //
-// Fast path (D a multiple of 64, D <= 2048, 16-byte aligned rows): a row belongs to a
-// team of LPR lanes, each lane streams K 16-byte chunks of it into registers with
-// L1-bypassing vector loads, so the row crosses HBM exactly once (read once, written
-// once), with no shared memory and no __syncthreads. The statistics go through
-// ref_pair_tree_sum, which reproduces the reference CTA's addition order, and the
-// per-element epilogue uses the reference's expressions, so outputs match the
-// reference kernels bit for bit.
-//
-//   D      LPR  K  rows/warp       D      LPR  K  rows/warp
-//   64      8   1      4           512     8   8      4
-//   128     8   2      4           1024   16   8      2
-//   256     8   4      4           2048   32   8      1
+// Fast path (D a multiple of 64, D <= 2048, 16-byte aligned rows): the "segment"
+// kernels below. Each lane owns one 64-element segment of a row -- the 32 pairs that
+// one warp of the reference's row CTA reduces -- so the reference's addition tree is
+// replayed exactly: its warp-level shfl_down tree as 31 in-register adds, its cross-warp
+// level as lane XORs inside the row's team. Rows stream through a per-warp ring of
+// shared-memory slots filled ahead by cp.async, and results leave through the same slot
+// with coalesced 16-byte stores: every row is read from HBM once and written once (the
+// reference reads it twice and runs three __syncthreads per reduction on a 1024-thread
+// CTA per row). Outputs match the reference kernels bit for bit.
 //
 // Generic path (any even D, any 2-byte alignment): one CTA per row with the reference's
 // own thread layout and scalar accesses. Same bits, reference-like speed.
@@ -33,272 +30,435 @@ __device__ __forceinline__ float ln_var(float sq, float mean, int D) {
 // product into an fma with the second.
 __device__ __forceinline__ float resid_sq_pair(float h0, float h1) { return fmaf(h0, h0, h1 * h1); }
 
-// ---------------------------------------------------------------- row ops
-// Each op loads its row chunks (first phase), produces per-pair sum / sum-of-squares
-// values, and writes the outputs from the reduced statistics (second phase).
+// ------------------------------------------------ segment kernels (fast path)
+//
+// A row of D elements (D % 64 == 0, D <= 2048) is NW = D/64 "segments" of 64 elements:
+// exactly the 32 pairs one reference warp reduces (thread t owns pair t, so warp w owns
+// elements 64w..64w+63). Each lane owns one segment, so the reference's warp-level
+// shfl_down tree becomes 31 in-register adds in the same order, and its cross-warp
+// level is log2(NW) lane XORs inside the row's team of NW lanes. A warp therefore
+// handles a 4 KB "unit" of G = 32/NW consecutive rows per input.
+//
+// Data movement: persistent CTAs of 4 warps; each warp owns a ring of NST unit slots in
+// shared memory. Units are copied in NST ahead with 16-byte cp.async (coalesced: lane l
+// copies chunks l, l+32, ...), read back per segment, the outputs are written into the
+// same slot and stored to global memory coalesced again. Slots are XOR-swizzled at
+// 16-byte granularity inside each 128-byte group so that both patterns are free of bank
+// conflicts. Broadcast vectors (1+scale, shift, gate, weight) are converted to fp32 once
+// per CTA into shared memory (swizzled per segment the same way).
 
-struct LayerNormOp {  // layer_norm.cu:26-59
-    const anima_bf16 *x;
-    anima_bf16 *out;
-    int D;
-    float eps;
+constexpr int kSegWarps = 4;
+constexpr int kSegThreads = kSegWarps * 32;
+constexpr int kUnitChunks = 256;  // 16-byte chunks per input per unit (4 KB)
+
+__device__ __forceinline__ int swz(int c) { return (c & ~7) | ((c & 7) ^ ((c >> 3) & 7)); }
+
+// fp32 broadcast vector layout: float4 j (0..15) of segment s lives at 16s + (j ^ (s&7)).
+__device__ __forceinline__ int bc_pos(int d) {
+    const int s = d >> 6, j = (d >> 2) & 15;
+    return ((s << 4) + (j ^ (s & 7))) * 4 + (d & 3);
+}
+
+template <int NIN>
+struct SegShape {
+    static constexpr int kStages = NIN == 1 ? 3 : 2;
+    static constexpr int kRingBytes = kSegWarps * kStages * NIN * kUnitChunks * 16;
 };
 
-struct AdaLNOp {  // layer_norm.cu:83-125
-    const anima_bf16 *x, *scale, *shift;
-    anima_bf16 *out;
-    int D;
-    float eps;
-};
+__device__ __forceinline__ void cp_async16(void *smem, const void *gmem) {
+    const unsigned a = (unsigned)__cvta_generic_to_shared(smem);
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(a), "l"(gmem) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
 
-struct LnModulateOp {  // layer_norm.cu:26-59 then elementwise.cu:216-236
-    const anima_bf16 *x, *scale, *shift;
-    anima_bf16 *out;
-    int D;
-    float eps;
-};
-
-struct RmsOp {  // rms_norm.cu:9-67
-    const anima_bf16 *x, *weight;  // weight nullable
-    anima_bf16 *out;
-    int D;
-    float eps;
-};
-
-struct AdaRmsOp {  // adaln.cu:11-58 (per-row scale/shift)
-    const anima_bf16 *x, *scale, *shift;
-    anima_bf16 *out;
-    int D;
-    float eps;
-};
-
-// --------------------------------------------------- team (fast path) kernels
-
-template <int LPR, int K>
-struct TeamRow {
-    int64_t row;
-    int l;     // lane index inside the team
-    bool live; // row < N; dead lanes still join every shuffle
-    __device__ __forceinline__ int64_t chunk_off(int k) const {
-        return (int64_t)(l + LPR * k) * 8;
-    }
-};
-
-// Loads the K chunks of `base + row*D` (zeros for dead lanes).
-template <int LPR, int K>
-__device__ __forceinline__ void load_row(const TeamRow<LPR, K> &t, const anima_bf16 *base, int D,
-                                         Vec8 (&v)[K]) {
-    const anima_bf16 *r = base + t.row * (int64_t)D;
+// The reference warp's shfl_down tree over the 32 pairs of one segment, in registers.
+// p(k, j) is pair 4k+j (chunk k, pair j of the chunk).
+template <class PairFn>
+__device__ __forceinline__ float seg_tree(PairFn p) {
+    float a[16];
 #pragma unroll
-    for (int k = 0; k < K; ++k) {
-        if (t.live) v[k] = ld_stream(r + t.chunk_off(k));
-        else v[k] = Vec8{{0u, 0u, 0u, 0u}};
+    for (int k = 0; k < 4; ++k)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) a[4 * k + j] = p(k, j) + p(k + 4, j);  // offset 16
+    float b[8], c[4];
+#pragma unroll
+    for (int r = 0; r < 8; ++r) b[r] = a[r] + a[r + 8];                  // offset 8
+#pragma unroll
+    for (int r = 0; r < 4; ++r) c[r] = b[r] + b[r + 4];                  // offset 4
+    const float d0 = c[0] + c[2], d1 = c[1] + c[3];                      // offset 2
+    return d0 + d1;                                                      // offset 1
+}
+
+// The reference's second level: warp 0 reduces the NW per-warp sums, zero-padded to 32.
+// Segment s sits in lane s of the row's team, so reference offset o is lane XOR o.
+template <int NW>
+__device__ __forceinline__ float seg_cross(float v) {
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1)
+        if (off < NW) v = v + __shfl_xor_sync(0xffffffffu, v, off);
+    return v;
+}
+
+// Sum and sum of squares of a plain bf16 segment (pair values: v0+v1, round(v0^2+v1^2)).
+__device__ __forceinline__ void seg_stats(const Vec8 (&v)[8], float &sum, float &sq) {
+    sum = seg_tree([&](int k, int j) { return bf_lo(v[k].w[j]) + bf_hi(v[k].w[j]); });
+    sq = seg_tree([&](int k, int j) {
+        const float a = bf_lo(v[k].w[j]), b = bf_hi(v[k].w[j]);
+        return fmaf(b, b, a * a);
+    });
+}
+
+__device__ __forceinline__ void load_seg(const Vec8 *buf, int lane, Vec8 (&v)[8]) {
+#pragma unroll
+    for (int k = 0; k < 8; ++k) v[k] = buf[swz(8 * lane + k)];
+}
+
+__device__ __forceinline__ void bc8(const float *bc, int seg, int k, float (&f)[8]) {
+    const float4 *q = reinterpret_cast<const float4 *>(bc) + (seg << 4);
+    const float4 a = q[(2 * k) ^ (seg & 7)], b = q[(2 * k + 1) ^ (seg & 7)];
+    f[0] = a.x; f[1] = a.y; f[2] = a.z; f[3] = a.w;
+    f[4] = b.x; f[5] = b.y; f[6] = b.z; f[7] = b.w;
+}
+
+// Packed fp32x2 arithmetic (sm_100 FFMA2/FADD2/FMUL2): two lanes of IEEE round-to-nearest
+// per instruction, so results equal the scalar ops bit for bit at half the issue cost.
+__device__ __forceinline__ float2 f2(float a, float b) { return make_float2(a, b); }
+
+// out[e] = fma((x[e] - mean) * inv, mul[e], add[e]) for e < 8, optionally rounding the
+// normalised value to bf16 first.
+template <bool kRoundFirst>
+__device__ __forceinline__ void ln_modulate8(const float (&x)[8], float mean, float inv, const float (&mul)[8],
+                                             const float (&add)[8], float (&out)[8]) {
+    const float2 nm = f2(-mean, -mean), iv = f2(inv, inv);
+#pragma unroll
+    for (int e = 0; e < 8; e += 2) {
+        float2 n = __fmul2_rn(__fadd2_rn(f2(x[e], x[e + 1]), nm), iv);
+        if constexpr (kRoundFirst) n = f2(bf16_round(n.x), bf16_round(n.y));
+        const float2 o = __ffma2_rn(n, f2(mul[e], mul[e + 1]), f2(add[e], add[e + 1]));
+        out[e] = o.x;
+        out[e + 1] = o.y;
     }
 }
 
-// Per-pair statistics of plain bf16 data: s = v0 + v1, q = round(v0^2 + v1^2). The bf16
-// squares are exact in fp32, so this is the same value whichever order the reference's
-// kernels accumulate the pair in (layer_norm.cu:44-46, :103-104; rms_norm.cu:35-36).
-template <int K>
-__device__ __forceinline__ void pair_stats(const Vec8 (&v)[K], float (&s)[K][4], float (&q)[K][4]) {
+__device__ __forceinline__ float bf(const anima_bf16 *p, int i) {
+    return __bfloat162float(reinterpret_cast<const __nv_bfloat16 *>(p)[i]);
+}
+
+// ---- ops: NIN streamed inputs, NOUT outputs (written over input buffers 0..NOUT-1),
+// NB fp32 broadcast vectors.
+
+struct LayerNormOp {  // layer_norm.cu:26-59
+    static constexpr int NIN = 1, NOUT = 1, NB = 0;
+    const anima_bf16 *x;
+    anima_bf16 *out;
+    float eps;
+    __device__ const anima_bf16 *src(int) const { return x; }
+    __device__ anima_bf16 *dst(int) const { return out; }
+    __device__ void load_bcast(float *, int, int) const {}
+    template <int NW>
+    __device__ void segment(Vec8 *slot, const float *, int lane, int, int D) const {
+        Vec8 v[8];
+        load_seg(slot, lane, v);
+        float sum, sq;
+        seg_stats(v, sum, sq);
+        sum = seg_cross<NW>(sum);
+        sq = seg_cross<NW>(sq);
+        const float mean = __fdiv_rn(sum, (float)D);
+        const float inv = rsqrtf(ln_var(sq, mean, D) + eps);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+            float f[8];
+            unpack8(v[k], f);
+            const float2 nm = f2(-mean, -mean), iv = f2(inv, inv);
+#pragma unroll
+            for (int e = 0; e < 8; e += 2) {
+                const float2 n = __fmul2_rn(__fadd2_rn(f2(f[e], f[e + 1]), nm), iv);
+                f[e] = n.x;
+                f[e + 1] = n.y;
+            }
+            slot[swz(8 * lane + k)] = pack8(f);
+        }
+    }
+};
+
+template <bool kRoundFirst>  // false: adaLN (layer_norm.cu:83-125); true: LN -> bf16 -> modulate
+struct AdaLNOp {
+    static constexpr int NIN = 1, NOUT = 1, NB = 2;
+    const anima_bf16 *x, *scale, *shift;
+    anima_bf16 *out;
+    float eps;
+    __device__ const anima_bf16 *src(int) const { return x; }
+    __device__ anima_bf16 *dst(int) const { return out; }
+    __device__ void load_bcast(float *bc, int d, int D) const {
+        bc[bc_pos(d)] = 1.0f + bf(scale, d);  // the reference's (1.0f + s) is exact to fp32 rounding
+        bc[D + bc_pos(d)] = bf(shift, d);
+    }
+    template <int NW>
+    __device__ void segment(Vec8 *slot, const float *bc, int lane, int seg, int D) const {
+        Vec8 v[8];
+        load_seg(slot, lane, v);
+        float sum, sq;
+        seg_stats(v, sum, sq);
+        sum = seg_cross<NW>(sum);
+        sq = seg_cross<NW>(sq);
+        const float mean = __fdiv_rn(sum, (float)D);
+        const float inv = rsqrtf(ln_var(sq, mean, D) + eps);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+            float f[8], sc[8], sh[8];
+            unpack8(v[k], f);
+            bc8(bc, seg, k, sc);
+            bc8(bc + D, seg, k, sh);
+            ln_modulate8<kRoundFirst>(f, mean, inv, sc, sh, f);
+            slot[swz(8 * lane + k)] = pack8(f);
+        }
+    }
+};
+
+struct ResGateAdaLNOp {  // layer_norm.cu:146-196
+    static constexpr int NIN = 2, NOUT = 2, NB = 3;
+    anima_bf16 *hidden;
+    const anima_bf16 *sub_out, *gate, *scale, *shift;
+    anima_bf16 *normed;
+    float eps;
+    __device__ const anima_bf16 *src(int i) const { return i == 0 ? hidden : sub_out; }
+    __device__ anima_bf16 *dst(int o) const { return o == 0 ? hidden : normed; }
+    __device__ void load_bcast(float *bc, int d, int D) const {
+        bc[bc_pos(d)] = bf(gate, d);
+        bc[D + bc_pos(d)] = 1.0f + bf(scale, d);
+        bc[2 * D + bc_pos(d)] = bf(shift, d);
+    }
+    template <int NW>
+    __device__ void segment(Vec8 *slot, const float *bc, int lane, int seg, int D) const {
+        Vec8 x[8], y[8];
+        load_seg(slot, lane, x);
+        load_seg(slot + kUnitChunks, lane, y);
+        // h = x + y*gate in fp32 (the bf16 product is exact, so fma rounds like the
+        // reference); the statistics use the unrounded h, the output the bf16 h.
+        float h[8][8];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+            float g[8], fx[8], fy[8];
+            bc8(bc, seg, k, g);
+            unpack8(x[k], fx);
+            unpack8(y[k], fy);
+#pragma unroll
+            for (int e = 0; e < 8; e += 2) {
+                const float2 hv = __ffma2_rn(f2(fy[e], fy[e + 1]), f2(g[e], g[e + 1]), f2(fx[e], fx[e + 1]));
+                h[k][e] = hv.x;
+                h[k][e + 1] = hv.y;
+            }
+        }
+        float sum = seg_tree([&](int k, int j) { return h[k][2 * j] + h[k][2 * j + 1]; });
+        float sq = seg_tree([&](int k, int j) { return resid_sq_pair(h[k][2 * j], h[k][2 * j + 1]); });
+        sum = seg_cross<NW>(sum);
+        sq = seg_cross<NW>(sq);
+        const float mean = __fdiv_rn(sum, (float)D);
+        const float inv = rsqrtf(ln_var(sq, mean, D) + eps);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+            const Vec8 hb = pack8(h[k]);
+            float f[8], sc[8], sh[8];
+            unpack8(hb, f);
+            bc8(bc + D, seg, k, sc);
+            bc8(bc + 2 * D, seg, k, sh);
+            ln_modulate8<false>(f, mean, inv, sc, sh, f);
+            slot[swz(8 * lane + k)] = hb;
+            slot[kUnitChunks + swz(8 * lane + k)] = pack8(f);
+        }
+    }
+};
+
+template <bool kWeight>
+struct RmsOp {  // rms_norm.cu:9-67
+    static constexpr int NIN = 1, NOUT = 1, NB = kWeight ? 1 : 0;
+    const anima_bf16 *x, *weight;
+    anima_bf16 *out;
+    float eps;
+    __device__ const anima_bf16 *src(int) const { return x; }
+    __device__ anima_bf16 *dst(int) const { return out; }
+    __device__ void load_bcast(float *bc, int d, int) const {
+        if constexpr (kWeight) bc[bc_pos(d)] = bf(weight, d);
+    }
+    template <int NW>
+    __device__ void segment(Vec8 *slot, const float *bc, int lane, int seg, int D) const {
+        Vec8 v[8];
+        load_seg(slot, lane, v);
+        float sq = seg_tree([&](int k, int j) {
+            const float a = bf_lo(v[k].w[j]), b = bf_hi(v[k].w[j]);
+            return fmaf(b, b, a * a);
+        });
+        sq = seg_cross<NW>(sq);
+        const float r = rsqrtf(__fdiv_rn(sq, (float)D) + eps);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+            float f[8];
+            unpack8(v[k], f);
+            if constexpr (kWeight) {
+                float w[8];
+                bc8(bc, seg, k, w);
+#pragma unroll
+                for (int e = 0; e < 8; e += 2) {
+                    const float2 o = __fmul2_rn(__fmul2_rn(f2(f[e], f[e + 1]), f2(r, r)), f2(w[e], w[e + 1]));
+                    f[e] = o.x;
+                    f[e + 1] = o.y;
+                }
+            } else {
+#pragma unroll
+                for (int e = 0; e < 8; ++e) f[e] = f[e] * r;
+            }
+            slot[swz(8 * lane + k)] = pack8(f);
+        }
+    }
+};
+
+struct AdaRmsOp {  // adaln.cu:11-58 (per-row scale/shift streamed alongside x)
+    static constexpr int NIN = 3, NOUT = 1, NB = 0;
+    const anima_bf16 *x, *scale, *shift;
+    anima_bf16 *out;
+    float eps;
+    __device__ const anima_bf16 *src(int i) const { return i == 0 ? x : (i == 1 ? scale : shift); }
+    __device__ anima_bf16 *dst(int) const { return out; }
+    __device__ void load_bcast(float *, int, int) const {}
+    template <int NW>
+    __device__ void segment(Vec8 *slot, const float *, int lane, int, int D) const {
+        Vec8 v[8];
+        load_seg(slot, lane, v);
+        float sq = seg_tree([&](int k, int j) {
+            const float a = bf_lo(v[k].w[j]), b = bf_hi(v[k].w[j]);
+            return fmaf(b, b, a * a);
+        });
+        sq = seg_cross<NW>(sq);
+        const float r = rsqrtf(__fdiv_rn(sq, (float)D) + eps);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+            float f[8], sc[8], sh[8];
+            unpack8(v[k], f);
+            unpack8(slot[kUnitChunks + swz(8 * lane + k)], sc);
+            unpack8(slot[2 * kUnitChunks + swz(8 * lane + k)], sh);
+#pragma unroll
+            for (int e = 0; e < 8; ++e) f[e] = fmaf(f[e] * r, 1.0f + sc[e], sh[e]);
+            slot[swz(8 * lane + k)] = pack8(f);
+        }
+    }
+};
+
+template <int NW, class Op>
+__global__ void __launch_bounds__(kSegThreads) row_seg(Op op, int64_t N, int D) {
+    constexpr int NIN = Op::NIN, NOUT = Op::NOUT, NB = Op::NB;
+    constexpr int G = 32 / NW;  // rows per unit
+    constexpr int NST = SegShape<NIN>::kStages;
+    constexpr int kRowChunks = NW * 8;
+    extern __shared__ __align__(16) unsigned char seg_smem[];
+    float *bc = reinterpret_cast<float *>(seg_smem);
+    Vec8 *ring = reinterpret_cast<Vec8 *>(seg_smem + (size_t)NB * D * 4) +
+                 (size_t)(threadIdx.x >> 5) * NST * NIN * kUnitChunks;
+    const int lane = threadIdx.x & 31;
+    if constexpr (NB > 0) {
+        for (int d = threadIdx.x; d < D; d += kSegThreads) op.load_bcast(bc, d, D);
+        __syncthreads();
+    }
+    const int64_t units = (N + G - 1) / G;
+    const int64_t nwarps = (int64_t)gridDim.x * kSegWarps;
+    const int64_t first = (int64_t)blockIdx.x * kSegWarps + (threadIdx.x >> 5);
+    auto unit_chunks = [&](int64_t u) {
+        const int64_t left = N - u * G;
+        return left >= G ? kUnitChunks : (int)left * kRowChunks;
+    };
+    auto issue = [&](int64_t u, int st) {
+        if (u < units) {
+            const int nch = unit_chunks(u);
+#pragma unroll
+            for (int in = 0; in < NIN; ++in) {
+                const anima_bf16 *src = op.src(in) + u * G * (int64_t)D;
+                Vec8 *buf = ring + (st * NIN + in) * kUnitChunks;
+#pragma unroll
+                for (int k = 0; k < 8; ++k) {
+                    const int c = lane + 32 * k;
+                    if (c < nch) cp_async16(buf + swz(c), src + (int64_t)c * 8);
+                }
+            }
+        }
+        cp_async_commit();  // one group per unit, empty or not, keeps the counting uniform
+    };
+#pragma unroll
+    for (int st = 0; st < NST; ++st) issue(first + st * nwarps, st);
+    int st = 0;
+    for (int64_t u = first; u < units; u += nwarps) {
+        cp_async_wait<NST - 1>();  // this lane's copies of unit u have landed ...
+        __syncwarp();              // ... and so have every other lane's
+        Vec8 *slot = ring + st * NIN * kUnitChunks;
+        op.template segment<NW>(slot, bc, lane, lane % NW, D);
+        __syncwarp();
+        const int nch = unit_chunks(u);
+#pragma unroll
+        for (int o = 0; o < NOUT; ++o) {
+            anima_bf16 *dst = op.dst(o) + u * G * (int64_t)D;
+#pragma unroll
+            for (int k = 0; k < 8; ++k) {
+                const int c = lane + 32 * k;
+                if (c < nch) st_vec(dst + (int64_t)c * 8, slot[o * kUnitChunks + swz(c)]);
+            }
+        }
+        __syncwarp();  // every lane is done with the slot before it is refilled
+        issue(u + (int64_t)NST * nwarps, st);
+        st = st + 1 == NST ? 0 : st + 1;
+    }
+    cp_async_wait<0>();
+}
+
+// ------------------------------------------------ small-row RMSNorm (D <= 256)
+// Per-head QK-norm rows (D = 128, 64) are a few hundred bytes, too short for the unit
+// pipeline above to pay off. Here every 8-lane team loads its row with direct 16-byte
+// loads, all K chunks issued at once: 32 rows per 256-thread CTA and up to 64 resident
+// warps per SM, so a launch keeps most of its rows in flight together. The reference tree is replayed with the transposed butterfly of
+// ref_pair_tree_sum (lanes hold chunks l and l+8k, i.e. reference lanes 4(l%8)+j).
+template <int K, bool kWeight>
+__global__ void __launch_bounds__(kRowBlock) rms_small(const anima_bf16 *x, const anima_bf16 *w, anima_bf16 *out,
+                                                       int64_t N, int D, float eps) {
+    constexpr int LPR = 8;
+    const int l = threadIdx.x & (LPR - 1);
+    const int64_t row = (int64_t)blockIdx.x * (kRowBlock / LPR) + threadIdx.x / LPR;
+    const bool live = row < N;
+    const anima_bf16 *xr = x + row * (int64_t)D;
+    Vec8 v[K], wv[K];
+#pragma unroll
+    for (int k = 0; k < K; ++k) v[k] = live ? ld_stream(xr + (l + LPR * k) * 8) : Vec8{{0u, 0u, 0u, 0u}};
+    if constexpr (kWeight) {
+#pragma unroll
+        for (int k = 0; k < K; ++k) wv[k] = ld_cached(w + (l + LPR * k) * 8);
+    }
+    float q[K][4];
 #pragma unroll
     for (int k = 0; k < K; ++k)
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
-            float a = bf_lo(v[k].w[j]), b = bf_hi(v[k].w[j]);
-            s[k][j] = a + b;
+            const float a = bf_lo(v[k].w[j]), b = bf_hi(v[k].w[j]);
             q[k][j] = fmaf(b, b, a * a);
         }
-}
-
-template <int LPR, int K>
-__device__ __forceinline__ float row_mean_invstd(const TeamRow<LPR, K> &t, const Vec8 (&v)[K], int D,
-                                                 float eps, float &mean) {
-    float s[K][4], q[K][4];
-    pair_stats<K>(v, s, q);
-    const float sum = ref_pair_tree_sum<LPR, K>(s, t.l, kFull);
-    const float sq = ref_pair_tree_sum<LPR, K>(q, t.l, kFull);
-    mean = __fdiv_rn(sum, (float)D);
-    return rsqrtf(ln_var(sq, mean, D) + eps);
-}
-
-template <int LPR, int K>
-__device__ __forceinline__ float row_rms_inv(const TeamRow<LPR, K> &t, const Vec8 (&v)[K], int D,
-                                             float eps) {
-    float s[K][4], q[K][4];
-    pair_stats<K>(v, s, q);
-    const float sq = ref_pair_tree_sum<LPR, K>(q, t.l, kFull);
-    return rsqrtf(__fdiv_rn(sq, (float)D) + eps);
-}
-
-template <int LPR, int K>
-__device__ __forceinline__ TeamRow<LPR, K> team_row(int64_t N) {
-    TeamRow<LPR, K> t;
-    t.l = threadIdx.x & (LPR - 1);
-    t.row = (int64_t)blockIdx.x * (blockDim.x / LPR) + threadIdx.x / LPR;
-    t.live = t.row < N;
-    return t;
-}
-
-template <int LPR, int K>
-__global__ void __launch_bounds__(kRowBlock) layer_norm_team(LayerNormOp op, int64_t N) {
-    auto t = team_row<LPR, K>(N);
-    Vec8 v[K];
-    load_row(t, op.x, op.D, v);
-    float mean;
-    const float inv = row_mean_invstd(t, v, op.D, op.eps, mean);
-    if (!t.live) return;
-    anima_bf16 *o = op.out + t.row * (int64_t)op.D;
-#pragma unroll
-    for (int k = 0; k < K; ++k) {
-        float f[8];
-        unpack8(v[k], f);
-#pragma unroll
-        for (int e = 0; e < 8; ++e) f[e] = (f[e] - mean) * inv;
-        st_vec(o + t.chunk_off(k), pack8(f));
-    }
-}
-
-template <int LPR, int K>
-__global__ void __launch_bounds__(kRowBlock) adaln_team(AdaLNOp op, int64_t N) {
-    auto t = team_row<LPR, K>(N);
-    Vec8 v[K];
-    load_row(t, op.x, op.D, v);
-    float mean;
-    const float inv = row_mean_invstd(t, v, op.D, op.eps, mean);
-    if (!t.live) return;
-    anima_bf16 *o = op.out + t.row * (int64_t)op.D;
-#pragma unroll
-    for (int k = 0; k < K; ++k) {
-        float f[8], sc[8], sh[8];
-        unpack8(v[k], f);
-        unpack8(ld_cached(op.scale + t.chunk_off(k)), sc);
-        unpack8(ld_cached(op.shift + t.chunk_off(k)), sh);
-#pragma unroll
-        for (int e = 0; e < 8; ++e) f[e] = fmaf((f[e] - mean) * inv, 1.0f + sc[e], sh[e]);
-        st_vec(o + t.chunk_off(k), pack8(f));
-    }
-}
-
-template <int LPR, int K>
-__global__ void __launch_bounds__(kRowBlock) ln_modulate_team(LnModulateOp op, int64_t N) {
-    auto t = team_row<LPR, K>(N);
-    Vec8 v[K];
-    load_row(t, op.x, op.D, v);
-    float mean;
-    const float inv = row_mean_invstd(t, v, op.D, op.eps, mean);
-    if (!t.live) return;
-    anima_bf16 *o = op.out + t.row * (int64_t)op.D;
-#pragma unroll
-    for (int k = 0; k < K; ++k) {
-        float f[8], sc[8], sh[8];
-        unpack8(v[k], f);
-        unpack8(ld_cached(op.scale + t.chunk_off(k)), sc);
-        unpack8(ld_cached(op.shift + t.chunk_off(k)), sh);
-#pragma unroll
-        for (int e = 0; e < 8; ++e)
-            f[e] = fmaf(bf16_round((f[e] - mean) * inv), 1.0f + sc[e], sh[e]);
-        st_vec(o + t.chunk_off(k), pack8(f));
-    }
-}
-
-struct ResGateAdaLNOp {  // layer_norm.cu:146-196
-    anima_bf16 *hidden;
-    const anima_bf16 *sub_out, *gate, *scale, *shift;
-    anima_bf16 *normed;
-    int D;
-    float eps;
-};
-
-template <int LPR, int K>
-__global__ void __launch_bounds__(kRowBlock) residual_gate_adaln_team(ResGateAdaLNOp op, int64_t N) {
-    auto t = team_row<LPR, K>(N);
-    Vec8 x[K], y[K];
-    load_row(t, op.hidden, op.D, x);
-    load_row(t, op.sub_out, op.D, y);
-    float s[K][4], q[K][4];
-    Vec8 hb[K];  // bf16(h), written back to hidden and re-read by the reference's pass 2
-#pragma unroll
-    for (int k = 0; k < K; ++k) {
-        const Vec8 g = ld_cached(op.gate + t.chunk_off(k));
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            // h = x + y*gate: the bf16 product is exact, so the reference's fma and
-            // this one round identically.
-            float h0 = fmaf(bf_lo(y[k].w[j]), bf_lo(g.w[j]), bf_lo(x[k].w[j]));
-            float h1 = fmaf(bf_hi(y[k].w[j]), bf_hi(g.w[j]), bf_hi(x[k].w[j]));
-            hb[k].w[j] = pack_bf2(h0, h1);
-            s[k][j] = h0 + h1;
-            q[k][j] = resid_sq_pair(h0, h1);
-        }
-    }
-    const float sum = ref_pair_tree_sum<LPR, K>(s, t.l, kFull);
-    const float sq = ref_pair_tree_sum<LPR, K>(q, t.l, kFull);
-    const float mean = __fdiv_rn(sum, (float)op.D);
-    const float inv = rsqrtf(ln_var(sq, mean, op.D) + op.eps);
-    if (!t.live) return;
-    anima_bf16 *hr = op.hidden + t.row * (int64_t)op.D;
-    anima_bf16 *nr = op.normed + t.row * (int64_t)op.D;
-#pragma unroll
-    for (int k = 0; k < K; ++k) {
-        st_vec(hr + t.chunk_off(k), hb[k]);
-        float f[8], sc[8], sh[8];
-        unpack8(hb[k], f);
-        unpack8(ld_cached(op.scale + t.chunk_off(k)), sc);
-        unpack8(ld_cached(op.shift + t.chunk_off(k)), sh);
-#pragma unroll
-        for (int e = 0; e < 8; ++e) f[e] = fmaf((f[e] - mean) * inv, 1.0f + sc[e], sh[e]);
-        st_vec(nr + t.chunk_off(k), pack8(f));
-    }
-}
-
-template <int LPR, int K, bool kWeight>
-__global__ void __launch_bounds__(kRowBlock) rms_norm_team(RmsOp op, int64_t N) {
-    auto t = team_row<LPR, K>(N);
-    Vec8 v[K];
-    load_row(t, op.x, op.D, v);
-    Vec8 w[K];
-    if constexpr (kWeight) {
-#pragma unroll
-        for (int k = 0; k < K; ++k) w[k] = ld_cached(op.weight + t.chunk_off(k));
-    }
-    const float r = row_rms_inv(t, v, op.D, op.eps);
-    if (!t.live) return;
-    anima_bf16 *o = op.out + t.row * (int64_t)op.D;
+    const float r = rsqrtf(__fdiv_rn(ref_pair_tree_sum<LPR, K>(q, l, kFull), (float)D) + eps);
+    if (!live) return;
+    anima_bf16 *o = out + row * (int64_t)D;
 #pragma unroll
     for (int k = 0; k < K; ++k) {
         float f[8];
         unpack8(v[k], f);
         if constexpr (kWeight) {
             float g[8];
-            unpack8(w[k], g);
+            unpack8(wv[k], g);
 #pragma unroll
-            for (int e = 0; e < 8; ++e) f[e] = (f[e] * r) * g[e];
+            for (int e = 0; e < 8; e += 2) {
+                const float2 t = __fmul2_rn(__fmul2_rn(f2(f[e], f[e + 1]), f2(r, r)), f2(g[e], g[e + 1]));
+                f[e] = t.x;
+                f[e + 1] = t.y;
+            }
         } else {
 #pragma unroll
             for (int e = 0; e < 8; ++e) f[e] = f[e] * r;
         }
-        st_vec(o + t.chunk_off(k), pack8(f));
-    }
-}
-
-template <int LPR, int K>
-__global__ void __launch_bounds__(kRowBlock) adaln_rms_team(AdaRmsOp op, int64_t N) {
-    auto t = team_row<LPR, K>(N);
-    Vec8 v[K];
-    load_row(t, op.x, op.D, v);
-    const float r = row_rms_inv(t, v, op.D, op.eps);
-    if (!t.live) return;
-    const int64_t base = t.row * (int64_t)op.D;
-#pragma unroll
-    for (int k = 0; k < K; ++k) {
-        float f[8], sc[8], sh[8];
-        unpack8(v[k], f);
-        unpack8(ld_stream(op.scale + base + t.chunk_off(k)), sc);
-        unpack8(ld_stream(op.shift + base + t.chunk_off(k)), sh);
-#pragma unroll
-        for (int e = 0; e < 8; ++e) f[e] = fmaf(f[e] * r, 1.0f + sc[e], sh[e]);
-        st_vec(op.out + base + t.chunk_off(k), pack8(f));
+        st_vec(o + (l + LPR * k) * 8, pack8(f));
     }
 }
 
@@ -411,24 +571,34 @@ __global__ void gemma_rms_generic(const anima_bf16 *x, const anima_bf16 *w, anim
 
 // ------------------------------------------------------------- dispatch
 
-// Picks (LPR, K) for the fast path: K = 8 chunks per lane whenever the row is wide
-// enough, so every lane has 128 bytes of loads in flight.
-template <class Launch>
-bool dispatch_team(int D, Launch &&launch) {
-    switch (D) {
-    case 64: launch.template go<8, 1>(); return true;
-    case 128: launch.template go<8, 2>(); return true;
-    case 256: launch.template go<8, 4>(); return true;
-    case 512: launch.template go<8, 8>(); return true;
-    case 1024: launch.template go<16, 8>(); return true;
-    case 2048: launch.template go<32, 8>(); return true;
-    default: return false;
-    }
+template <class Op, int NW>
+int launch_seg(const Op &op, int64_t N, int D, cudaStream_t s) {
+    const int smem = Op::NB * D * 4 + SegShape<Op::NIN>::kRingBytes;
+    auto kern = row_seg<NW, Op>;
+    int err = ANIMA_OK;
+    const int per_sm = resident_ctas((const void *)kern, kSegThreads, smem, &err);
+    if (per_sm <= 0) return err != ANIMA_OK ? err : ANIMA_ERR_NO_DEVICE;
+    constexpr int G = 32 / NW;
+    const int64_t units = (N + G - 1) / G;
+    int64_t grid = (units + kSegWarps - 1) / kSegWarps;
+    const int64_t cap = (int64_t)per_sm * sm_count();
+    if (grid > cap) grid = cap;
+    kern<<<(unsigned)grid, kSegThreads, smem, s>>>(op, N, D);
+    return launch_status();
 }
 
-inline unsigned team_grid(int64_t N, int LPR) {
-    const int64_t rows_per_block = kRowBlock / LPR;
-    return (unsigned)((N + rows_per_block - 1) / rows_per_block);
+// Fast path for D in {64, 128, ..., 2048}: one 64-element segment per lane.
+template <class Op>
+bool dispatch_seg(const Op &op, int64_t N, int D, cudaStream_t s, int &status) {
+    switch (D) {
+    case 64: status = launch_seg<Op, 1>(op, N, D, s); return true;
+    case 128: status = launch_seg<Op, 2>(op, N, D, s); return true;
+    case 256: status = launch_seg<Op, 4>(op, N, D, s); return true;
+    case 512: status = launch_seg<Op, 8>(op, N, D, s); return true;
+    case 1024: status = launch_seg<Op, 16>(op, N, D, s); return true;
+    case 2048: status = launch_seg<Op, 32>(op, N, D, s); return true;
+    default: return false;
+    }
 }
 
 inline unsigned generic_grid(int64_t N) { return (unsigned)(N < 2147483647 ? N : 2147483647); }
@@ -440,62 +610,6 @@ int check_row_args(int64_t N, int D) {
 }
 
 bool bf16_ok(const void *p) { return aligned_to(p, 2); }
-
-// Launchers the C entry points hand to dispatch_team (one per row op).
-struct LaunchLayerNormOp {
-    LayerNormOp op;
-    int64_t N;
-    cudaStream_t s;
-    template <int LPR, int K> void go() {
-        layer_norm_team<LPR, K><<<team_grid(N, LPR), kRowBlock, 0, s>>>(op, N);
-    }
-};
-
-struct LaunchAdaLNOp {
-    AdaLNOp op;
-    int64_t N;
-    cudaStream_t s;
-    template <int LPR, int K> void go() {
-        adaln_team<LPR, K><<<team_grid(N, LPR), kRowBlock, 0, s>>>(op, N);
-    }
-};
-
-struct LaunchLnModulateOp {
-    LnModulateOp op;
-    int64_t N;
-    cudaStream_t s;
-    template <int LPR, int K> void go() {
-        ln_modulate_team<LPR, K><<<team_grid(N, LPR), kRowBlock, 0, s>>>(op, N);
-    }
-};
-
-struct LaunchResGateAdaLNOp {
-    ResGateAdaLNOp op;
-    int64_t N;
-    cudaStream_t s;
-    template <int LPR, int K> void go() {
-        residual_gate_adaln_team<LPR, K><<<team_grid(N, LPR), kRowBlock, 0, s>>>(op, N);
-    }
-};
-
-struct LaunchRmsOp {
-    RmsOp op;
-    int64_t N;
-    cudaStream_t s;
-    template <int LPR, int K> void go() {
-        if (op.weight) rms_norm_team<LPR, K, true><<<team_grid(N, LPR), kRowBlock, 0, s>>>(op, N);
-        else rms_norm_team<LPR, K, false><<<team_grid(N, LPR), kRowBlock, 0, s>>>(op, N);
-    }
-};
-
-struct LaunchAdaRmsOp {
-    AdaRmsOp op;
-    int64_t N;
-    cudaStream_t s;
-    template <int LPR, int K> void go() {
-        adaln_rms_team<LPR, K><<<team_grid(N, LPR), kRowBlock, 0, s>>>(op, N);
-    }
-};
 
 }  // namespace
 }  // namespace anima
@@ -512,12 +626,10 @@ extern "C" int anima_layer_norm_bf16(const anima_bf16 *x, anima_bf16 *out, int N
     if (!bf16_ok(x) || !bf16_ok(out)) return ANIMA_ERR_MISALIGNED;
     const int64_t n = (int64_t)N * D * 2;
     if (partial_overlap(x, n, out, n)) return ANIMA_ERR_OVERLAP;
-    LayerNormOp op{x, out, D, eps};
-    LaunchLayerNormOp l{op, N, stream};
-    if (!(aligned16(x) && aligned16(out) && dispatch_team(D, l))) {
-        GenArgs a{x, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, out, D, eps};
-        row_generic<GenKind::LayerNorm><<<generic_grid(N), ref_row_threads(D), 0, stream>>>(a, N);
-    }
+    int st;
+    if (aligned16(x) && aligned16(out) && dispatch_seg(LayerNormOp{x, out, eps}, N, D, stream, st)) return st;
+    GenArgs a{x, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, out, D, eps};
+    row_generic<GenKind::LayerNorm><<<generic_grid(N), ref_row_threads(D), 0, stream>>>(a, N);
     return launch_status();
 }
 
@@ -530,12 +642,12 @@ extern "C" int anima_adaln_layernorm_bf16(const anima_bf16 *x, const anima_bf16 
     if (!bf16_ok(x) || !bf16_ok(scale) || !bf16_ok(shift) || !bf16_ok(out)) return ANIMA_ERR_MISALIGNED;
     const int64_t n = (int64_t)N * D * 2;
     if (partial_overlap(x, n, out, n)) return ANIMA_ERR_OVERLAP;
-    AdaLNOp op{x, scale, shift, out, D, eps};
-    LaunchAdaLNOp l{op, N, stream};
-    if (!(aligned16(x) && aligned16(out) && aligned16(scale) && aligned16(shift) && dispatch_team(D, l))) {
-        GenArgs a{x, nullptr, nullptr, nullptr, scale, shift, nullptr, out, D, eps};
-        row_generic<GenKind::AdaLN><<<generic_grid(N), ref_row_threads(D), 0, stream>>>(a, N);
-    }
+    int st;
+    if (aligned16(x) && aligned16(out) && aligned16(scale) && aligned16(shift) &&
+        dispatch_seg(AdaLNOp<false>{x, scale, shift, out, eps}, N, D, stream, st))
+        return st;
+    GenArgs a{x, nullptr, nullptr, nullptr, scale, shift, nullptr, out, D, eps};
+    row_generic<GenKind::AdaLN><<<generic_grid(N), ref_row_threads(D), 0, stream>>>(a, N);
     return launch_status();
 }
 
@@ -548,12 +660,12 @@ extern "C" int anima_layer_norm_modulate_bf16(const anima_bf16 *x, const anima_b
     if (!bf16_ok(x) || !bf16_ok(scale) || !bf16_ok(shift) || !bf16_ok(out)) return ANIMA_ERR_MISALIGNED;
     const int64_t n = (int64_t)N * D * 2;
     if (partial_overlap(x, n, out, n)) return ANIMA_ERR_OVERLAP;
-    LnModulateOp op{x, scale, shift, out, D, eps};
-    LaunchLnModulateOp l{op, N, stream};
-    if (!(aligned16(x) && aligned16(out) && aligned16(scale) && aligned16(shift) && dispatch_team(D, l))) {
-        GenArgs a{x, nullptr, nullptr, nullptr, scale, shift, nullptr, out, D, eps};
-        row_generic<GenKind::LnModulate><<<generic_grid(N), ref_row_threads(D), 0, stream>>>(a, N);
-    }
+    int st;
+    if (aligned16(x) && aligned16(out) && aligned16(scale) && aligned16(shift) &&
+        dispatch_seg(AdaLNOp<true>{x, scale, shift, out, eps}, N, D, stream, st))
+        return st;
+    GenArgs a{x, nullptr, nullptr, nullptr, scale, shift, nullptr, out, D, eps};
+    row_generic<GenKind::LnModulate><<<generic_grid(N), ref_row_threads(D), 0, stream>>>(a, N);
     return launch_status();
 }
 
@@ -572,13 +684,13 @@ extern "C" int anima_residual_gate_adaln_bf16(anima_bf16 *hidden, const anima_bf
     if (partial_overlap(hidden, n, normed, n) || hidden == normed) return ANIMA_ERR_OVERLAP;
     if (partial_overlap(sub_out, n, hidden, n) || partial_overlap(sub_out, n, normed, n))
         return ANIMA_ERR_OVERLAP;
-    ResGateAdaLNOp op{hidden, sub_out, gate, scale, shift, normed, D, eps};
-    LaunchResGateAdaLNOp l{op, N, stream};
-    if (!(aligned16(hidden) && aligned16(sub_out) && aligned16(gate) && aligned16(scale) &&
-          aligned16(shift) && aligned16(normed) && dispatch_team(D, l))) {
-        GenArgs a{hidden, hidden, sub_out, gate, scale, shift, nullptr, normed, D, eps};
-        row_generic<GenKind::ResGate><<<generic_grid(N), ref_row_threads(D), 0, stream>>>(a, N);
-    }
+    int st;
+    if (aligned16(hidden) && aligned16(sub_out) && aligned16(gate) && aligned16(scale) && aligned16(shift) &&
+        aligned16(normed) &&
+        dispatch_seg(ResGateAdaLNOp{hidden, sub_out, gate, scale, shift, normed, eps}, N, D, stream, st))
+        return st;
+    GenArgs a{hidden, hidden, sub_out, gate, scale, shift, nullptr, normed, D, eps};
+    row_generic<GenKind::ResGate><<<generic_grid(N), ref_row_threads(D), 0, stream>>>(a, N);
     return launch_status();
 }
 
@@ -590,12 +702,27 @@ extern "C" int anima_rms_norm_bf16(const anima_bf16 *x, const anima_bf16 *weight
     if (!bf16_ok(x) || !bf16_ok(out) || (weight && !bf16_ok(weight))) return ANIMA_ERR_MISALIGNED;
     const int64_t n = (int64_t)N * D * 2;
     if (partial_overlap(x, n, out, n)) return ANIMA_ERR_OVERLAP;
-    RmsOp op{x, weight, out, D, eps};
-    LaunchRmsOp l{op, N, stream};
-    if (!(aligned16(x) && aligned16(out) && (!weight || aligned16(weight)) && dispatch_team(D, l))) {
-        GenArgs a{x, nullptr, nullptr, nullptr, nullptr, nullptr, weight, out, D, eps};
-        row_generic<GenKind::Rms><<<generic_grid(N), ref_row_threads(D), 0, stream>>>(a, N);
+    int st;
+    if (aligned16(x) && aligned16(out) && (!weight || aligned16(weight)) && (D == 64 || D == 128 || D == 256)) {
+        const unsigned grid = (unsigned)((N + kRowBlock / 8 - 1) / (kRowBlock / 8));
+        switch (D) {
+#define ANIMA_RMS_SMALL(Dv, Kv)                                                                          \
+    case Dv:                                                                                            \
+        if (weight) rms_small<Kv, true><<<grid, kRowBlock, 0, stream>>>(x, weight, out, N, D, eps);       \
+        else rms_small<Kv, false><<<grid, kRowBlock, 0, stream>>>(x, weight, out, N, D, eps);             \
+        break;
+            ANIMA_RMS_SMALL(64, 1) ANIMA_RMS_SMALL(128, 2) ANIMA_RMS_SMALL(256, 4)
+#undef ANIMA_RMS_SMALL
+        }
+        return launch_status();
     }
+    if (aligned16(x) && aligned16(out) && (!weight || aligned16(weight))) {
+        const bool done = weight ? dispatch_seg(RmsOp<true>{x, weight, out, eps}, N, D, stream, st)
+                                 : dispatch_seg(RmsOp<false>{x, weight, out, eps}, N, D, stream, st);
+        if (done) return st;
+    }
+    GenArgs a{x, nullptr, nullptr, nullptr, nullptr, nullptr, weight, out, D, eps};
+    row_generic<GenKind::Rms><<<generic_grid(N), ref_row_threads(D), 0, stream>>>(a, N);
     return launch_status();
 }
 
@@ -610,12 +737,12 @@ extern "C" int anima_adaln_rms_norm_bf16(const anima_bf16 *x, const anima_bf16 *
     if (partial_overlap(x, n, out, n) || partial_overlap(scale, n, out, n) ||
         partial_overlap(shift, n, out, n))
         return ANIMA_ERR_OVERLAP;
-    AdaRmsOp op{x, scale, shift, out, D, eps};
-    LaunchAdaRmsOp l{op, N, stream};
-    if (!(aligned16(x) && aligned16(out) && aligned16(scale) && aligned16(shift) && dispatch_team(D, l))) {
-        GenArgs a{x, nullptr, nullptr, nullptr, scale, shift, nullptr, out, D, eps};
-        row_generic<GenKind::AdaRms><<<generic_grid(N), ref_row_threads(D), 0, stream>>>(a, N);
-    }
+    int st;
+    if (aligned16(x) && aligned16(out) && aligned16(scale) && aligned16(shift) &&
+        dispatch_seg(AdaRmsOp{x, scale, shift, out, eps}, N, D, stream, st))
+        return st;
+    GenArgs a{x, nullptr, nullptr, nullptr, scale, shift, nullptr, out, D, eps};
+    row_generic<GenKind::AdaRms><<<generic_grid(N), ref_row_threads(D), 0, stream>>>(a, N);
     return launch_status();
 }
 

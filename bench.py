@@ -172,7 +172,8 @@ class Chain:
             self.sets.append(dict(
                 hidden=randn((R, D)), normed=torch.empty((R, D), dtype=torch.bfloat16, device=device),
                 sub=randn((R, D)), q=randn((R, H * HD)), k=randn((R, H * HD)), qc=randn((R, H * HD)),
-                kc=randn((self.B * self.T, H * HD)), ff=randn((R, self.M))))
+                kc=randn((self.B * self.T, H * HD)), ff=randn((R, self.M)),
+                ff_out=torch.empty((R, self.M), dtype=torch.bfloat16, device=device)))
         # fresh modulation per block (3 adaLN-Zero sets of shift|scale|gate) + temb
         self.mod_raw = randn((self.NB, 3, 3 * D), std=0.1)
         self.mod = torch.empty_like(self.mod_raw)
@@ -224,7 +225,9 @@ class Chain:
         shift, scale, gate3 = (P(mod[2]), P(mod[2]) + 2 * D, P(mod[2]) + 4 * D)
         run("residual_gate_adaln", o.residual_gate_adaln, P(bs["hidden"]), P(bs["sub"]), gate2, scale, shift,
             P(bs["normed"]), R, D, self.eps, st)
-        run("gelu_tanh", o.gelu_tanh, P(bs["ff"]), P(bs["ff"]), R * self.M, st)
+        # the FFN activation is fresh every step (a GEMM output), so GELU reads ff and
+        # writes ff_out rather than re-applying itself to its own output
+        run("gelu_tanh", o.gelu_tanh, P(bs["ff"]), P(bs["ff_out"]), R * self.M, st)
         run("residual_gate_bcast", o.residual_gate_bcast, P(bs["hidden"]), P(bs["sub"]), gate3, P(bs["hidden"]), R,
             D, st)
 
@@ -358,7 +361,7 @@ def per_op_times(chain, ops, reps):
     return out
 
 
-def headline_kernels(ops, device, peak, reps=50):
+def headline_kernels(ops, device, peak, reps=192):
     """Each row kernel at the headline [4096, 2048] (GELU at [4096, 8192]), cycling 8
     buffer sets (> 4x L2) so every launch reads from HBM. Returns op -> GB/s, frac, us."""
     import torch
@@ -368,33 +371,43 @@ def headline_kernels(ops, device, peak, reps=50):
     x = [torch.randn((N, D), device=device).to(torch.bfloat16) for _ in range(sets)]
     y = [torch.randn((N, D), device=device).to(torch.bfloat16) for _ in range(sets)]
     o = [torch.empty((N, D), dtype=torch.bfloat16, device=device) for _ in range(sets)]
-    f = [torch.randn((N, M), device=device).to(torch.bfloat16) for _ in range(2)]
+    f = [torch.randn((N, M), device=device).to(torch.bfloat16) for _ in range(4)]
     v = (torch.randn((3 * D,), device=device) * 0.1).to(torch.bfloat16)
     sc, sh, g = v.data_ptr(), v.data_ptr() + 2 * D, v.data_ptr() + 4 * D
-    s = torch.cuda.current_stream().cuda_stream
     eps = 1e-6
+
+    def S():
+        return torch.cuda.current_stream().cuda_stream  # the capture stream inside capture()
+
     cases = {
-        "adaln_layernorm": (4 * N * D + 4 * D, lambda i: ops.adaln_layernorm(x[i].data_ptr(), sc, sh, o[i].data_ptr(), N, D, eps, s)),
+        "adaln_layernorm": (4 * N * D + 4 * D, lambda i: ops.adaln_layernorm(x[i].data_ptr(), sc, sh, o[i].data_ptr(), N, D, eps, S())),
         "residual_gate_adaln": (8 * N * D + 6 * D, lambda i: ops.residual_gate_adaln(
-            x[i].data_ptr(), y[i].data_ptr(), g, sc, sh, o[i].data_ptr(), N, D, eps, s)),
+            x[i].data_ptr(), y[i].data_ptr(), g, sc, sh, o[i].data_ptr(), N, D, eps, S())),
         "residual_gate_bcast": (6 * N * D + 2 * D, lambda i: ops.residual_gate_bcast(
-            x[i].data_ptr(), y[i].data_ptr(), g, x[i].data_ptr(), N, D, s)),
+            x[i].data_ptr(), y[i].data_ptr(), g, x[i].data_ptr(), N, D, S())),
         "rms_norm_qk128": (4 * N * D + 256, lambda i: ops.rms_norm(x[i].data_ptr(), v.data_ptr(), o[i].data_ptr(),
-                                                                   N * 16, 128, eps, s)),
-        "gelu_tanh_4096x8192": (4 * N * M, lambda i: ops.gelu_tanh(f[i % 2].data_ptr(), f[i % 2].data_ptr(), N * M, s)),
+                                                                   N * 16, 128, eps, S())),
+        "gelu_tanh_4096x8192": (4 * N * M, lambda i: ops.gelu_tanh(f[i % 2].data_ptr(), f[2 + i % 2].data_ptr(), N * M,
+                                                                   S())),
     }
     res = {}
+    per_graph = 6 * sets  # launches per captured graph, cycling the buffer sets
     for name, (nbytes, fn) in cases.items():
         for i in range(4):
             fn(i % sets)
         torch.cuda.synchronize()
+        graph = capture(lambda st: [fn(i % sets) for i in range(per_graph)])
+        graph.replay()
+        torch.cuda.synchronize()
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        n_rep = max(1, reps // per_graph)
         a.record()
-        for i in range(reps):
-            fn(i % sets)
+        for _ in range(n_rep):
+            graph.replay()
         b.record()
         torch.cuda.synchronize()
-        us = a.elapsed_time(b) * 1e3 / reps
+        del graph
+        us = a.elapsed_time(b) * 1e3 / (n_rep * per_graph)
         gbs = nbytes / (us * 1e-6) / 1e9
         res[name] = {"gbs": round(gbs, 1), "frac": round(gbs / peak, 3), "us": round(us, 2), "bytes": nbytes}
     del x, y, o, f
@@ -442,6 +455,26 @@ def cpu_baseline_sample(blocks=2, rows=8192):
     return nbytes / dt / 1e9, f"{blocks} of the 28 blocks of the cfg2 chain at {R} rows ({dt:.1f} s)"
 
 
+def profile_one_op(args, chain, launches_per_step, bytes_per_launch):
+    """--only: W eager warm-up steps then K timed eager steps of one op type (its real
+    arguments across the 28 blocks). Small and self-contained, for ncu captures."""
+    import torch
+
+    s = torch.cuda.current_stream().cuda_stream
+    for _ in range(args.warmup):
+        chain.blocks(s, only=args.only)
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(args.steps):
+        chain.blocks(s, only=args.only)
+    b.record()
+    torch.cuda.synchronize()
+    us = a.elapsed_time(b) * 1e3 / (args.steps * launches_per_step)
+    print(json.dumps({"op": args.only, "impl": args.impl, "launches": args.steps * launches_per_step,
+                      "us_per_launch": round(us, 2), "gbs": round(bytes_per_launch / (us * 1e-6) / 1e9, 1)}))
+
+
 # ---------------------------------------------------------------- main
 def main():
     ap = argparse.ArgumentParser()
@@ -452,6 +485,8 @@ def main():
     ap.add_argument("--eager", action="store_true", help="time eager launches instead of CUDA graph replay")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-headline", action="store_true")
+    ap.add_argument("--only", default=None,
+                    help="profiling aid: run only this op type of the chain (eager), print its timing, exit")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -480,6 +515,9 @@ def main():
     stream = torch.cuda.current_stream()
     peak, peak_kind = peaks()
     total_bytes, per_block, lpb = chain_bytes()
+
+    if args.only is not None:
+        return profile_one_op(args, chain, lpb[args.only] * CFG["blocks"], per_block[args.only] / lpb[args.only])
 
     # warm-up (also initialises every kernel and the library's device caches)
     for _ in range(args.warmup):

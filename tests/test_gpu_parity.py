@@ -199,6 +199,35 @@ def test_unary_extreme_inputs(anima, ref, op):
     assert_bit_exact(host(out), host(out_ref), f"{op} extremes vs reference")
 
 
+@pytest.mark.parametrize("op", ["gelu_tanh", "silu"])
+def test_unary_exhaustive(anima, ref, op):
+    """GELU and SiLU map one bf16 input to one bf16 output, so all 65536 inputs (both
+    zeros, subnormals, Inf, every NaN payload) settle parity completely -- for the
+    table-driven fast path and its inline-formula fallback alike."""
+    x = np.arange(65536, dtype=np.uint32).astype(np.uint16)
+    x = np.concatenate([x, x[::-1]])  # both halves of a bf16 pair see every value
+    dx = dev(x)
+    n = x.size
+    out, out_ref = empty_bf16(n), empty_bf16(n)
+    getattr(anima, op)(dx, out, n)
+    getattr(ref, op + "_bf16")(dx.data_ptr(), out_ref.data_ptr(), n, stream_ptr())
+    torch.cuda.synchronize()
+    assert np.array_equal(host(out), host(out_ref)), f"{op}: {int((host(out) != host(out_ref)).sum())} of {n} differ"
+
+
+def test_swiglu_exhaustive_gate(anima, ref, rng):
+    x = np.arange(65536, dtype=np.uint32).astype(np.uint16)
+    u = O.randn_bf16(rng, x.size)
+    dg, du = dev(x), dev(u)
+    out = empty_bf16(x.size)
+    anima.swiglu(dg, du, out, x.size)
+    gr = dev(x)
+    ref.silu_bf16(gr.data_ptr(), gr.data_ptr(), x.size, stream_ptr())
+    ref.mul_bf16(gr.data_ptr(), du.data_ptr(), gr.data_ptr(), x.size, stream_ptr())
+    torch.cuda.synchronize()
+    assert np.array_equal(host(out), host(gr))
+
+
 @pytest.mark.parametrize("op", ["gelu_tanh_bias", "silu_bias"])
 @pytest.mark.parametrize("M,D", [(3, 6144), (1000, 8), (7, 10)])
 def test_unary_bias(anima, ref, rng, op, M, D):
