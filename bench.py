@@ -296,6 +296,24 @@ class ClockSampler:
                 "power_w_max": max(power) if power else None, "reasons": sorted(reasons), "samples": len(sm)}
 
 
+# ---------------------------------------------------------------- multi-rank plumbing
+def reduce_max(value: float, dist, device) -> float:
+    """Max of a per-rank scalar over all ranks (the slowest rank's device time)."""
+    if dist is None:
+        return value
+    import torch
+
+    t = torch.tensor([value], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def aggregate_gbs(n_ranks: int, bytes_per_step: int, steps: int, max_ms: float) -> float:
+    """Whole-job throughput: every rank processed `steps` steps of `bytes_per_step`
+    (weak scaling); the job took as long as its slowest rank."""
+    return n_ranks * bytes_per_step * steps / (max_ms * 1e-3) / 1e9
+
+
 # ---------------------------------------------------------------- measurements
 def peaks():
     try:
@@ -546,14 +564,12 @@ def main():
     t_begin = clocks.mark()
     ms = time_steps(chain, args.steps, stream, graph)
     t_end = clocks.mark()
+    ms = reduce_max(ms, dist, device)
     if dist is not None:
-        t = torch.tensor([ms], device=device, dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
         dist.barrier()
     clk = clocks.stop(t_begin, t_end)
     ms_per_step = ms / args.steps
-    value = n_gpus * total_bytes * args.steps / (ms * 1e-3) / 1e9
+    value = aggregate_gbs(n_gpus, total_bytes, args.steps, ms)
 
     # per-op device times (graph replay of each op type alone) -> roofline
     ops_t = per_op_times(chain, {k: v * CFG["blocks"] for k, v in lpb.items()}, max(3, min(args.steps, 20)))
@@ -591,11 +607,7 @@ def main():
         h_out.copy_(chain.sets[(CFG["blocks"] - 1) % NSETS]["hidden"], non_blocking=True)
     b.record()
     torch.cuda.synchronize()
-    e2e_ms = a.elapsed_time(b) / e2e_steps
-    if dist is not None:
-        t = torch.tensor([e2e_ms], device=device, dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e2e_ms = float(t.item())
+    e2e_ms = reduce_max(a.elapsed_time(b) / e2e_steps, dist, device)
     h2d = h_in.numel() * 2 + m_in.numel() * 2 + (0 if args.impl == "anima" else CFG["ts_dim"] * 2)
     d2h = h_out.numel() * 2
 
@@ -627,7 +639,7 @@ def main():
                    "timing": ("CUDA graph replay of the 28 blocks + eager timestep launch per step"
                               if used_graph else "eager launches"),
                    "parallelism": f"replicas x{n_gpus} (rows independent; no collective on the data path)"},
-        "e2e": {"value": round(n_gpus * total_bytes / (e2e_ms * 1e-3) / 1e9, 1), "unit": "GB/s",
+        "e2e": {"value": round(aggregate_gbs(n_gpus, total_bytes, 1, e2e_ms), 1), "unit": "GB/s",
                 "ms_per_step": round(e2e_ms, 4), "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
         "gpu_launches": launches_per_step * args.steps if args.impl == "anima" else 0,
         "roofline": {"bound": "hbm", "kernel": dom, "achieved": dk["gbs"], "peak": peak, "unit": "GB/s",

@@ -1,0 +1,71 @@
+"""Multi-rank plumbing of bench.py on the CPU: two gloo ranks (127.0.0.1) exercise the
+max-over-ranks reduction and the whole-job aggregate that the GPU run uses over NCCL,
+and the reference arm's rule that only rank 0 runs (the reference is single-GPU code)."""
+import os
+import socket
+import sys
+
+import pytest
+import torch.multiprocessing as mp
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _worker(rank, world, port, q):
+    import datetime
+
+    import torch.distributed as dist
+
+    sys.path.insert(0, ROOT)
+    import bench
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
+    local_ms = 100.0 + 50.0 * rank  # rank 1 is the slow one
+    m = bench.reduce_max(local_ms, dist, "cpu")
+    v = bench.aggregate_gbs(world, 10**9, 10, m)
+    q.put((rank, m, v))
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+def test_two_rank_max_and_aggregate():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = sorted(q.get(timeout=120) for _ in procs)
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    for rank, m, v in res:
+        assert m == 150.0  # every rank sees the slowest rank's time
+        assert v == pytest.approx(2 * 10**9 * 10 / 0.150 / 1e9)
+
+
+def test_reference_arm_runs_on_rank_zero_only(monkeypatch):
+    sys.path.insert(0, ROOT)
+    import bench
+
+    monkeypatch.setenv("RANK", "1")
+    monkeypatch.setenv("WORLD_SIZE", "2")
+    monkeypatch.setenv("LOCAL_RANK", "1")
+    monkeypatch.setattr(sys, "argv", ["bench.py", "--impl", "reference", "--gpus", "2"])
+    assert bench.main() is None  # returns before touching a GPU
+
+
+def test_chain_byte_count_matches_the_survey_figure():
+    sys.path.insert(0, ROOT)
+    import bench
+
+    total, per_block, launches = bench.chain_bytes()
+    assert abs(total / 28 / 1e6 - 1049.6) < 1.5  # MB per block at cfg2 (plus the tiny mod adds)
+    assert sum(launches.values()) == 14
