@@ -324,6 +324,20 @@ def peaks():
         return 6650.0, "fallback"
 
 
+def dram_traffic(op):
+    """DRAM bytes per launch of `op` from the ncu capture summarised in profiles/ (None
+    if that kernel has not been captured)."""
+    try:
+        with open(os.path.join(ROOT, "profiles", "dram_traffic.txt")) as f:
+            for line in f:
+                parts = line.split()
+                if parts and not parts[0].startswith("#") and parts[0] == op:
+                    return int(parts[1])
+    except OSError:
+        pass
+    return None
+
+
 def time_steps(chain, steps, stream_obj, graph, ts=True):
     """Device time (ms) of `steps` steps on the current stream, events on both sides."""
     import torch
@@ -643,7 +657,8 @@ def main():
                 "ms_per_step": round(e2e_ms, 4), "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
         "gpu_launches": launches_per_step * args.steps if args.impl == "anima" else 0,
         "roofline": {"bound": "hbm", "kernel": dom, "achieved": dk["gbs"], "peak": peak, "unit": "GB/s",
-                     "frac": dk["frac"], "peak_kind": peak_kind, "traffic": None,
+                     "frac": dk["frac"], "peak_kind": peak_kind,
+                     "traffic": dram_traffic(dom) if args.impl == "anima" else None,
                      "bytes_per_launch": dk["bytes_per_launch"], "us_per_launch": dk["us"]},
         "chain_frac_of_peak": round(value / n_gpus / peak, 3),
         "cpu_baseline": cpu,
