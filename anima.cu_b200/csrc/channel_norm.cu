@@ -51,6 +51,7 @@ struct CnArgs {
 
 template <bool kSilu>
 __global__ void __launch_bounds__(kCnBlock) channel_norm_tile(CnArgs a) {
+    pdl_wait();
     extern __shared__ __align__(16) anima_bf16 tile[];  // [C][kCnPix]
     __shared__ float rms_s[kCnPix];
     const int b = blockIdx.x / a.tiles_per_image;
@@ -82,6 +83,7 @@ __global__ void __launch_bounds__(kCnBlock) channel_norm_tile(CnArgs a) {
         rms_s[p] = rsqrtf(__fdiv_rn(q, (float)a.C) + a.eps);
     }
     __syncthreads();
+    pdl_launch();
 
     // vae_kernels.cu:75-80: out = (x * rms) * gamma[c], from shared memory.
     for (int q = threadIdx.x; q < nchunks; q += kCnBlock) {
@@ -104,6 +106,7 @@ __global__ void __launch_bounds__(kCnBlock) channel_norm_tile(CnArgs a) {
 // Reference-order kernel for any shape: one thread per (image, pixel).
 template <bool kSilu>
 __global__ void channel_norm_serial(CnArgs a, int64_t pixels) {
+    pdl_wait();
     for (int64_t p = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; p < pixels;
          p += (int64_t)gridDim.x * blockDim.x) {
         const int64_t b = p / a.spatial, s = p % a.spatial;
@@ -141,13 +144,13 @@ int channel_norm(const anima_bf16 *x, const anima_bf16 *gamma, anima_bf16 *out, 
         tiles < 2147483647) {
         auto kern = channel_norm_tile<kSilu>;
         if (int e = allow_dynamic_smem((const void *)kern, kCnMaxSmem, kSilu ? 1 : 0)) return e;
-        kern<<<(unsigned)tiles, kCnBlock, (size_t)smem, stream>>>(a);
+        launch(kern, (unsigned)tiles, kCnBlock, (size_t)smem, stream, a);
     } else {
         const int64_t pixels = (int64_t)B * spatial;
         int64_t blocks = (pixels + 255) / 256;
         const int64_t wave = (int64_t)sm_count() * 8;
         if (blocks > wave) blocks = wave;
-        channel_norm_serial<kSilu><<<(unsigned)blocks, 256, 0, stream>>>(a, pixels);
+        launch(channel_norm_serial<kSilu>, (unsigned)blocks, 256, 0, stream, a, pixels);
     }
     return launch_status();
 }

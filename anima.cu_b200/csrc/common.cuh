@@ -185,6 +185,16 @@ __host__ __device__ __forceinline__ int ref_row_threads(int D) {
     return t < 32 ? 32 : t;
 }
 
+// ------------------------------------------------- programmatic dependent launch
+// Every kernel is launched with programmatic stream serialisation, so its CTAs may be
+// scheduled while the previous kernel in the stream drains. pdl_wait() -- the first
+// statement of every kernel, before any global memory access -- blocks until that
+// previous kernel has completed and its writes are visible (a no-op when the launch had
+// no predecessor or was not programmatic). pdl_launch() lets the next kernel start its
+// launch early; a CTA that exits counts as having called it.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 // ------------------------------------------------------------------ host side
 
 // Number of SMs of the current device (cached per device ordinal).
@@ -210,6 +220,23 @@ inline bool partial_overlap(const void *a, int64_t na, const void *b, int64_t nb
     uintptr_t x = reinterpret_cast<uintptr_t>(a), y = reinterpret_cast<uintptr_t>(b);
     if (x == y) return false;
     return x < y + (uintptr_t)nb && y < x + (uintptr_t)na;
+}
+
+// Launches `kernel` on `stream` with programmatic dependent launch allowed.
+template <typename... KArgs, typename... Args>
+inline void launch(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                   Args &&...args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
 }
 
 // Status of the launch just issued (launch-configuration errors only; kernels run async).

@@ -97,6 +97,7 @@ __device__ __forceinline__ float ldb(const anima_bf16 *p) {
 
 template <class Op, int U>
 __global__ void __launch_bounds__(kEwBlock) ew_kernel(EwArgs a, Op op) {
+    pdl_wait();
     constexpr int NS = Op::NS, NB = Op::NB;
     const int64_t tid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     const int64_t stride = (int64_t)gridDim.x * blockDim.x;
@@ -140,6 +141,7 @@ __global__ void __launch_bounds__(kEwBlock) ew_kernel(EwArgs a, Op op) {
             }
         }
     }
+    pdl_launch();
     // Scalar path: the tail past the last full chunk, or everything when misaligned.
     for (int64_t e = done + tid; e < a.n; e += stride) {
         float s[2] = {ldb(a.s0 + e), NS > 1 ? ldb(a.s1 + e) : 0.0f};
@@ -162,7 +164,7 @@ int launch_ew(const EwArgs &a, cudaStream_t stream) {
     const int64_t wave = (int64_t)sm_count() * (2048 / kEwBlock);
     if (blocks > wave) blocks = wave;
     if (blocks < 1) blocks = 1;
-    ew_kernel<Op, U><<<(unsigned)blocks, kEwBlock, 0, stream>>>(a, Op{});
+    launch(ew_kernel<Op, U>, (unsigned)blocks, kEwBlock, 0, stream, a, Op{});
     return launch_status();
 }
 
@@ -283,6 +285,7 @@ __device__ __forceinline__ Vec8 fast_chunk(const Vec8 &v) {
 // NS = 1: out = F(x). NS = 2 (SwiGLU): out = bf16(F(gate)) * up, as silu_bf16 then mul_bf16.
 template <class F, int NS>
 __global__ void __launch_bounds__(kEwBlock) fast_act_kernel(EwArgs a) {
+    pdl_wait();
     constexpr int U = 4;
     const int64_t tid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     const int64_t stride = (int64_t)gridDim.x * blockDim.x;
@@ -315,6 +318,7 @@ __global__ void __launch_bounds__(kEwBlock) fast_act_kernel(EwArgs a) {
             st_vec(a.out + i * 8, o);
         }
     }
+    pdl_launch();
     for (int64_t e = (nch << 3) + tid; e < a.n; e += stride) {
         const uint32_t r = exact_bf16<F>(*reinterpret_cast<const uint16_t *>(a.s0 + e));
         if constexpr (NS == 1) {
@@ -334,7 +338,7 @@ int launch_fast_act(const EwArgs &a, cudaStream_t stream) {
     const int64_t wave = (int64_t)sm_count() * (2048 / kEwBlock);
     if (blocks > wave) blocks = wave;
     if (blocks < 1) blocks = 1;
-    fast_act_kernel<F, NS><<<(unsigned)blocks, kEwBlock, 0, stream>>>(a);
+    launch(fast_act_kernel<F, NS>, (unsigned)blocks, kEwBlock, 0, stream, a);
     return launch_status();
 }
 

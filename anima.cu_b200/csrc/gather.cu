@@ -22,6 +22,7 @@ struct GatherArgs {
 };
 
 __global__ void __launch_bounds__(kGatherBlock) gather_vec(GatherArgs a) {
+    pdl_wait();
     const int lane = threadIdx.x & 31;
     const int64_t t = (int64_t)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
     if (t >= a.T) return;
@@ -49,6 +50,7 @@ __global__ void __launch_bounds__(kGatherBlock) gather_vec(GatherArgs a) {
 
 // Any D and 2-byte alignment: element copies.
 __global__ void gather_scalar(GatherArgs a) {
+    pdl_wait();
     const int64_t t = (int64_t)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
     if (t >= a.T) return;
     const int lane = threadIdx.x & 31;
@@ -78,8 +80,8 @@ extern "C" int anima_embedding_lookup_bf16(const anima_bf16 *table, const int32_
     const int64_t per_block = kGatherBlock / 32;
     const unsigned grid = (unsigned)((T + per_block - 1) / per_block);
     if (D % 8 == 0 && aligned16(table) && aligned16(out))
-        gather_vec<<<grid, kGatherBlock, 0, stream>>>(a);
+        launch(gather_vec, grid, kGatherBlock, 0, stream, a);
     else
-        gather_scalar<<<grid, kGatherBlock, 0, stream>>>(a);
+        launch(gather_scalar, grid, kGatherBlock, 0, stream, a);
     return launch_status();
 }

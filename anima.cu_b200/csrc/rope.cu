@@ -47,6 +47,7 @@ struct CosmosArgs {
 };
 
 __global__ void __launch_bounds__(kRopeBlock) rope_cosmos_vec(CosmosArgs a) {
+    pdl_wait();
     const int64_t stride = (int64_t)gridDim.x * blockDim.x;
     const uint32_t per_row = (uint32_t)a.H * a.hc;
     const int half = a.HD / 2;
@@ -82,11 +83,13 @@ __global__ void __launch_bounds__(kRopeBlock) rope_cosmos_vec(CosmosArgs a) {
             st_vec(p[u] + half, pack8(o_i));
         }
     }
+    pdl_launch();
 }
 
 // One thread per element pair, scalar accesses (any even HD, any 2-byte alignment).
 __global__ void rope_cosmos_scalar(anima_bf16 *x, const anima_bf16 *cos_t, const anima_bf16 *sin_t,
                                    int S, int H, int HD, int64_t pairs) {
+    pdl_wait();
     const int half = HD / 2;
     const int64_t per_row = (int64_t)H * half;
     for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < pairs;
@@ -110,6 +113,7 @@ struct StdArgs {
 };
 
 __global__ void __launch_bounds__(kRopeBlock) rope_standard_vec(StdArgs a) {
+    pdl_wait();
     const int64_t stride = (int64_t)gridDim.x * blockDim.x;
     const int half = a.D / 2;
     for (int64_t base = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; base < a.units;
@@ -150,10 +154,12 @@ __global__ void __launch_bounds__(kRopeBlock) rope_standard_vec(StdArgs a) {
             st_vec(p[u] + half, pack8(o2));
         }
     }
+    pdl_launch();
 }
 
 __global__ void rope_standard_scalar(anima_bf16 *x, const float *cos_t, const float *sin_t, int T,
                                      int D, int64_t pairs) {
+    pdl_wait();
     const int half = D / 2;
     for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < pairs;
          i += (int64_t)gridDim.x * blockDim.x) {
@@ -181,6 +187,7 @@ struct QkArgs {
 };
 
 __global__ void __launch_bounds__(kRopeBlock) qk_norm_rope_128(QkArgs a) {
+    pdl_wait();
     constexpr int LPR = 8, K = 2, HD = 128;
     const int l = threadIdx.x & (LPR - 1);
     const int64_t hid = (int64_t)blockIdx.x * (blockDim.x / LPR) + threadIdx.x / LPR;
@@ -209,6 +216,7 @@ __global__ void __launch_bounds__(kRopeBlock) qk_norm_rope_128(QkArgs a) {
         }
     const float sq = ref_pair_tree_sum<LPR, K>(q, l, 0xffffffffu);
     const float r = rsqrtf(__fdiv_rn(sq, (float)HD) + a.eps);
+    pdl_launch();
     if (!live) return;
     float x0[8], x1[8], w0[8], w1[8], c[8], sn[8], o0[8], o1[8];
     unpack8(v[0], x0);
@@ -257,12 +265,10 @@ extern "C" int anima_rope_cosmos_strided_bf16(anima_bf16 *x, const anima_bf16 *c
         return ANIMA_ERR_OVERLAP;
     if (HD % 16 == 0 && aligned16(x) && aligned16(cos_table) && aligned16(sin_table)) {
         CosmosArgs a{x, cos_table, sin_table, S, H, HD, rows * H * (HD / 16), (uint32_t)(HD / 16)};
-        rope_cosmos_vec<<<grid_for((a.units + kRopeU - 1) / kRopeU, kRopeBlock), kRopeBlock, 0,
-                          stream>>>(a);
+        launch(rope_cosmos_vec, grid_for((a.units + kRopeU - 1) / kRopeU, kRopeBlock), kRopeBlock, 0, stream, a);
     } else {
         const int64_t pairs = rows * H * (HD / 2);
-        rope_cosmos_scalar<<<grid_for(pairs, kRopeBlock), kRopeBlock, 0, stream>>>(
-            x, cos_table, sin_table, S, H, HD, pairs);
+        launch(rope_cosmos_scalar, grid_for(pairs, kRopeBlock), kRopeBlock, 0, stream, x, cos_table, sin_table, S, H, HD, pairs);
     }
     return launch_status();
 }
@@ -275,12 +281,10 @@ extern "C" int anima_rope_standard_bf16(anima_bf16 *x, const float *cos_table, c
     if (!bf16_ok(x) || !aligned_to(cos_table, 4) || !aligned_to(sin_table, 4)) return ANIMA_ERR_MISALIGNED;
     if (D % 16 == 0 && aligned16(x) && aligned16(cos_table) && aligned16(sin_table)) {
         StdArgs a{x, cos_table, sin_table, T, D, (int64_t)total_rows * (D / 16), (uint32_t)(D / 16)};
-        rope_standard_vec<<<grid_for((a.units + kRopeU - 1) / kRopeU, kRopeBlock), kRopeBlock, 0,
-                            stream>>>(a);
+        launch(rope_standard_vec, grid_for((a.units + kRopeU - 1) / kRopeU, kRopeBlock), kRopeBlock, 0, stream, a);
     } else {
         const int64_t pairs = (int64_t)total_rows * (D / 2);
-        rope_standard_scalar<<<grid_for(pairs, kRopeBlock), kRopeBlock, 0, stream>>>(
-            x, cos_table, sin_table, T, D, pairs);
+        launch(rope_standard_scalar, grid_for(pairs, kRopeBlock), kRopeBlock, 0, stream, x, cos_table, sin_table, T, D, pairs);
     }
     return launch_status();
 }
@@ -301,7 +305,7 @@ extern "C" int anima_qk_norm_rope_bf16(anima_bf16 *x, const anima_bf16 *weight,
             return ANIMA_ERR_OVERLAP;
         QkArgs a{x, weight, cos_table, sin_table, S, H, heads, eps};
         const int64_t per_block = kRopeBlock / 8;
-        qk_norm_rope_128<<<(unsigned)((heads + per_block - 1) / per_block), kRopeBlock, 0, stream>>>(a);
+        launch(qk_norm_rope_128, (unsigned)((heads + per_block - 1) / per_block), kRopeBlock, 0, stream, a);
         return launch_status();
     }
     // Other head sizes: the same two steps as the reference, back to back.

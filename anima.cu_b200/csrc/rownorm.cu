@@ -347,6 +347,7 @@ struct AdaRmsOp {  // adaln.cu:11-58 (per-row scale/shift streamed alongside x)
 
 template <int NW, class Op>
 __global__ void __launch_bounds__(kSegThreads) row_seg(Op op, int64_t N, int D) {
+    pdl_wait();
     constexpr int NIN = Op::NIN, NOUT = Op::NOUT, NB = Op::NB;
     constexpr int G = 32 / NW;  // rows per unit
     constexpr int NST = SegShape<NIN>::kStages;
@@ -406,6 +407,7 @@ __global__ void __launch_bounds__(kSegThreads) row_seg(Op op, int64_t N, int D) 
         issue(u + (int64_t)NST * nwarps, st);
         st = st + 1 == NST ? 0 : st + 1;
     }
+    pdl_launch();
     cp_async_wait<0>();
 }
 
@@ -418,6 +420,7 @@ __global__ void __launch_bounds__(kSegThreads) row_seg(Op op, int64_t N, int D) 
 template <int K, bool kWeight>
 __global__ void __launch_bounds__(kRowBlock) rms_small(const anima_bf16 *x, const anima_bf16 *w, anima_bf16 *out,
                                                        int64_t N, int D, float eps) {
+    pdl_wait();
     constexpr int LPR = 8;
     const int l = threadIdx.x & (LPR - 1);
     const int64_t row = (int64_t)blockIdx.x * (kRowBlock / LPR) + threadIdx.x / LPR;
@@ -439,6 +442,7 @@ __global__ void __launch_bounds__(kRowBlock) rms_small(const anima_bf16 *x, cons
             q[k][j] = fmaf(b, b, a * a);
         }
     const float r = rsqrtf(__fdiv_rn(ref_pair_tree_sum<LPR, K>(q, l, kFull), (float)D) + eps);
+    pdl_launch();
     if (!live) return;
     anima_bf16 *o = out + row * (int64_t)D;
 #pragma unroll
@@ -487,6 +491,7 @@ struct GenArgs {
 
 template <GenKind KIND>
 __global__ void row_generic(GenArgs a, int64_t N) {
+    pdl_wait();
     __shared__ float red[33];
     const int D2 = a.D / 2, T = blockDim.x;
     for (int64_t row = blockIdx.x; row < N; row += gridDim.x) {
@@ -554,6 +559,7 @@ __global__ void row_generic(GenArgs a, int64_t N) {
 // gemma_ops.cu:132-168: scalar loop over D with min(roundup32(D),1024) threads per row.
 __global__ void gemma_rms_generic(const anima_bf16 *x, const anima_bf16 *w, anima_bf16 *out,
                                   int64_t N, int D, float eps) {
+    pdl_wait();
     __shared__ float red[33];
     for (int64_t row = blockIdx.x; row < N; row += gridDim.x) {
         const int64_t base = row * (int64_t)D;
@@ -583,7 +589,7 @@ int launch_seg(const Op &op, int64_t N, int D, cudaStream_t s) {
     int64_t grid = (units + kSegWarps - 1) / kSegWarps;
     const int64_t cap = (int64_t)per_sm * sm_count();
     if (grid > cap) grid = cap;
-    kern<<<(unsigned)grid, kSegThreads, smem, s>>>(op, N, D);
+    launch(kern, (unsigned)grid, kSegThreads, (size_t)smem, s, op, N, D);
     return launch_status();
 }
 
@@ -629,7 +635,7 @@ extern "C" int anima_layer_norm_bf16(const anima_bf16 *x, anima_bf16 *out, int N
     int st;
     if (aligned16(x) && aligned16(out) && dispatch_seg(LayerNormOp{x, out, eps}, N, D, stream, st)) return st;
     GenArgs a{x, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, out, D, eps};
-    row_generic<GenKind::LayerNorm><<<generic_grid(N), ref_row_threads(D), 0, stream>>>(a, N);
+    launch(row_generic<GenKind::LayerNorm>, generic_grid(N), ref_row_threads(D), 0, stream, a, N);
     return launch_status();
 }
 
@@ -647,7 +653,7 @@ extern "C" int anima_adaln_layernorm_bf16(const anima_bf16 *x, const anima_bf16 
         dispatch_seg(AdaLNOp<false>{x, scale, shift, out, eps}, N, D, stream, st))
         return st;
     GenArgs a{x, nullptr, nullptr, nullptr, scale, shift, nullptr, out, D, eps};
-    row_generic<GenKind::AdaLN><<<generic_grid(N), ref_row_threads(D), 0, stream>>>(a, N);
+    launch(row_generic<GenKind::AdaLN>, generic_grid(N), ref_row_threads(D), 0, stream, a, N);
     return launch_status();
 }
 
@@ -665,7 +671,7 @@ extern "C" int anima_layer_norm_modulate_bf16(const anima_bf16 *x, const anima_b
         dispatch_seg(AdaLNOp<true>{x, scale, shift, out, eps}, N, D, stream, st))
         return st;
     GenArgs a{x, nullptr, nullptr, nullptr, scale, shift, nullptr, out, D, eps};
-    row_generic<GenKind::LnModulate><<<generic_grid(N), ref_row_threads(D), 0, stream>>>(a, N);
+    launch(row_generic<GenKind::LnModulate>, generic_grid(N), ref_row_threads(D), 0, stream, a, N);
     return launch_status();
 }
 
@@ -690,7 +696,7 @@ extern "C" int anima_residual_gate_adaln_bf16(anima_bf16 *hidden, const anima_bf
         dispatch_seg(ResGateAdaLNOp{hidden, sub_out, gate, scale, shift, normed, eps}, N, D, stream, st))
         return st;
     GenArgs a{hidden, hidden, sub_out, gate, scale, shift, nullptr, normed, D, eps};
-    row_generic<GenKind::ResGate><<<generic_grid(N), ref_row_threads(D), 0, stream>>>(a, N);
+    launch(row_generic<GenKind::ResGate>, generic_grid(N), ref_row_threads(D), 0, stream, a, N);
     return launch_status();
 }
 
@@ -708,8 +714,8 @@ extern "C" int anima_rms_norm_bf16(const anima_bf16 *x, const anima_bf16 *weight
         switch (D) {
 #define ANIMA_RMS_SMALL(Dv, Kv)                                                                          \
     case Dv:                                                                                            \
-        if (weight) rms_small<Kv, true><<<grid, kRowBlock, 0, stream>>>(x, weight, out, N, D, eps);       \
-        else rms_small<Kv, false><<<grid, kRowBlock, 0, stream>>>(x, weight, out, N, D, eps);             \
+        if (weight) launch(rms_small<Kv, true>, grid, kRowBlock, 0, stream, x, weight, out, (int64_t)N, D, eps);  \
+        else launch(rms_small<Kv, false>, grid, kRowBlock, 0, stream, x, weight, out, (int64_t)N, D, eps);        \
         break;
             ANIMA_RMS_SMALL(64, 1) ANIMA_RMS_SMALL(128, 2) ANIMA_RMS_SMALL(256, 4)
 #undef ANIMA_RMS_SMALL
@@ -722,7 +728,7 @@ extern "C" int anima_rms_norm_bf16(const anima_bf16 *x, const anima_bf16 *weight
         if (done) return st;
     }
     GenArgs a{x, nullptr, nullptr, nullptr, nullptr, nullptr, weight, out, D, eps};
-    row_generic<GenKind::Rms><<<generic_grid(N), ref_row_threads(D), 0, stream>>>(a, N);
+    launch(row_generic<GenKind::Rms>, generic_grid(N), ref_row_threads(D), 0, stream, a, N);
     return launch_status();
 }
 
@@ -742,7 +748,7 @@ extern "C" int anima_adaln_rms_norm_bf16(const anima_bf16 *x, const anima_bf16 *
         dispatch_seg(AdaRmsOp{x, scale, shift, out, eps}, N, D, stream, st))
         return st;
     GenArgs a{x, nullptr, nullptr, nullptr, scale, shift, nullptr, out, D, eps};
-    row_generic<GenKind::AdaRms><<<generic_grid(N), ref_row_threads(D), 0, stream>>>(a, N);
+    launch(row_generic<GenKind::AdaRms>, generic_grid(N), ref_row_threads(D), 0, stream, a, N);
     return launch_status();
 }
 
@@ -756,6 +762,6 @@ extern "C" int anima_gemma_rms_norm_bf16(const anima_bf16 *x, const anima_bf16 *
     const int64_t n = (int64_t)N * D * 2;
     if (partial_overlap(x, n, out, n)) return ANIMA_ERR_OVERLAP;
     int threads = (D <= 1024) ? ((D + 31) / 32 * 32) : 1024;
-    gemma_rms_generic<<<generic_grid(N), threads, 0, stream>>>(x, weight, out, N, D, eps);
+    launch(gemma_rms_generic, generic_grid(N), threads, 0, stream, x, weight, out, (int64_t)N, D, eps);
     return launch_status();
 }

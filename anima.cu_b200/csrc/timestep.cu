@@ -29,6 +29,7 @@ struct TsArgs {
 };
 
 __global__ void timestep_embedding(TsArgs a) {
+    pdl_wait();
     extern __shared__ __align__(16) __nv_bfloat16 row[];  // [dim]
     __shared__ float red[33];
     const int half = a.dim / 2;
@@ -82,6 +83,6 @@ extern "C" int anima_timestep_embedding_bf16(float timestep, const anima_bf16 *n
     if (smem > 48 * 1024) {
         if (int e = allow_dynamic_smem((const void *)timestep_embedding, 64 * 1024, 2)) return e;
     }
-    timestep_embedding<<<1, ref_row_threads(dim), smem, stream>>>(a);
+    launch(timestep_embedding, 1, ref_row_threads(dim), smem, stream, a);
     return launch_status();
 }
