@@ -47,8 +47,6 @@ __device__ __forceinline__ float resid_sq_pair(float h0, float h1) { return fmaf
 // conflicts. Broadcast vectors (1+scale, shift, gate, weight) are converted to fp32 once
 // per CTA into shared memory (swizzled per segment the same way).
 
-constexpr int kSegWarps = 4;
-constexpr int kSegThreads = kSegWarps * 32;
 constexpr int kUnitChunks = 256;  // 16-byte chunks per input per unit (4 KB)
 
 __device__ __forceinline__ int swz(int c) { return (c & ~7) | ((c & 7) ^ ((c >> 3) & 7)); }
@@ -59,10 +57,16 @@ __device__ __forceinline__ int bc_pos(int d) {
     return ((s << 4) + (j ^ (s & 7))) * 4 + (d & 3);
 }
 
+// CTA size, ring depth and occupancy target per number of streamed inputs: one-input ops
+// run 2 CTAs of 8 warps per SM with 3 slots per warp (192 KB of rows in flight, at most 128
+// registers per thread); two- and three-input ops 2 CTAs of 4 warps with 2 slots.
 template <int NIN>
 struct SegShape {
+    static constexpr int kWarps = NIN == 1 ? 8 : 4;
+    static constexpr int kThreads = kWarps * 32;
     static constexpr int kStages = NIN == 1 ? 3 : 2;
-    static constexpr int kRingBytes = kSegWarps * kStages * NIN * kUnitChunks * 16;
+    static constexpr int kMinCtas = 2;
+    static constexpr int kRingBytes = kWarps * kStages * NIN * kUnitChunks * 16;
 };
 
 __device__ __forceinline__ void cp_async16(void *smem, const void *gmem) {
@@ -346,11 +350,13 @@ struct AdaRmsOp {  // adaln.cu:11-58 (per-row scale/shift streamed alongside x)
 };
 
 template <int NW, class Op>
-__global__ void __launch_bounds__(kSegThreads) row_seg(Op op, int64_t N, int D) {
+__global__ void __launch_bounds__(SegShape<Op::NIN>::kThreads, SegShape<Op::NIN>::kMinCtas)
+    row_seg(Op op, int64_t N, int D) {
     pdl_wait();
     constexpr int NIN = Op::NIN, NOUT = Op::NOUT, NB = Op::NB;
     constexpr int G = 32 / NW;  // rows per unit
     constexpr int NST = SegShape<NIN>::kStages;
+    constexpr int kSegWarps = SegShape<NIN>::kWarps, kSegThreads = SegShape<NIN>::kThreads;
     constexpr int kRowChunks = NW * 8;
     extern __shared__ __align__(16) unsigned char seg_smem[];
     float *bc = reinterpret_cast<float *>(seg_smem);
@@ -582,6 +588,7 @@ int launch_seg(const Op &op, int64_t N, int D, cudaStream_t s) {
     const int smem = Op::NB * D * 4 + SegShape<Op::NIN>::kRingBytes;
     auto kern = row_seg<NW, Op>;
     int err = ANIMA_OK;
+    constexpr int kSegWarps = SegShape<Op::NIN>::kWarps, kSegThreads = SegShape<Op::NIN>::kThreads;
     const int per_sm = resident_ctas((const void *)kern, kSegThreads, smem, &err);
     if (per_sm <= 0) return err != ANIMA_OK ? err : ANIMA_ERR_NO_DEVICE;
     constexpr int G = 32 / NW;
