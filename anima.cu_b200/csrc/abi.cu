@@ -78,6 +78,15 @@ int resident_ctas(const void *kernel, int block, int smem, int *err) {
     return n;
 }
 
+unsigned wave_grid(const void *kernel, int block, int smem, int64_t work, int *err) {
+    const int per_sm = resident_ctas(kernel, block, smem, err);
+    if (*err) return 0;
+    int64_t blocks = (work + block - 1) / block;
+    const int64_t wave = (int64_t)per_sm * sm_count();
+    if (blocks > wave) blocks = wave;
+    return (unsigned)(blocks < 1 ? 1 : blocks);
+}
+
 }  // namespace anima
 
 extern "C" const char *anima_status_string(int status) {

@@ -147,10 +147,10 @@ int channel_norm(const anima_bf16 *x, const anima_bf16 *gamma, anima_bf16 *out, 
         launch(kern, (unsigned)tiles, kCnBlock, (size_t)smem, stream, a);
     } else {
         const int64_t pixels = (int64_t)B * spatial;
-        int64_t blocks = (pixels + 255) / 256;
-        const int64_t wave = (int64_t)sm_count() * 8;
-        if (blocks > wave) blocks = wave;
-        launch(channel_norm_serial<kSilu>, (unsigned)blocks, 256, 0, stream, a, pixels);
+        int err = ANIMA_OK;
+        const unsigned blocks = wave_grid((const void *)channel_norm_serial<kSilu>, 256, 0, pixels, &err);
+        if (err) return err;
+        launch(channel_norm_serial<kSilu>, blocks, 256, 0, stream, a, pixels);
     }
     return launch_status();
 }

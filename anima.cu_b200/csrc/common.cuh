@@ -210,6 +210,11 @@ int allow_dynamic_smem(const void *kernel, int bytes, int slot);
 // and stores the status in *err.
 int resident_ctas(const void *kernel, int block, int smem, int *err);
 
+// CTAs for a grid-stride kernel: enough for `work` items at one per thread, but at most one
+// resident wave (SMs x the CTAs of `kernel` that fit on one SM together), so no CTA waits
+// for a second wave. On failure returns 0 and stores the status in *err.
+unsigned wave_grid(const void *kernel, int block, int smem, int64_t work, int *err);
+
 inline bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 inline bool aligned_to(const void *p, unsigned a) {
     return (reinterpret_cast<uintptr_t>(p) & (a - 1)) == 0;

@@ -160,11 +160,10 @@ int launch_ew(const EwArgs &a, cudaStream_t stream) {
     if (a.n <= 0) return ANIMA_OK;
     constexpr int U = Op::NS > 1 ? 2 : 4;
     const int64_t work = a.vec ? ((a.n >> 3) + U - 1) / U : a.n;
-    int64_t blocks = (work + kEwBlock - 1) / kEwBlock;
-    const int64_t wave = (int64_t)sm_count() * (2048 / kEwBlock);
-    if (blocks > wave) blocks = wave;
-    if (blocks < 1) blocks = 1;
-    launch(ew_kernel<Op, U>, (unsigned)blocks, kEwBlock, 0, stream, a, Op{});
+    int err = ANIMA_OK;
+    const unsigned blocks = wave_grid((const void *)ew_kernel<Op, U>, kEwBlock, 0, work, &err);
+    if (err) return err;
+    launch(ew_kernel<Op, U>, blocks, kEwBlock, 0, stream, a, Op{});
     return launch_status();
 }
 
@@ -172,19 +171,28 @@ int launch_ew(const EwArgs &a, cudaStream_t stream) {
 //
 // The reference formulas (tanhf, expf and an IEEE divide per element) cost ~25
 // instructions per element, which makes them issue-bound on B200 rather than
-// memory-bound. Here each element is first evaluated with hardware approximations --
-// tanh(u) = 1 - 2/(1 + 2^(2u*log2 e)) and sigma(x) = 1/(1 + 2^(-x*log2 e)) with
-// ex2.approx and rcp.approx -- whose distance from the reference's fp32 result is
-// bounded (below). If the whole interval [r - delta, r + delta] rounds to a single bf16
-// value, that value is the reference's bf16 output; otherwise (about 1% of N(0,1) inputs
-// for GELU, mostly x < -2 where 1 + tanh cancels, and ~0.1% for SiLU) the element takes
-// the reference formula itself. The outputs are therefore the reference's bit for bit;
-// the tests check all 65536 bf16 inputs of both functions.
+// memory-bound. Here each element is first evaluated with hardware approximations
+// (ex2.approx, rcp.approx) in a form without cancellation:
+//   GELU: x/2 (1 + tanh u) = x * sigma(2u) = x / (1 + 2^(-2u log2 e)),
+//   SiLU: x * sigma(x)     = x / (1 + 2^(-x log2 e)),
+// and bracketed by an interval [a, b] that provably contains the reference's fp32 result.
+// If a and b round to the same bf16 value, that value is the reference's bf16 output;
+// otherwise (about 0.1% of N(0,1) inputs, mostly GELU at x < -2.5 where the reference's
+// 1 + tanhf(u) cancels) the element takes the reference formula itself. The outputs are
+// therefore the reference's bit for bit; the tests check all 65536 bf16 inputs.
 //
-// Bounds. GELU: |t_fast - tanhf(u)| <= 2^-21 (ex2/rcp relative errors near 2^-22, the
-// rounding of the exponent argument damped by q(1-q)) plus 2 ulp for tanhf's own error,
-// so |r_fast - r_ref| <= |x/2| (2^-21 + 2^-22) + ulp(r) < 2^-19 |x/2|; delta = 2^-18 |x/2|.
-// SiLU: no cancellation, |r_fast - r_ref| <= 2^-20 |r|; delta = 2^-18 |r|.
+// Bounds. x sigma_fast carries a relative error below 2^-21 + (1 - sigma) |z| 2^-22.4:
+// ex2 and rcp near 2^-22 each, three fp32 roundings, and the rounding of the exponent
+// argument z (three roundings from the reference's u), which moves 2^z by |z| 2^-22.4
+// relative and reaches sigma damped by 1 - sigma.
+// GELU, z = -2u log2 e: the reference's tanhf is within 2 ulp (<= 2^-23 absolute), so its
+// fma(x/2, t, x/2) lies within |x| 2^-24 + |r| 2^-24 of x sigma(2u). The interval
+// r (1 +- 2^-19) +- |x| 2^-23 holds it: the argument term stays below 2^-20 up to |u| = 4,
+// and beyond, sigma(2u) < 3e-4 makes it negligible against |x| 2^-24 (u < 0) or the
+// damping does (u > 0).
+// SiLU, z = -x log2 e: no cancellation; the reference (expf within 2 ulp, an IEEE divide)
+// and the fast value each stay within 2^-21 + |x| 2^-24 of x sigma(x), so the interval
+// r +- |r| (2^-19 + |x| 2^-23) holds the reference's result.
 
 __device__ __forceinline__ float ex2_fast(float x) {
     float y;
@@ -196,127 +204,142 @@ __device__ __forceinline__ float rcp_fast(float x) {
     asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
     return y;
 }
-
-template <class F>
-__device__ __noinline__ uint32_t exact_bf16(uint32_t b) {  // the reference formula, out of line
-    const __nv_bfloat16 r = __float2bfloat16_rn(F::f(__uint_as_float(b << 16)));
-    return *reinterpret_cast<const uint16_t *>(&r);
-}
+__device__ __forceinline__ float2 f2(float v) { return make_float2(v, v); }
 
 struct GeluF {
     __device__ static float f(float v) { return gelu_tanh_f(v); }
-    // fast value of two elements and the half-width of their uncertainty
-    __device__ static void fast(float2 v, float2 &r, float2 &delta) {
-        const float2 c2 = make_float2(0.044715f, 0.044715f), c1 = make_float2(0.7978845608028654f, 0.7978845608028654f);
-        const float2 vsq = __fmul2_rn(v, v);
-        const float2 inner = __fmul2_rn(c1, __ffma2_rn(__fmul2_rn(c2, vsq), v, v));  // as gelu.cu:28
-        const float2 hv = __fmul2_rn(make_float2(0.5f, 0.5f), v);
-        const float2 z = __fmul2_rn(inner, make_float2(2.8853900817779268f, 2.8853900817779268f));  // 2 log2(e)
-        const float2 d = __fadd2_rn(make_float2(ex2_fast(z.x), ex2_fast(z.y)), make_float2(1.0f, 1.0f));
-        const float2 t = __ffma2_rn(make_float2(rcp_fast(d.x), rcp_fast(d.y)), make_float2(-2.0f, -2.0f),
-                                    make_float2(1.0f, 1.0f));
-        r = __ffma2_rn(hv, t, hv);
-        delta = __fmul2_rn(hv, make_float2(0x1p-18f, 0x1p-18f));
+    // Two elements: both ends of the interval that holds each reference fp32 result.
+    __device__ static void fast(float2 v, float2 &a, float2 &b) {
+        // -2 log2(e) * u with u = sqrt(2/pi) (x + 0.044715 x^3), the polynomial as gelu.cu:27-28
+        const float2 p = __ffma2_rn(__fmul2_rn(f2(0.044715f), __fmul2_rn(v, v)), v, v);
+        const float2 z = __fmul2_rn(p, f2(-0x1.26aec2p+1f));  // -2 log2(e) * 0.7978845608f
+        const float2 d = __fadd2_rn(make_float2(ex2_fast(z.x), ex2_fast(z.y)), f2(1.0f));
+        // x sigma(2u); adding +0 turns -0 into +0 as the reference's fma(-0, -0, -0) does
+        const float2 r = __ffma2_rn(v, make_float2(rcp_fast(d.x), rcp_fast(d.y)), f2(0.0f));
+        // r and x share a sign, so r c + x e and r c' - x e are the interval's two ends
+        a = __ffma2_rn(r, f2(1.0f + 0x1p-19f), __fmul2_rn(v, f2(0x1p-23f)));
+        b = __ffma2_rn(r, f2(1.0f - 0x1p-19f), __fmul2_rn(v, f2(-0x1p-23f)));
     }
 };
 
 struct SiluF {
     __device__ static float f(float v) { return silu_f(v); }
-    __device__ static void fast(float2 v, float2 &r, float2 &delta) {
-        const float2 z = __fmul2_rn(v, make_float2(-1.4426950408889634f, -1.4426950408889634f));  // -log2(e)
-        const float2 d = __fadd2_rn(make_float2(ex2_fast(z.x), ex2_fast(z.y)), make_float2(1.0f, 1.0f));
-        r = __fmul2_rn(v, make_float2(rcp_fast(d.x), rcp_fast(d.y)));
-        delta = __fmul2_rn(r, make_float2(0x1p-18f, 0x1p-18f));
+    __device__ static void fast(float2 v, float2 &a, float2 &b) {
+        const float2 z = __fmul2_rn(v, f2(-1.4426950408889634f));  // -log2(e)
+        const float2 d = __fadd2_rn(make_float2(ex2_fast(z.x), ex2_fast(z.y)), f2(1.0f));
+        const float2 r = __fmul2_rn(v, make_float2(rcp_fast(d.x), rcp_fast(d.y)));
+        // r +- r (2^-19 + |x| 2^-23): the rounding of the exponent argument grows with |x|.
+        // A zero r (x < -87, where rcp.approx flushes a subnormal 1/d) gives the ends -0
+        // and +0, which never pass as decided.
+        const float2 ax = make_float2(fabsf(v.x), fabsf(v.y));
+        const float2 dl = __fmul2_rn(r, __ffma2_rn(ax, f2(0x1p-23f), f2(0x1p-19f)));
+        a = __fadd2_rn(r, dl);
+        b = __fadd2_rn(r, make_float2(-dl.x, -dl.y));
     }
 };
 
-// GELU, the reference formula itself on eight elements, with the polynomial and the
-// final fma as packed fp32x2 operations (each lane rounds exactly like the scalar op of
-// gelu.cu:27-30); only tanhf stays scalar. The ~1% of GELU inputs the fast-path test
-// above cannot decide (x < -2, where 1 + tanh cancels) make that path lose to this one.
-__device__ __forceinline__ Vec8 gelu_exact_chunk(const Vec8 &v) {
-    const float2 c2 = make_float2(0.044715f, 0.044715f), c1 = make_float2(0.7978845608028654f, 0.7978845608028654f);
-    Vec8 o;
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-        const float2 x = make_float2(bf_lo(v.w[j]), bf_hi(v.w[j]));
-        const float2 inner = __fmul2_rn(c1, __ffma2_rn(__fmul2_rn(c2, __fmul2_rn(x, x)), x, x));
-        const float2 hv = __fmul2_rn(make_float2(0.5f, 0.5f), x);
-        const float2 r = __ffma2_rn(hv, make_float2(tanhf(inner.x), tanhf(inner.y)), hv);
-        o.w[j] = pack_bf2(r.x, r.y);
-    }
-    return o;
+template <class F>
+__device__ __forceinline__ uint32_t exact_bits(uint32_t b) {  // the reference formula on bf16 bits
+    const __nv_bfloat16 r = __float2bfloat16_rn(F::f(__uint_as_float(b << 16)));
+    return *reinterpret_cast<const uint16_t *>(&r);
+}
+
+template <class F>
+__device__ __noinline__ uint32_t exact_bf16(uint32_t b) {  // out of line, for the ragged tail
+    return exact_bits<F>(b);
 }
 
 // One 16-byte chunk: eight bf16 inputs -> eight bf16 outputs equal to bf16(F::f(x)).
 template <class F>
 __device__ __forceinline__ Vec8 fast_chunk(const Vec8 &v) {
-    Vec8 o;
-    uint32_t miss = 0;
+    Vec8 o, alt;
+    uint32_t diff = 0;
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
-        float2 r, dl;
-        F::fast(make_float2(bf_lo(v.w[j]), bf_hi(v.w[j])), r, dl);
-        const float2 hi = __fadd2_rn(r, dl), lo = __fadd2_rn(r, make_float2(-dl.x, -dl.y));
-        const uint32_t p0 = pack_bf2(hi.x, lo.x), p1 = pack_bf2(hi.y, lo.y);
-        miss |= ((p0 ^ (p0 >> 16)) & 0xffffu ? 1u : 0u) << (2 * j);
-        miss |= ((p1 ^ (p1 >> 16)) & 0xffffu ? 1u : 0u) << (2 * j + 1);
-        o.w[j] = __byte_perm(p0, p1, 0x5410);  // low halves of p0 and p1
+        float2 a, b;
+        F::fast(make_float2(bf_lo(v.w[j]), bf_hi(v.w[j])), a, b);
+        o.w[j] = pack_bf2(a.x, a.y);
+        alt.w[j] = pack_bf2(b.x, b.y);
+        diff |= o.w[j] ^ alt.w[j];
     }
-    // Undecided elements: each lane walks only its own misses (usually none or one), so
-    // the warp runs the reference formula max-misses-per-lane times.
-    uint32_t out[8];
+    if (diff) {
+        // Rare: elements whose interval holds a bf16 rounding boundary. Each lane walks only
+        // its own (usually one), with one inlined copy of the reference formula; words are
+        // picked by selects so that nothing is indexed at run time.
+        uint32_t miss = 0;
 #pragma unroll
-    for (int e = 0; e < 8; ++e) out[e] = e & 1 ? o.w[e >> 1] >> 16 : o.w[e >> 1] & 0xffffu;
-    while (miss) {
-        const int e = __ffs(miss) - 1;
-        miss &= miss - 1;
-        const uint32_t w = v.w[e >> 1];
-        const __nv_bfloat16 r = __float2bfloat16_rn(F::f(e & 1 ? bf_hi(w) : bf_lo(w)));
-        const uint32_t rb = *reinterpret_cast<const uint16_t *>(&r);
+        for (int j = 0; j < 4; ++j) {
+            const uint32_t d = o.w[j] ^ alt.w[j];
+            miss |= (d & 0xffffu ? 1u : 0u) << (2 * j) | (d >> 16 ? 1u : 0u) << (2 * j + 1);
+        }
+        while (miss) {
+            const int e = __ffs(miss) - 1;
+            miss &= miss - 1;
+            const int j = e >> 1;
+            const uint32_t w = j == 0 ? v.w[0] : j == 1 ? v.w[1] : j == 2 ? v.w[2] : v.w[3];
+            const uint32_t r = exact_bits<F>(e & 1 ? w >> 16 : w & 0xffffu);
 #pragma unroll
-        for (int k = 0; k < 8; ++k) out[k] = k == e ? rb : out[k];
+            for (int k = 0; k < 4; ++k)
+                if (k == j) o.w[k] = e & 1 ? (o.w[k] & 0xffffu) | (r << 16) : (o.w[k] & 0xffff0000u) | r;
+        }
     }
-#pragma unroll
-    for (int j = 0; j < 4; ++j) o.w[j] = out[2 * j] | (out[2 * j + 1] << 16);
     return o;
+}
+
+// U chunks per thread and group, groups grid-strided; the next group's loads are issued
+// before the current group is computed, so every thread keeps U 16-byte loads in flight.
+template <int U, int NS>
+__device__ __forceinline__ void load_group(Vec8 (&in)[U][NS], const EwArgs &a, int64_t base, int64_t stride,
+                                           int64_t nch) {
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+        const int64_t i = base + u * stride;
+        if (i < nch) {
+            in[u][0] = ld_stream(a.s0 + i * 8);
+            if constexpr (NS > 1) in[u][1] = ld_stream(a.s1 + i * 8);
+        }
+    }
+}
+
+template <class F, int U, int NS>
+__device__ __forceinline__ void act_group(const Vec8 (&in)[U][NS], const EwArgs &a, int64_t base, int64_t stride,
+                                          int64_t nch) {
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+        const int64_t i = base + u * stride;
+        if (i >= nch) break;
+        Vec8 o = fast_chunk<F>(in[u][0]);
+        if constexpr (NS > 1) {  // elementwise.cu:138-140: product of the bf16 silu value and up
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const uint32_t uw = in[u][1].w[j];
+                const float2 p = __fmul2_rn(make_float2(bf_lo(o.w[j]), bf_hi(o.w[j])), make_float2(bf_lo(uw), bf_hi(uw)));
+                o.w[j] = pack_bf2(p.x, p.y);
+            }
+        }
+        st_vec(a.out + i * 8, o);
+    }
 }
 
 // NS = 1: out = F(x). NS = 2 (SwiGLU): out = bf16(F(gate)) * up, as silu_bf16 then mul_bf16.
 template <class F, int NS>
-__global__ void __launch_bounds__(kEwBlock) fast_act_kernel(EwArgs a) {
+__global__ void __launch_bounds__(kEwBlock, NS == 1 ? 4 : 2) fast_act_kernel(EwArgs a) {
     pdl_wait();
     constexpr int U = 4;
     const int64_t tid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     const int64_t stride = (int64_t)gridDim.x * blockDim.x;
     const int64_t nch = a.vec ? a.n >> 3 : 0;
-    for (int64_t base = tid; base < nch; base += stride * U) {
-        Vec8 in[U][NS];
-#pragma unroll
-        for (int u = 0; u < U; ++u) {
-            const int64_t i = base + u * stride;
-            if (i < nch) {
-                in[u][0] = ld_stream(a.s0 + i * 8);
-                if constexpr (NS > 1) in[u][1] = ld_stream(a.s1 + i * 8);
-            }
-        }
-#pragma unroll
-        for (int u = 0; u < U; ++u) {
-            const int64_t i = base + u * stride;
-            if (i >= nch) break;
-            Vec8 o;
-            if constexpr (std::is_same<F, GeluF>::value) o = gelu_exact_chunk(in[u][0]);
-            else o = fast_chunk<F>(in[u][0]);
-            if constexpr (NS > 1) {  // elementwise.cu:138-140: product of the bf16 silu value and up
-#pragma unroll
-                for (int j = 0; j < 4; ++j) {
-                    const uint32_t uw = in[u][1].w[j];
-                    const float2 p = __fmul2_rn(make_float2(bf_lo(o.w[j]), bf_hi(o.w[j])), make_float2(bf_lo(uw), bf_hi(uw)));
-                    o.w[j] = pack_bf2(p.x, p.y);
-                }
-            }
-            st_vec(a.out + i * 8, o);
-        }
+    Vec8 x0[U][NS], x1[U][NS];
+    const int64_t step = stride * U;
+    load_group<U, NS>(x0, a, tid, stride, nch);
+    for (int64_t base = tid; base < nch;) {  // unrolled by two so the buffers alternate without copies
+        load_group<U, NS>(x1, a, base + step, stride, nch);
+        act_group<F, U, NS>(x0, a, base, stride, nch);
+        base += step;
+        if (base >= nch) break;
+        load_group<U, NS>(x0, a, base + step, stride, nch);
+        act_group<F, U, NS>(x1, a, base, stride, nch);
+        base += step;
     }
     pdl_launch();
     for (int64_t e = (nch << 3) + tid; e < a.n; e += stride) {
@@ -334,11 +357,10 @@ template <class F, int NS>
 int launch_fast_act(const EwArgs &a, cudaStream_t stream) {
     if (a.n <= 0) return ANIMA_OK;
     const int64_t work = a.vec ? ((a.n >> 3) + 3) / 4 : a.n;
-    int64_t blocks = (work + kEwBlock - 1) / kEwBlock;
-    const int64_t wave = (int64_t)sm_count() * (2048 / kEwBlock);
-    if (blocks > wave) blocks = wave;
-    if (blocks < 1) blocks = 1;
-    launch(fast_act_kernel<F, NS>, (unsigned)blocks, kEwBlock, 0, stream, a);
+    int err = ANIMA_OK;
+    const unsigned blocks = wave_grid((const void *)fast_act_kernel<F, NS>, kEwBlock, 0, work, &err);
+    if (err) return err;
+    launch(fast_act_kernel<F, NS>, blocks, kEwBlock, 0, stream, a);
     return launch_status();
 }
 

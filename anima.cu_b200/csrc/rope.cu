@@ -235,13 +235,6 @@ __global__ void __launch_bounds__(kRopeBlock) qk_norm_rope_128(QkArgs a) {
     st_vec(p + 64, pack8(o1));
 }
 
-unsigned grid_for(int64_t work, int block) {
-    int64_t blocks = (work + block - 1) / block;
-    const int64_t wave = (int64_t)sm_count() * (2048 / block);
-    if (blocks > wave) blocks = wave;
-    return (unsigned)(blocks < 1 ? 1 : blocks);
-}
-
 bool bf16_ok(const void *p) { return aligned_to(p, 2); }
 
 }  // namespace
@@ -265,10 +258,16 @@ extern "C" int anima_rope_cosmos_strided_bf16(anima_bf16 *x, const anima_bf16 *c
         return ANIMA_ERR_OVERLAP;
     if (HD % 16 == 0 && aligned16(x) && aligned16(cos_table) && aligned16(sin_table)) {
         CosmosArgs a{x, cos_table, sin_table, S, H, HD, rows * H * (HD / 16), (uint32_t)(HD / 16)};
-        launch(rope_cosmos_vec, grid_for((a.units + kRopeU - 1) / kRopeU, kRopeBlock), kRopeBlock, 0, stream, a);
+        int err = ANIMA_OK;
+        const unsigned grid = wave_grid((const void *)rope_cosmos_vec, kRopeBlock, 0, (a.units + kRopeU - 1) / kRopeU, &err);
+        if (err) return err;
+        launch(rope_cosmos_vec, grid, kRopeBlock, 0, stream, a);
     } else {
         const int64_t pairs = rows * H * (HD / 2);
-        launch(rope_cosmos_scalar, grid_for(pairs, kRopeBlock), kRopeBlock, 0, stream, x, cos_table, sin_table, S, H, HD, pairs);
+        int err = ANIMA_OK;
+        const unsigned grid = wave_grid((const void *)rope_cosmos_scalar, kRopeBlock, 0, pairs, &err);
+        if (err) return err;
+        launch(rope_cosmos_scalar, grid, kRopeBlock, 0, stream, x, cos_table, sin_table, S, H, HD, pairs);
     }
     return launch_status();
 }
@@ -281,10 +280,16 @@ extern "C" int anima_rope_standard_bf16(anima_bf16 *x, const float *cos_table, c
     if (!bf16_ok(x) || !aligned_to(cos_table, 4) || !aligned_to(sin_table, 4)) return ANIMA_ERR_MISALIGNED;
     if (D % 16 == 0 && aligned16(x) && aligned16(cos_table) && aligned16(sin_table)) {
         StdArgs a{x, cos_table, sin_table, T, D, (int64_t)total_rows * (D / 16), (uint32_t)(D / 16)};
-        launch(rope_standard_vec, grid_for((a.units + kRopeU - 1) / kRopeU, kRopeBlock), kRopeBlock, 0, stream, a);
+        int err = ANIMA_OK;
+        const unsigned grid = wave_grid((const void *)rope_standard_vec, kRopeBlock, 0, (a.units + kRopeU - 1) / kRopeU, &err);
+        if (err) return err;
+        launch(rope_standard_vec, grid, kRopeBlock, 0, stream, a);
     } else {
         const int64_t pairs = (int64_t)total_rows * (D / 2);
-        launch(rope_standard_scalar, grid_for(pairs, kRopeBlock), kRopeBlock, 0, stream, x, cos_table, sin_table, T, D, pairs);
+        int err = ANIMA_OK;
+        const unsigned grid = wave_grid((const void *)rope_standard_scalar, kRopeBlock, 0, pairs, &err);
+        if (err) return err;
+        launch(rope_standard_scalar, grid, kRopeBlock, 0, stream, x, cos_table, sin_table, T, D, pairs);
     }
     return launch_status();
 }
