@@ -215,7 +215,7 @@ int resident_ctas(const void *kernel, int block, int smem, int *err);
 // for a second wave. On failure returns 0 and stores the status in *err.
 unsigned wave_grid(const void *kernel, int block, int smem, int64_t work, int *err);
 
-inline bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+__host__ __device__ inline bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 inline bool aligned_to(const void *p, unsigned a) {
     return (reinterpret_cast<uintptr_t>(p) & (a - 1)) == 0;
 }

@@ -57,15 +57,14 @@ __device__ __forceinline__ int bc_pos(int d) {
     return ((s << 4) + (j ^ (s & 7))) * 4 + (d & 3);
 }
 
-// CTA size, ring depth and occupancy target per number of streamed inputs: one-input ops
-// run 2 CTAs of 8 warps per SM with 3 slots per warp (192 KB of rows in flight, at most 128
-// registers per thread); two- and three-input ops 2 CTAs of 4 warps with 2 slots.
+// CTA size, ring depth and occupancy target: 4 warps with 2 slots each; one-input ops run 4
+// CTAs per SM (at most 128 registers per thread), two- and three-input ops 2.
 template <int NIN>
 struct SegShape {
-    static constexpr int kWarps = NIN == 1 ? 8 : 4;
+    static constexpr int kWarps = 4;
     static constexpr int kThreads = kWarps * 32;
-    static constexpr int kStages = NIN == 1 ? 3 : 2;
-    static constexpr int kMinCtas = 2;
+    static constexpr int kStages = 2;
+    static constexpr int kMinCtas = NIN == 1 ? 4 : 2;
     static constexpr int kRingBytes = kWarps * kStages * NIN * kUnitChunks * 16;
 };
 
@@ -77,22 +76,34 @@ __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commi
 template <int N>
 __device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
 
-// The reference warp's shfl_down tree over the 32 pairs of one segment, in registers.
-// p(k, j) is pair 4k+j (chunk k, pair j of the chunk).
-template <class PairFn>
-__device__ __forceinline__ float seg_tree(PairFn p) {
-    float a[16];
+// The reference warp's shfl_down tree over the 32 pairs of one segment, in registers, as
+// packed fp32x2 adds (each lane of FADD2 rounds like the scalar add, so the sums are the
+// reference's bit for bit at half the instructions). q(k, h) returns pairs 4k+2h and
+// 4k+2h+1 (chunk k, words 2h and 2h+1). With scalar a_s[4k+2h+t] = a[2k+h].t, each level
+// below adds exactly the pairs the reference's offset adds.
+template <class PairFn2>
+__device__ __forceinline__ float seg_tree(PairFn2 q) {
+    float2 a[8], b[4], c[2];
 #pragma unroll
     for (int k = 0; k < 4; ++k)
 #pragma unroll
-        for (int j = 0; j < 4; ++j) a[4 * k + j] = p(k, j) + p(k + 4, j);  // offset 16
-    float b[8], c[4];
+        for (int h = 0; h < 2; ++h) a[2 * k + h] = __fadd2_rn(q(k, h), q(k + 4, h));  // offset 16
 #pragma unroll
-    for (int r = 0; r < 8; ++r) b[r] = a[r] + a[r + 8];                  // offset 8
+    for (int i = 0; i < 4; ++i) b[i] = __fadd2_rn(a[i], a[i + 4]);                    // offset 8
 #pragma unroll
-    for (int r = 0; r < 4; ++r) c[r] = b[r] + b[r + 4];                  // offset 4
-    const float d0 = c[0] + c[2], d1 = c[1] + c[3];                      // offset 2
-    return d0 + d1;                                                      // offset 1
+    for (int i = 0; i < 2; ++i) c[i] = __fadd2_rn(b[i], b[i + 2]);                    // offset 4
+    const float2 d = __fadd2_rn(c[0], c[1]);                                           // offset 2
+    return d.x + d.y;                                                                  // offset 1
+}
+
+// Words 2h, 2h+1 of a chunk as (low elements) and (high elements).
+__device__ __forceinline__ float2 lo2(const Vec8 &v, int h) { return make_float2(bf_lo(v.w[2 * h]), bf_lo(v.w[2 * h + 1])); }
+__device__ __forceinline__ float2 hi2(const Vec8 &v, int h) { return make_float2(bf_hi(v.w[2 * h]), bf_hi(v.w[2 * h + 1])); }
+
+// Pair sums of squares fmaf(b, b, a*a) (nvcc's contraction of the reference's a*a + b*b).
+__device__ __forceinline__ float2 sq_pairs(const Vec8 &v, int h) {
+    const float2 a = lo2(v, h), b = hi2(v, h);
+    return __ffma2_rn(b, b, __fmul2_rn(a, a));
 }
 
 // The reference's second level: warp 0 reduces the NW per-warp sums, zero-padded to 32.
@@ -107,11 +118,8 @@ __device__ __forceinline__ float seg_cross(float v) {
 
 // Sum and sum of squares of a plain bf16 segment (pair values: v0+v1, round(v0^2+v1^2)).
 __device__ __forceinline__ void seg_stats(const Vec8 (&v)[8], float &sum, float &sq) {
-    sum = seg_tree([&](int k, int j) { return bf_lo(v[k].w[j]) + bf_hi(v[k].w[j]); });
-    sq = seg_tree([&](int k, int j) {
-        const float a = bf_lo(v[k].w[j]), b = bf_hi(v[k].w[j]);
-        return fmaf(b, b, a * a);
-    });
+    sum = seg_tree([&](int k, int h) { return __fadd2_rn(lo2(v[k], h), hi2(v[k], h)); });
+    sq = seg_tree([&](int k, int h) { return sq_pairs(v[k], h); });
 }
 
 __device__ __forceinline__ void load_seg(const Vec8 *buf, int lane, Vec8 (&v)[8]) {
@@ -160,7 +168,6 @@ struct LayerNormOp {  // layer_norm.cu:26-59
     float eps;
     __device__ const anima_bf16 *src(int) const { return x; }
     __device__ anima_bf16 *dst(int) const { return out; }
-    __device__ void load_bcast(float *, int, int) const {}
     template <int NW>
     __device__ void segment(Vec8 *slot, const float *, int lane, int, int D) const {
         Vec8 v[8];
@@ -195,10 +202,8 @@ struct AdaLNOp {
     float eps;
     __device__ const anima_bf16 *src(int) const { return x; }
     __device__ anima_bf16 *dst(int) const { return out; }
-    __device__ void load_bcast(float *bc, int d, int D) const {
-        bc[bc_pos(d)] = 1.0f + bf(scale, d);  // the reference's (1.0f + s) is exact to fp32 rounding
-        bc[D + bc_pos(d)] = bf(shift, d);
-    }
+    static constexpr unsigned kPlusOne = 1u;  // the reference's (1.0f + scale[d]), rounded to fp32
+    __device__ const anima_bf16 *bvec(int i) const { return i == 0 ? scale : shift; }
     template <int NW>
     __device__ void segment(Vec8 *slot, const float *bc, int lane, int seg, int D) const {
         Vec8 v[8];
@@ -229,11 +234,8 @@ struct ResGateAdaLNOp {  // layer_norm.cu:146-196
     float eps;
     __device__ const anima_bf16 *src(int i) const { return i == 0 ? hidden : sub_out; }
     __device__ anima_bf16 *dst(int o) const { return o == 0 ? hidden : normed; }
-    __device__ void load_bcast(float *bc, int d, int D) const {
-        bc[bc_pos(d)] = bf(gate, d);
-        bc[D + bc_pos(d)] = 1.0f + bf(scale, d);
-        bc[2 * D + bc_pos(d)] = bf(shift, d);
-    }
+    static constexpr unsigned kPlusOne = 2u;
+    __device__ const anima_bf16 *bvec(int i) const { return i == 0 ? gate : (i == 1 ? scale : shift); }
     template <int NW>
     __device__ void segment(Vec8 *slot, const float *bc, int lane, int seg, int D) const {
         Vec8 x[8], y[8];
@@ -255,8 +257,14 @@ struct ResGateAdaLNOp {  // layer_norm.cu:146-196
                 h[k][e + 1] = hv.y;
             }
         }
-        float sum = seg_tree([&](int k, int j) { return h[k][2 * j] + h[k][2 * j + 1]; });
-        float sq = seg_tree([&](int k, int j) { return resid_sq_pair(h[k][2 * j], h[k][2 * j + 1]); });
+        // pairs (h[k][4i], h[k][4i+1]) and (h[k][4i+2], h[k][4i+3]); resid_sq_pair packed
+        float sum = seg_tree([&](int k, int i) {
+            return __fadd2_rn(f2(h[k][4 * i], h[k][4 * i + 2]), f2(h[k][4 * i + 1], h[k][4 * i + 3]));
+        });
+        float sq = seg_tree([&](int k, int i) {
+            const float2 h0 = f2(h[k][4 * i], h[k][4 * i + 2]), h1 = f2(h[k][4 * i + 1], h[k][4 * i + 3]);
+            return __ffma2_rn(h0, h0, __fmul2_rn(h1, h1));
+        });
         sum = seg_cross<NW>(sum);
         sq = seg_cross<NW>(sq);
         const float mean = __fdiv_rn(sum, (float)D);
@@ -283,17 +291,13 @@ struct RmsOp {  // rms_norm.cu:9-67
     float eps;
     __device__ const anima_bf16 *src(int) const { return x; }
     __device__ anima_bf16 *dst(int) const { return out; }
-    __device__ void load_bcast(float *bc, int d, int) const {
-        if constexpr (kWeight) bc[bc_pos(d)] = bf(weight, d);
-    }
+    static constexpr unsigned kPlusOne = 0u;
+    __device__ const anima_bf16 *bvec(int) const { return weight; }
     template <int NW>
     __device__ void segment(Vec8 *slot, const float *bc, int lane, int seg, int D) const {
         Vec8 v[8];
         load_seg(slot, lane, v);
-        float sq = seg_tree([&](int k, int j) {
-            const float a = bf_lo(v[k].w[j]), b = bf_hi(v[k].w[j]);
-            return fmaf(b, b, a * a);
-        });
+        float sq = seg_tree([&](int k, int h) { return sq_pairs(v[k], h); });
         sq = seg_cross<NW>(sq);
         const float r = rsqrtf(__fdiv_rn(sq, (float)D) + eps);
 #pragma unroll
@@ -325,15 +329,11 @@ struct AdaRmsOp {  // adaln.cu:11-58 (per-row scale/shift streamed alongside x)
     float eps;
     __device__ const anima_bf16 *src(int i) const { return i == 0 ? x : (i == 1 ? scale : shift); }
     __device__ anima_bf16 *dst(int) const { return out; }
-    __device__ void load_bcast(float *, int, int) const {}
     template <int NW>
     __device__ void segment(Vec8 *slot, const float *, int lane, int, int D) const {
         Vec8 v[8];
         load_seg(slot, lane, v);
-        float sq = seg_tree([&](int k, int j) {
-            const float a = bf_lo(v[k].w[j]), b = bf_hi(v[k].w[j]);
-            return fmaf(b, b, a * a);
-        });
+        float sq = seg_tree([&](int k, int h) { return sq_pairs(v[k], h); });
         sq = seg_cross<NW>(sq);
         const float r = rsqrtf(__fdiv_rn(sq, (float)D) + eps);
 #pragma unroll
@@ -345,6 +345,56 @@ struct AdaRmsOp {  // adaln.cu:11-58 (per-row scale/shift streamed alongside x)
 #pragma unroll
             for (int e = 0; e < 8; ++e) f[e] = fmaf(f[e] * r, 1.0f + sc[e], sh[e]);
             slot[swz(8 * lane + k)] = pack8(f);
+        }
+    }
+};
+
+// The op's NB broadcast vectors -> fp32 in shared memory (bc_pos layout), 1.0f added to those
+// in Op::kPlusOne. Split in two so that the row prefetch can be issued in between: the
+// vectors' 16-byte loads go out first (they hit L2 and must not queue behind megabytes of
+// rows), then the rows, then the conversion. Vectors that are not 16-byte aligned are read
+// with scalar loads in the second half.
+template <class Op>
+struct BcastStage {
+    static constexpr int kThreads = SegShape<Op::NIN>::kThreads;
+    static constexpr int kPer = (Op::NB * 256 + kThreads - 1) / kThreads;  // D <= 2048: <= 256 chunks per vector
+    Vec8 v[kPer];
+
+    __device__ __forceinline__ void load(const Op &op, int D) {
+        const int nch = D >> 3;
+#pragma unroll
+        for (int k = 0; k < kPer; ++k) {
+            const int i = threadIdx.x + k * kThreads;
+            if (i < Op::NB * nch) {
+                const int b = i / nch;
+                const anima_bf16 *src = op.bvec(b);
+                if (aligned16(src)) v[k] = ld_cached(src + 8 * (i - b * nch));
+            }
+        }
+    }
+    __device__ __forceinline__ void store(const Op &op, float *bc, int D) const {
+        const int nch = D >> 3;
+#pragma unroll
+        for (int k = 0; k < kPer; ++k) {
+            const int i = threadIdx.x + k * kThreads;
+            if (i < Op::NB * nch) {
+                const int b = i / nch, c = i - b * nch;
+                const anima_bf16 *src = op.bvec(b);
+                float f[8];
+                if (aligned16(src)) {
+                    unpack8(v[k], f);
+                } else {
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) f[e] = bf(src, 8 * c + e);
+                }
+                if ((Op::kPlusOne >> b) & 1u) {
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) f[e] = 1.0f + f[e];
+                }
+                float4 *q = reinterpret_cast<float4 *>(bc + b * D);
+                q[bc_pos(8 * c) >> 2] = make_float4(f[0], f[1], f[2], f[3]);
+                q[bc_pos(8 * c + 4) >> 2] = make_float4(f[4], f[5], f[6], f[7]);
+            }
         }
     }
 };
@@ -363,10 +413,6 @@ __global__ void __launch_bounds__(SegShape<Op::NIN>::kThreads, SegShape<Op::NIN>
     Vec8 *ring = reinterpret_cast<Vec8 *>(seg_smem + (size_t)NB * D * 4) +
                  (size_t)(threadIdx.x >> 5) * NST * NIN * kUnitChunks;
     const int lane = threadIdx.x & 31;
-    if constexpr (NB > 0) {
-        for (int d = threadIdx.x; d < D; d += kSegThreads) op.load_bcast(bc, d, D);
-        __syncthreads();
-    }
     const int64_t units = (N + G - 1) / G;
     const int64_t nwarps = (int64_t)gridDim.x * kSegWarps;
     const int64_t first = (int64_t)blockIdx.x * kSegWarps + (threadIdx.x >> 5);
@@ -390,8 +436,17 @@ __global__ void __launch_bounds__(SegShape<Op::NIN>::kThreads, SegShape<Op::NIN>
         }
         cp_async_commit();  // one group per unit, empty or not, keeps the counting uniform
     };
+    if constexpr (NB > 0) {
+        BcastStage<Op> bcs;
+        bcs.load(op, D);
 #pragma unroll
-    for (int st = 0; st < NST; ++st) issue(first + st * nwarps, st);
+        for (int st = 0; st < NST; ++st) issue(first + st * nwarps, st);
+        bcs.store(op, bc, D);
+        __syncthreads();
+    } else {
+#pragma unroll
+        for (int st = 0; st < NST; ++st) issue(first + st * nwarps, st);
+    }
     int st = 0;
     for (int64_t u = first; u < units; u += nwarps) {
         cp_async_wait<NST - 1>();  // this lane's copies of unit u have landed ...
