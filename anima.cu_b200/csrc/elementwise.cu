@@ -211,14 +211,16 @@ struct GeluF {
     // Two elements: both ends of the interval that holds each reference fp32 result.
     __device__ static void fast(float2 v, float2 &a, float2 &b) {
         // -2 log2(e) * u with u = sqrt(2/pi) (x + 0.044715 x^3), the polynomial as gelu.cu:27-28
-        const float2 p = __ffma2_rn(__fmul2_rn(f2(0.044715f), __fmul2_rn(v, v)), v, v);
-        const float2 z = __fmul2_rn(p, f2(-0x1.26aec2p+1f));  // -2 log2(e) * 0.7978845608f
+        // z = x (K + K c x^2) with K = -2 log2(e) * 0.7978845608f and c = 0.044715f: three
+        // roundings away from K times the reference's u, as the bound above assumes
+        const float2 z = __fmul2_rn(v, __ffma2_rn(__fmul2_rn(v, v), f2(-0x1.26aec2p+1f * 0.044715f), f2(-0x1.26aec2p+1f)));
         const float2 d = __fadd2_rn(make_float2(ex2_fast(z.x), ex2_fast(z.y)), f2(1.0f));
         // x sigma(2u); adding +0 turns -0 into +0 as the reference's fma(-0, -0, -0) does
         const float2 r = __ffma2_rn(v, make_float2(rcp_fast(d.x), rcp_fast(d.y)), f2(0.0f));
         // r and x share a sign, so r c + x e and r c' - x e are the interval's two ends
-        a = __ffma2_rn(r, f2(1.0f + 0x1p-19f), __fmul2_rn(v, f2(0x1p-23f)));
-        b = __ffma2_rn(r, f2(1.0f - 0x1p-19f), __fmul2_rn(v, f2(-0x1p-23f)));
+        const float2 e = __fmul2_rn(v, f2(0x1p-23f));
+        a = __ffma2_rn(r, f2(1.0f + 0x1p-19f), e);
+        b = __ffma2_rn(r, f2(1.0f - 0x1p-19f), make_float2(-e.x, -e.y));
     }
 };
 
