@@ -38,49 +38,93 @@ __device__ __forceinline__ void rot_f32(float x1, float x2, float c, float s, fl
     o2 = __fmaf_rn(x1, s, x2 * c);
 }
 
+// Position of unit i in a [rows, per_row] grid and the row's phase row % P (the table
+// row), advanced by the grid stride without divisions: the stride's quotient, remainder
+// and quotient mod P are taken once per thread.
+struct UnitCursor {
+    int64_t row, drow;
+    uint32_t rem, drem, ph, dph;
+    __device__ __forceinline__ UnitCursor(int64_t i, int64_t stride, uint32_t per_row, uint32_t P) {
+        row = i / per_row;
+        rem = (uint32_t)(i - row * per_row);
+        ph = (uint32_t)(row % P);
+        drow = stride / per_row;
+        drem = (uint32_t)(stride - drow * per_row);
+        dph = (uint32_t)(drow % P);
+    }
+    __device__ __forceinline__ void advance(uint32_t per_row, uint32_t P) {
+        row += drow;
+        rem += drem;
+        ph += dph;
+        if (rem >= per_row) {
+            rem -= per_row;
+            ++row;
+            ++ph;
+        }
+        if (ph >= P) ph -= P;  // ph + dph + 1 < 2P
+    }
+};
+
+// rot_bf16 on two element pairs at once; each lane of the packed ops rounds as the scalar
+// op does.
+__device__ __forceinline__ void rot_bf16_x2(float2 xr, float2 xi, float2 c, float2 s, float2 &o_r, float2 &o_i) {
+    const float2 t = __fmul2_rn(xi, s);
+    o_r = __ffma2_rn(xr, c, make_float2(-t.x, -t.y));
+    o_i = __ffma2_rn(xi, c, __fmul2_rn(xr, s));
+}
+
 struct CosmosArgs {
     anima_bf16 *x;
     const anima_bf16 *cos_t, *sin_t;
     int S, H, HD;
     int64_t units;   // rows * H * (HD/16)
     uint32_t hc;     // chunks per half head = HD/16
+    int hc_shift;    // log2(hc) when hc is a power of two, else -1
 };
 
-__global__ void __launch_bounds__(kRopeBlock) rope_cosmos_vec(CosmosArgs a) {
+__global__ void __launch_bounds__(kRopeBlock, 3) rope_cosmos_vec(CosmosArgs a) {
     pdl_wait();
     const int64_t stride = (int64_t)gridDim.x * blockDim.x;
     const uint32_t per_row = (uint32_t)a.H * a.hc;
     const int half = a.HD / 2;
-    for (int64_t base = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; base < a.units;
-         base += stride * kRopeU) {
+    int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    UnitCursor cur(i, stride, per_row, (uint32_t)a.S);
+    while (i < a.units) {
         Vec8 xr[kRopeU], xi[kRopeU], cv[kRopeU], sv[kRopeU];
         anima_bf16 *p[kRopeU];
+        bool ok[kRopeU];
 #pragma unroll
         for (int u = 0; u < kRopeU; ++u) {
-            const int64_t i = base + u * stride;
-            if (i >= a.units) break;
-            const int64_t row = i / per_row;
-            const uint32_t rem = (uint32_t)(i - row * per_row);
-            const uint32_t h = rem / a.hc, c = rem - h * a.hc;
-            const int64_t s = row % a.S;
-            p[u] = a.x + row * (int64_t)a.H * a.HD + (int64_t)h * a.HD + c * 8;
-            xr[u] = ld_stream(p[u]);
-            xi[u] = ld_stream(p[u] + half);
-            cv[u] = ld_cached(a.cos_t + s * a.HD + c * 8);
-            sv[u] = ld_cached(a.sin_t + s * a.HD + c * 8);
+            ok[u] = i < a.units;
+            if (ok[u]) {
+                const uint32_t h = a.hc_shift >= 0 ? cur.rem >> a.hc_shift : cur.rem / a.hc;
+                const uint32_t c = cur.rem - h * a.hc;
+                p[u] = a.x + cur.row * (int64_t)a.H * a.HD + (int64_t)h * a.HD + c * 8;
+                xr[u] = ld_stream(p[u]);
+                xi[u] = ld_stream(p[u] + half);
+                const int64_t t = (int64_t)cur.ph * a.HD + c * 8;
+                cv[u] = ld_cached(a.cos_t + t);
+                sv[u] = ld_cached(a.sin_t + t);
+            }
+            i += stride;
+            cur.advance(per_row, (uint32_t)a.S);
         }
 #pragma unroll
         for (int u = 0; u < kRopeU; ++u) {
-            if (base + u * stride >= a.units) break;
-            float r[8], im[8], c[8], s[8], o_r[8], o_i[8];
-            unpack8(xr[u], r);
-            unpack8(xi[u], im);
-            unpack8(cv[u], c);
-            unpack8(sv[u], s);
+            if (!ok[u]) break;
+            Vec8 o_r, o_i;
 #pragma unroll
-            for (int e = 0; e < 8; ++e) rot_bf16(r[e], im[e], c[e], s[e], o_r[e], o_i[e]);
-            st_vec(p[u], pack8(o_r));
-            st_vec(p[u] + half, pack8(o_i));
+            for (int j = 0; j < 4; ++j) {
+                float2 r, m;
+                rot_bf16_x2(make_float2(bf_lo(xr[u].w[j]), bf_hi(xr[u].w[j])),
+                            make_float2(bf_lo(xi[u].w[j]), bf_hi(xi[u].w[j])),
+                            make_float2(bf_lo(cv[u].w[j]), bf_hi(cv[u].w[j])),
+                            make_float2(bf_lo(sv[u].w[j]), bf_hi(sv[u].w[j])), r, m);
+                o_r.w[j] = pack_bf2(r.x, r.y);
+                o_i.w[j] = pack_bf2(m.x, m.y);
+            }
+            st_vec(p[u], o_r);
+            st_vec(p[u] + half, o_i);
         }
     }
     pdl_launch();
@@ -112,35 +156,39 @@ struct StdArgs {
     uint32_t hc;    // chunks per half row = D/16
 };
 
-__global__ void __launch_bounds__(kRopeBlock) rope_standard_vec(StdArgs a) {
+__global__ void __launch_bounds__(kRopeBlock, 3) rope_standard_vec(StdArgs a) {
     pdl_wait();
     const int64_t stride = (int64_t)gridDim.x * blockDim.x;
     const int half = a.D / 2;
-    for (int64_t base = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; base < a.units;
-         base += stride * kRopeU) {
+    int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    UnitCursor cur(i, stride, a.hc, (uint32_t)a.T);
+    while (i < a.units) {
         Vec8 x1[kRopeU], x2[kRopeU];
         float4 cv[kRopeU][2], sv[kRopeU][2];
         anima_bf16 *p[kRopeU];
+        bool ok[kRopeU];
 #pragma unroll
         for (int u = 0; u < kRopeU; ++u) {
-            const int64_t i = base + u * stride;
-            if (i >= a.units) break;
-            const int64_t row = i / a.hc;
-            const uint32_t c = (uint32_t)(i - row * a.hc);
-            const int64_t t = row % a.T;
-            p[u] = a.x + row * a.D + c * 8;
-            x1[u] = ld_stream(p[u]);
-            x2[u] = ld_stream(p[u] + half);
-            const float4 *cp = reinterpret_cast<const float4 *>(a.cos_t + t * half + c * 8);
-            const float4 *sp = reinterpret_cast<const float4 *>(a.sin_t + t * half + c * 8);
-            cv[u][0] = __ldg(cp);
-            cv[u][1] = __ldg(cp + 1);
-            sv[u][0] = __ldg(sp);
-            sv[u][1] = __ldg(sp + 1);
+            ok[u] = i < a.units;
+            if (ok[u]) {
+                const uint32_t c = cur.rem;
+                p[u] = a.x + cur.row * a.D + c * 8;
+                x1[u] = ld_stream(p[u]);
+                x2[u] = ld_stream(p[u] + half);
+                const int64_t t = (int64_t)cur.ph * half + c * 8;
+                const float4 *cp = reinterpret_cast<const float4 *>(a.cos_t + t);
+                const float4 *sp = reinterpret_cast<const float4 *>(a.sin_t + t);
+                cv[u][0] = __ldg(cp);
+                cv[u][1] = __ldg(cp + 1);
+                sv[u][0] = __ldg(sp);
+                sv[u][1] = __ldg(sp + 1);
+            }
+            i += stride;
+            cur.advance(a.hc, (uint32_t)a.T);
         }
 #pragma unroll
         for (int u = 0; u < kRopeU; ++u) {
-            if (base + u * stride >= a.units) break;
+            if (!ok[u]) break;
             float f1[8], f2[8], o1[8], o2[8];
             unpack8(x1[u], f1);
             unpack8(x2[u], f2);
@@ -257,7 +305,9 @@ extern "C" int anima_rope_cosmos_strided_bf16(anima_bf16 *x, const anima_bf16 *c
         x == cos_table || x == sin_table)
         return ANIMA_ERR_OVERLAP;
     if (HD % 16 == 0 && aligned16(x) && aligned16(cos_table) && aligned16(sin_table)) {
-        CosmosArgs a{x, cos_table, sin_table, S, H, HD, rows * H * (HD / 16), (uint32_t)(HD / 16)};
+        const int hc = HD / 16;
+        CosmosArgs a{x, cos_table, sin_table, S, H, HD, rows * H * hc, (uint32_t)hc,
+                     (hc & (hc - 1)) == 0 ? __builtin_ctz((unsigned)hc) : -1};
         int err = ANIMA_OK;
         const unsigned grid = wave_grid((const void *)rope_cosmos_vec, kRopeBlock, 0, (a.units + kRopeU - 1) / kRopeU, &err);
         if (err) return err;
