@@ -4,7 +4,7 @@
 // read as 16-byte chunks with L1-bypassing loads, NB broadcast vectors (0..2) indexed by
 // column (element % D, read through L1), and an Op that maps fp32 inputs to one fp32
 // output. Each thread keeps U chunks per input in flight. The grid is sized to one
-// resident wave (SMs x 2048 threads) and loops, so a launch costs the same at any size.
+// resident wave (SMs x the CTAs that fit on one SM) and loops, so no CTA waits for a second wave.
 // Elements past the last full chunk, and every element when a pointer is not 16-byte
 // aligned, take a scalar path inside the same launch.
 //
