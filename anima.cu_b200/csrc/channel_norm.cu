@@ -7,31 +7,33 @@
 // (once for the sum, once for the output), launched once per batch item.
 //
 // Here one 256-thread CTA owns a tile of 64 consecutive pixels x all C channels of one
-// image. The tile is staged into shared memory with 16-byte cp.async copies (each
-// channel contributes one contiguous 128-byte segment, so every warp request is four
-// full segments), then one thread per pixel walks the channels in order -- the
-// reference's own summation order, so the statistics and outputs match it bit for bit
-// -- and finally all threads scale the tile out of shared memory with 16-byte stores.
-// x crosses HBM once and out once. Shared memory per CTA is C*128 bytes (64 KB at
-// C = 512: three CTAs per SM keep ~190 KB of loads in flight).
+// image. The tile is staged into shared memory with 16-byte cp.async copies (each channel
+// contributes one contiguous 128-byte segment), then 64 threads walk the channels of their
+// pixel in order -- the reference's own summation order, so the statistics and outputs
+// match it bit for bit -- with the next 8 channels' shared-memory loads issued before the
+// current 8 fmas, and finally all threads scale the tile out of shared memory with 16-byte
+// stores (the fused SiLU through the decided fast path of activation.cuh). x crosses HBM
+// once and out once. Shared memory per CTA is C*128 bytes (64 KB at C = 512). A sweep of
+// tile widths (32, 64 pixels) and CTA sizes (32 to 256 threads) at the VAE decoder's four
+// shapes put this one first or within 5 % of first everywhere: fewer threads starve the
+// SiLU epilogue, narrower tiles halve the 128-byte channel segments.
 //
 // Tensors whose rows are not 16-byte aligned (spatial % 8 != 0) or whose tile would not
 // fit in shared memory use the generic kernel: one thread per pixel, the reference's
 // arithmetic, one launch for all batch items.
 #include "common.cuh"
+#include "activation.cuh"
 
 namespace anima {
 namespace {
 
-constexpr int kCnBlock = 256;
 constexpr int kCnPix = 64;                  // pixels per tile
+constexpr int kCnBlock = 256;
 constexpr int kCnMaxSmem = 200 * 1024;      // tile bytes we allow per CTA
 
 __device__ __forceinline__ float ldb(const anima_bf16 *p) {
     return __bfloat162float(*reinterpret_cast<const __nv_bfloat16 *>(p));
 }
-
-__device__ __forceinline__ float silu_f(float v) { return v / (1.0f + expf(-v)); }  // silu.cu:20-21
 
 __device__ __forceinline__ void cp_async16(void *smem, const void *gmem) {
     const unsigned s = (unsigned)__cvta_generic_to_shared(smem);
@@ -52,17 +54,18 @@ struct CnArgs {
 template <bool kSilu>
 __global__ void __launch_bounds__(kCnBlock) channel_norm_tile(CnArgs a) {
     pdl_wait();
+    constexpr int kVecs = kCnPix / 8;  // 16-byte chunks per channel row of the tile
     extern __shared__ __align__(16) anima_bf16 tile[];  // [C][kCnPix]
-    __shared__ float rms_s[kCnPix];
+    __shared__ __align__(16) float rms_s[kCnPix];
     const int b = blockIdx.x / a.tiles_per_image;
     const int s_tile = (blockIdx.x - b * a.tiles_per_image) * kCnPix;
     const int live_vecs = min(kCnPix, a.spatial - s_tile) / 8;  // spatial % 8 == 0
     const int64_t img = (int64_t)b * a.C * a.spatial;
-    const int nchunks = a.C * (kCnPix / 8);
+    const int nchunks = a.C * kVecs;
 
-    // Stage: chunk q = (channel q/8, pixel vector q%8).
+    // Stage: chunk q = (channel q / kVecs, pixel vector q % kVecs).
     for (int q = threadIdx.x; q < nchunks; q += kCnBlock) {
-        const int c = q >> 3, v = q & 7;
+        const int c = q / kVecs, v = q % kVecs;
         if (v < live_vecs)
             cp_async16(tile + c * kCnPix + v * 8, a.x + img + (int64_t)c * a.spatial + s_tile + v * 8);
     }
@@ -75,7 +78,27 @@ __global__ void __launch_bounds__(kCnBlock) channel_norm_tile(CnArgs a) {
         float q = 0.0f;
         if (p < live_vecs * 8) {
             const __nv_bfloat16 *col = reinterpret_cast<const __nv_bfloat16 *>(tile) + p;
-            for (int c = 0; c < a.C; ++c) {
+            const int full = a.C & ~7;
+            float cur[8];
+            if (full > 0) {
+#pragma unroll
+                for (int j = 0; j < 8; ++j) cur[j] = __bfloat162float(col[j * kCnPix]);
+            }
+            for (int c = 0; c < full; c += 8) {
+                float nxt[8];
+                const bool more = c + 8 < full;
+                if (more) {
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) nxt[j] = __bfloat162float(col[(c + 8 + j) * kCnPix]);
+                }
+#pragma unroll
+                for (int j = 0; j < 8; ++j) q = __fmaf_rn(cur[j], cur[j], q);
+                if (more) {
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) cur[j] = nxt[j];
+                }
+            }
+            for (int c = full; c < a.C; ++c) {
                 const float f = __bfloat162float(col[c * kCnPix]);
                 q = __fmaf_rn(f, f, q);
             }
@@ -85,21 +108,25 @@ __global__ void __launch_bounds__(kCnBlock) channel_norm_tile(CnArgs a) {
     __syncthreads();
     pdl_launch();
 
-    // vae_kernels.cu:75-80: out = (x * rms) * gamma[c], from shared memory.
+    // vae_kernels.cu:75-80: out = (x * rms) * gamma[c], from shared memory; SiLU (silu.cu)
+    // of the stored bf16 value when fused.
     for (int q = threadIdx.x; q < nchunks; q += kCnBlock) {
-        const int c = q >> 3, v = q & 7;
+        const int c = q / kVecs, v = q % kVecs;
         if (v >= live_vecs) continue;
         const Vec8 xv = *reinterpret_cast<const Vec8 *>(tile + c * kCnPix + v * 8);
+        const float4 r0 = reinterpret_cast<const float4 *>(rms_s)[2 * v];
+        const float4 r1 = reinterpret_cast<const float4 *>(rms_s)[2 * v + 1];
+        const float r[8] = {r0.x, r0.y, r0.z, r0.w, r1.x, r1.y, r1.z, r1.w};
         const float gm = ldb(a.gamma + c);
-        float f[8];
-        unpack8(xv, f);
+        Vec8 o;
 #pragma unroll
-        for (int e = 0; e < 8; ++e) {
-            float o = (f[e] * rms_s[v * 8 + e]) * gm;
-            if constexpr (kSilu) o = silu_f(bf16_round(o));
-            f[e] = o;
+        for (int j = 0; j < 4; ++j) {
+            const float2 t = __fmul2_rn(make_float2(bf_lo(xv.w[j]), bf_hi(xv.w[j])), make_float2(r[2 * j], r[2 * j + 1]));
+            const float2 u = __fmul2_rn(t, make_float2(gm, gm));
+            o.w[j] = pack_bf2(u.x, u.y);
         }
-        st_vec(a.out + img + (int64_t)c * a.spatial + s_tile + v * 8, pack8(f));
+        if constexpr (kSilu) o = fast_chunk<SiluF>(o);
+        st_vec(a.out + img + (int64_t)c * a.spatial + s_tile + v * 8, o);
     }
 }
 

@@ -107,6 +107,26 @@ class AnimaOps:
     def timestep(self, t, w, sin_out, normed, dim, eps, s, host_buf=None):
         self._ck("timestep", self.L.anima_timestep_embedding_bf16(t, w, sin_out, normed, dim, eps, s))
 
+    def call(self, name, *args):
+        """Any entry point that keeps the reference launcher's argument list."""
+        self._ck(name, getattr(self.L, "anima_" + name + "_bf16")(*args))
+
+    def embedding_lookup(self, table, ids, out, T, D, vocab, s):
+        self._ck("embedding", self.L.anima_embedding_lookup_bf16(table, ids, out, T, D, vocab, None, s))
+
+    # opt-in fused entry points (no reference counterpart; the reference arm runs its chain)
+    def swiglu(self, g, u, o, n, s):
+        self._ck("swiglu", self.L.anima_swiglu_bf16(g, u, o, n, s))
+
+    def rms_norm_channel_silu(self, x, gamma, o, B, C, sp, eps, s):
+        self._ck("cn_silu", self.L.anima_rms_norm_channel_silu_bf16(x, gamma, o, B, C, sp, eps, s))
+
+    def layer_norm_modulate(self, x, sc, sh, o, N, D, eps, s):
+        self._ck("ln_mod", self.L.anima_layer_norm_modulate_bf16(x, sc, sh, o, N, D, eps, s))
+
+    def qk_norm_rope(self, x, w, c, sn, B, S, H, HD, eps, s):
+        self._ck("qk_norm_rope", self.L.anima_qk_norm_rope_bf16(x, w, c, sn, B, S, H, HD, eps, s))
+
 
 class RefOps:
     """The reference's kernels.h launchers from oracle/_ref (C++ linkage, void)."""
@@ -147,6 +167,29 @@ class RefOps:
         host_buf.numpy()[:] = self.O.timestep_sinusoid(t, dim).view(np.int16)
         self._sin_tensor.copy_(host_buf, non_blocking=False)  # synchronous, like the reference's cudaMemcpy
         self.R.rms_norm_bf16(sin_out, w, normed, 1, dim, eps, s)
+
+    def call(self, name, *args):
+        getattr(self.R, name + "_bf16")(*args)
+
+    def embedding_lookup(self, table, ids, out, T, D, vocab, s):
+        self.R.embedding_lookup_bf16(table, ids, out, T, D, s)
+
+    # the reference's call chains that the fused entry points replace
+    def swiglu(self, g, u, o, n, s):  # qwen3.cpp:248-250
+        self.R.silu_bf16(g, o, n, s)
+        self.R.mul_bf16(o, u, o, n, s)
+
+    def rms_norm_channel_silu(self, x, gamma, o, B, C, sp, eps, s):  # vae.cpp:148,184
+        self.R.rms_norm_channel_bf16(x, gamma, o, B, C, sp, eps, s)
+        self.R.silu_bf16(o, o, B * C * sp, s)
+
+    def layer_norm_modulate(self, x, sc, sh, o, N, D, eps, s):  # transformer.cpp:563-564
+        self.R.layer_norm_bf16(x, o, N, D, eps, s)
+        self.R.scale_shift_bcast_bf16(o, sc, sh, o, N, D, s)
+
+    def qk_norm_rope(self, x, w, c, sn, B, S, H, HD, eps, s):  # transformer.cpp:350-358
+        self.R.rms_norm_bf16(x, w, x, B * S * H, HD, eps, s)
+        self.R.rope_cosmos_strided_bf16(x, c, sn, B, S, H, HD, s)
 
 
 # ---------------------------------------------------------------- device state
@@ -447,9 +490,135 @@ def headline_kernels(ops, device, peak, reps=192):
     return res
 
 
-def cpu_baseline_sample(blocks=2, rows=8192):
-    """The CPU restatement (oracle/, single thread) over `blocks` blocks of the same chain
-    at cfg2 shapes. Returns (GB/s, description)."""
+def other_ops(ops, device, peak, reps=96):
+    """The in-scope ops outside the cfg2 chain, at BASELINE's other configs, each through
+    the arm's own entry points: cfg3 (Qwen3-0.6B layer ops at seq 512), cfg4 (the VAE
+    decoder's channel RMSNorm + SiLU at its four shapes), and the final LayerNorm +
+    modulate and QK-norm + RoPE chains at cfg2. Where this library has a fused entry point
+    (SwiGLU, channel norm + SiLU, LayerNorm + modulate, QK-norm + RoPE) the anima arm
+    times the fused call and the reference arm the reference's call chain it replaces;
+    the anima arm also times its own drop-in chain. Each case cycles enough buffer sets
+    to exceed L2 where its tensors are large (small cfg3 tensors stay L2-resident, as in
+    the model) and is timed as a CUDA graph replay. Returns name -> us per call, GB/s."""
+    import torch
+
+    import tables
+
+    eps = 1e-6
+    P = lambda t: t.data_ptr()  # noqa: E731
+    g = torch.Generator(device=device).manual_seed(99)
+
+    def bf(shape, mean=0.0, std=1.0):
+        return (torch.randn(shape, generator=g, device=device) * std + mean).to(torch.bfloat16)
+
+    def S():
+        return torch.cuda.current_stream().cuda_stream
+
+    cases = []  # (name, algorithmic bytes per call, launches per call, sets, make(i) -> fn)
+
+    # ---- cfg3: Qwen3-0.6B, seq 512
+    T, Dq, V, F = 512, 1024, 151936, 3072
+    table = bf((V, Dq), std=0.02)
+    ids = torch.randint(0, V, (8, T), generator=g, device=device, dtype=torch.int32)
+    emb = [torch.empty((T, Dq), dtype=torch.bfloat16, device=device) for _ in range(8)]
+    cases.append(("cfg3_embedding_lookup_512x1024", 4 * T * Dq + 4 * T, 1, 8,
+                  lambda i: ops.embedding_lookup(P(table), P(ids[i]), P(emb[i]), T, Dq, V, S())))
+    xq = [bf((T, Dq)) for _ in range(8)]
+    wq = bf((Dq,), mean=1.0, std=0.02)
+    oq = [torch.empty_like(x) for x in xq]
+    cases.append(("cfg3_rms_norm_512x1024", 4 * T * Dq + 2 * Dq, 1, 8,
+                  lambda i: ops.call("rms_norm", P(xq[i]), P(wq), P(oq[i]), T, Dq, eps, S())))
+    qh = [bf((16 * T, 128)) for _ in range(8)]
+    wh = bf((128,), mean=1.0, std=0.02)
+    cases.append(("cfg3_qk_rms_norm_16x512x128", 4 * 16 * T * 128 + 256, 1, 8,
+                  lambda i: ops.call("rms_norm", P(qh[i]), P(wh), P(qh[i]), 16 * T, 128, eps, S())))
+    cs, sn = tables.standard_rope_tables(T, 128, 1e6)
+    cs_d, sn_d = torch.from_numpy(cs).to(device), torch.from_numpy(sn).to(device)
+    cases.append(("cfg3_rope_standard_16x512x128", 4 * 16 * T * 128 + 4 * T * 128, 1, 8,
+                  lambda i: ops.call("rope_standard", P(qh[i]), P(cs_d), P(sn_d), 16 * T, T, 128, S())))
+    gt = [bf((T, F)) for _ in range(8)]
+    ut = [bf((T, F)) for _ in range(8)]
+    st_ = [torch.empty_like(x) for x in gt]
+    cases.append(("cfg3_swiglu_512x3072", 6 * T * F, 1 if ops.kind == "anima" else 2, 8,
+                  lambda i: ops.swiglu(P(gt[i]), P(ut[i]), P(st_[i]), T * F, S())))
+    if ops.kind == "anima":
+        cases.append(("cfg3_swiglu_512x3072_as_silu_mul", 6 * T * F, 2, 8,
+                      lambda i: (ops.call("silu", P(gt[i]), P(st_[i]), T * F, S()),
+                                 ops.call("mul", P(st_[i]), P(ut[i]), P(st_[i]), T * F, S()))))
+
+    # ---- cfg4: VAE channel RMSNorm + SiLU, NCHW
+    for (C, Hs) in ((512, 128), (512, 256), (256, 512), (128, 1024)):
+        sp = Hs * Hs
+        sets = max(2, min(8, -(-512 * 2**20 // (4 * C * sp))))
+        xs = [bf((C, sp)) for _ in range(sets)]
+        ys = [torch.empty_like(x) for x in xs]
+        gm = bf((C,), mean=1.0, std=0.02)
+        cases.append((f"cfg4_rms_norm_channel_silu_{C}x{Hs}x{Hs}", 4 * C * sp + 2 * C,
+                      1 if ops.kind == "anima" else 2, sets,
+                      (lambda xs, ys, gm, C, sp: lambda i: ops.rms_norm_channel_silu(
+                          P(xs[i]), P(gm), P(ys[i]), 1, C, sp, eps, S()))(xs, ys, gm, C, sp)))
+        if ops.kind == "anima":
+            cases.append((f"cfg4_rms_norm_channel_silu_{C}x{Hs}x{Hs}_as_two_calls", 4 * C * sp + 2 * C, 2, sets,
+                          (lambda xs, ys, gm, C, sp: lambda i: (
+                              ops.call("rms_norm_channel", P(xs[i]), P(gm), P(ys[i]), 1, C, sp, eps, S()),
+                              ops.call("silu", P(ys[i]), P(ys[i]), C * sp, S())))(xs, ys, gm, C, sp)))
+
+    # ---- cfg2: final LayerNorm + modulate, QK RMSNorm + RoPE on q
+    R, D, H, HD = 8192, 2048, 16, 128
+    xl = [bf((R, D)) for _ in range(4)]
+    ol = [torch.empty_like(x) for x in xl]
+    mv = bf((2 * D,), std=0.1)
+    cases.append(("cfg2_layer_norm_modulate_8192x2048", 4 * R * D + 4 * D, 1 if ops.kind == "anima" else 2, 4,
+                  lambda i: ops.layer_norm_modulate(P(xl[i]), P(mv), P(mv) + 2 * D, P(ol[i]), R, D, eps, S())))
+    if ops.kind == "anima":
+        cases.append(("cfg2_layer_norm_modulate_8192x2048_as_two_calls", 4 * R * D + 4 * D, 2, 4,
+                      lambda i: (ops.call("layer_norm", P(xl[i]), P(ol[i]), R, D, eps, S()),
+                                 ops.call("scale_shift_bcast", P(ol[i]), P(mv), P(mv) + 2 * D, P(ol[i]), R, D,
+                                          S()))))
+    ct, st2 = tables.cosmos_rope_tables(1, 64, 64, HD)
+    ct_d = torch.from_numpy(ct.view(np.int16)).to(device)
+    st_d = torch.from_numpy(st2.view(np.int16)).to(device)
+    qk_bytes = 4 * R * D + 2 * HD + 2 * 4096 * HD * 2
+    cases.append(("cfg2_qk_norm_rope_8192x16x128", qk_bytes, 1 if ops.kind == "anima" else 2, 4,
+                  lambda i: ops.qk_norm_rope(P(xl[i]), P(wh), P(ct_d), P(st_d), 2, 4096, H, HD, eps, S())))
+    if ops.kind == "anima":
+        cases.append(("cfg2_qk_norm_rope_8192x16x128_as_two_calls", qk_bytes, 2, 4,
+                      lambda i: (ops.call("rms_norm", P(xl[i]), P(wh), P(xl[i]), R * H, HD, eps, S()),
+                                 ops.call("rope_cosmos_strided", P(xl[i]), P(ct_d), P(st_d), 2, 4096, H, HD,
+                                          S()))))
+
+    res = {}
+    for name, nbytes, launches, sets, fn in cases:
+        for i in range(sets):
+            fn(i)
+        torch.cuda.synchronize()
+        per_graph = sets * max(1, 16 // sets)
+        graph = capture(lambda st: [fn(i % sets) for i in range(per_graph)])
+        graph.replay()
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        n_rep = max(2, reps // per_graph)
+        a.record()
+        for _ in range(n_rep):
+            graph.replay()
+        b.record()
+        torch.cuda.synchronize()
+        del graph
+        us = a.elapsed_time(b) * 1e3 / (n_rep * per_graph)
+        gbs = nbytes / (us * 1e-6) / 1e9
+        res[name] = {"us": round(us, 2), "launches": launches, "bytes": nbytes, "gbs": round(gbs, 1),
+                     "frac": round(gbs / peak, 3), "l2_resident": nbytes * sets < 126 * 2**20}
+    torch.cuda.empty_cache()
+    return res
+
+
+def cpu_baseline_sample(blocks=2, rows=8192, threads=1):
+    """The CPU restatement (oracle/) over `blocks` blocks of the same chain at cfg2 shapes,
+    on `threads` host threads: every op's rows (GELU's elements) are split into `threads`
+    contiguous ranges, one oracle call per range (ctypes releases the GIL, so the C code
+    runs in parallel). Returns (GB/s, description)."""
+    from concurrent.futures import ThreadPoolExecutor
+
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import oracle as O
 
@@ -459,32 +628,59 @@ def cpu_baseline_sample(blocks=2, rows=8192):
     R = rows
     D, H, HD, M, T = c["hidden"], c["heads"], c["head_dim"], c["mlp"], c["text"]
     hidden, sub = O.randn_bf16(rng, (R, D)), O.randn_bf16(rng, (R, D))
-    q, k, qc = (O.randn_bf16(rng, (R, H * HD)) for _ in range(3))
-    kc = O.randn_bf16(rng, (B * T, H * HD))
+    q, k, qc = (O.randn_bf16(rng, (R * H, HD)) for _ in range(3))
+    kc = O.randn_bf16(rng, (B * T * H, HD))
     ff = O.randn_bf16(rng, R * M)
     mod = O.randn_bf16(rng, (3, 3 * D), std=0.1)
     temb = O.randn_bf16(rng, 3 * D, std=0.1)
     w = O.randn_bf16(rng, HD, mean=1.0, std=0.02)
     ct, st = O.cosmos_rope_tables(*c["pe"], HD)
+    pool = ThreadPoolExecutor(threads)
+
+    def split(n, align=1):
+        step = -(-n // (threads * align)) * align
+        return [(i, min(n, i + step)) for i in range(0, n, step)]
+
+    def rows_op(fn, n, *arrays):
+        """fn(lo, hi) -> result rows [lo, hi); results concatenated in order."""
+        parts = list(pool.map(lambda r: fn(*r), split(n)))
+        return parts[0] if len(parts) == 1 else np.concatenate(parts)
+
+    def rope(x):  # rows of [R*H, HD] grouped by token; table row = token % S
+        def part(lo, hi):
+            t0, t1 = lo // H, hi // H
+            out = []
+            while t0 < t1:
+                s0 = t0 % S
+                n = min(t1 - t0, S - s0)
+                out.append(O.rope_cosmos_strided(x[t0 * H:(t0 + n) * H], ct[s0:s0 + n], st[s0:s0 + n], 1, n, H, HD))
+                t0 += n
+            return np.concatenate(out) if len(out) > 1 else out[0]
+        parts = list(pool.map(lambda r: part(*r), split(x.shape[0], H)))
+        return parts[0] if len(parts) == 1 else np.concatenate(parts)
+
     t0 = time.perf_counter()
     for _ in range(blocks):
         m = [O.add(mod[j], temb) for j in range(3)]  # each [shift | scale | gate]
         shift, scale, gate = ([mj[:D], mj[D:2 * D], mj[2 * D:]] for mj in m)
-        O.adaln_layernorm(hidden, scale[0], shift[0], R, D)
-        q = O.rms_norm(q.reshape(R * H, HD), w, R * H, HD)
-        k = O.rms_norm(k.reshape(R * H, HD), w, R * H, HD)
-        q = O.rope_cosmos_strided(q, ct, st, B, R // B, H, HD)
-        k = O.rope_cosmos_strided(k, ct, st, B, R // B, H, HD)
-        hidden, _ = O.residual_gate_adaln(hidden, sub, gate[0], scale[1], shift[1], R, D)
-        qc = O.rms_norm(qc.reshape(R * H, HD), w, R * H, HD)
-        kc = O.rms_norm(kc.reshape(B * T * H, HD), w, B * T * H, HD)
-        hidden, _ = O.residual_gate_adaln(hidden, sub, gate[1], scale[2], shift[2], R, D)
-        ff = O.gelu_tanh(ff)
-        hidden = O.residual_gate_bcast(hidden, sub, gate[2], R, D)
+        rows_op(lambda lo, hi: O.adaln_layernorm(hidden[lo:hi], scale[0], shift[0], hi - lo, D), R)
+        q = rows_op(lambda lo, hi: O.rms_norm(q[lo:hi], w, hi - lo, HD), R * H)
+        k = rows_op(lambda lo, hi: O.rms_norm(k[lo:hi], w, hi - lo, HD), R * H)
+        q, k = rope(q), rope(k)
+        hidden = rows_op(lambda lo, hi: O.residual_gate_adaln(hidden[lo:hi], sub[lo:hi], gate[0], scale[1],
+                                                              shift[1], hi - lo, D)[0], R)
+        qc = rows_op(lambda lo, hi: O.rms_norm(qc[lo:hi], w, hi - lo, HD), R * H)
+        kc = rows_op(lambda lo, hi: O.rms_norm(kc[lo:hi], w, hi - lo, HD), B * T * H)
+        hidden = rows_op(lambda lo, hi: O.residual_gate_adaln(hidden[lo:hi], sub[lo:hi], gate[1], scale[2],
+                                                              shift[2], hi - lo, D)[0], R)
+        ff = rows_op(lambda lo, hi: O.gelu_tanh(ff[lo:hi]), R * M)
+        hidden = rows_op(lambda lo, hi: O.residual_gate_bcast(hidden[lo:hi], sub[lo:hi], gate[2], hi - lo, D), R)
     dt = time.perf_counter() - t0
+    pool.shutdown()
     _, per_block, _ = chain_bytes()
     nbytes = blocks * sum(per_block.values()) * R / (B * S)
-    return nbytes / dt / 1e9, f"{blocks} of the 28 blocks of the cfg2 chain at {R} rows ({dt:.1f} s)"
+    return nbytes / dt / 1e9, (f"{blocks} of the 28 blocks of the cfg2 chain at {R} rows on {threads} "
+                               f"thread{'s' if threads > 1 else ''} ({dt:.1f} s)")
 
 
 def profile_one_op(args, chain, launches_per_step, bytes_per_launch):
@@ -517,6 +713,7 @@ def main():
     ap.add_argument("--eager", action="store_true", help="time eager launches instead of CUDA graph replay")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-headline", action="store_true")
+    ap.add_argument("--no-other-ops", action="store_true", help="skip the cfg3/cfg4/fused-entry measurements")
     ap.add_argument("--only", default=None,
                     help="profiling aid: run only this op type of the chain (eager), print its timing, exit")
     args = ap.parse_args()
@@ -628,13 +825,19 @@ def main():
     headline = None
     if not args.no_headline and rank == 0:
         headline = headline_kernels(ops, device, peak)
+    other = None
+    if not args.no_other_ops and rank == 0:
+        other = other_ops(ops, device, peak)
 
     cpu = None
     if not args.no_cpu_baseline and rank == 0:
-        v, sample = cpu_baseline_sample()
-        cpu = {"value": round(v, 3), "unit": "GB/s", "cores": 1, "kind": "port", "sample": sample,
-               "note": "CPU restatement of the reference kernels (oracle/oracle.c, -O2, one thread); the "
-                       "reference itself has no CPU implementation of these ops"}
+        n_cores = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else (os.cpu_count() or 1)
+        v1, sample1 = cpu_baseline_sample(blocks=2, threads=1)
+        vn, samplen = cpu_baseline_sample(blocks=4 if n_cores >= 8 else 2, threads=n_cores)
+        cpu = {"value": round(vn, 3), "unit": "GB/s", "cores": n_cores, "kind": "port", "sample": samplen,
+               "single_thread": {"value": round(v1, 3), "cores": 1, "sample": sample1},
+               "note": "CPU restatement of the reference kernels (oracle/oracle.c, -O2), rows split over the "
+                       "host's threads; the reference itself has no CPU implementation of these ops"}
 
     used_graph = graph is not None
     del graph  # release the captured graph before the process group goes away
@@ -665,6 +868,7 @@ def main():
         "clocks": clk,
         "kernels": kernels,
         "headline_4096x2048": headline,
+        "other_ops": other,
     }
     if args.impl == "reference":
         line["impl"] = "reference"
