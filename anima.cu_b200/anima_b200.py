@@ -45,6 +45,8 @@ SIGNATURES = {
     "anima_qk_norm_rope_bf16": (P, P, P, P, I32, I32, I32, I32, F32, P),
     "anima_swiglu_bf16": (P, P, P, I64, P),
     "anima_layer_norm_modulate_bf16": (P, P, P, P, I32, I32, F32, P),
+    "anima_adaln_layernorm_temb_bf16": (P, P, P, P, P, I32, I32, F32, P),
+    "anima_residual_gate_adaln_temb_bf16": (P, P, P, P, P, P, P, I32, I32, F32, P),
     "anima_timestep_embedding_bf16": (F32, P, P, P, I32, F32, P),
 }
 
@@ -213,6 +215,17 @@ def swiglu(gate, up, out, N, stream=None):
 def layer_norm_modulate(x, scale, shift, out, N, D, eps=1e-6, stream=None):
     call("anima_layer_norm_modulate_bf16", _ptr(x), _ptr(scale), _ptr(shift), _ptr(out), N, D, eps,
          _stream(stream))
+
+
+def adaln_layernorm_temb(x, mod, temb, gate_out, out, N, D, eps=1e-6, stream=None):
+    call("anima_adaln_layernorm_temb_bf16", _ptr(x), _ptr(mod), _ptr(temb), _ptr(gate_out), _ptr(out), N, D,
+         eps, _stream(stream))
+
+
+def residual_gate_adaln_temb(hidden, sub_out, gate_in, mod, temb, gate_out, normed, N, D, eps=1e-6,
+                             stream=None):
+    call("anima_residual_gate_adaln_temb_bf16", _ptr(hidden), _ptr(sub_out), _ptr(gate_in), _ptr(mod),
+         _ptr(temb), _ptr(gate_out), _ptr(normed), N, D, eps, _stream(stream))
 
 
 def timestep_embedding(t, norm_weight, sinusoid_out, normed_out, dim, eps=1e-6, stream=None):

@@ -227,6 +227,12 @@ inline bool partial_overlap(const void *a, int64_t na, const void *b, int64_t nb
     return x < y + (uintptr_t)nb && y < x + (uintptr_t)na;
 }
 
+// True when [a, a+na) and [b, b+nb) share any byte (the same start included).
+inline bool overlaps(const void *a, int64_t na, const void *b, int64_t nb) {
+    uintptr_t x = reinterpret_cast<uintptr_t>(a), y = reinterpret_cast<uintptr_t>(b);
+    return x < y + (uintptr_t)nb && y < x + (uintptr_t)na;
+}
+
 // Launches `kernel` on `stream` with programmatic dependent launch allowed.
 template <typename... KArgs, typename... Args>
 inline void launch(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,

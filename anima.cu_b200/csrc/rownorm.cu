@@ -30,6 +30,43 @@ __device__ __forceinline__ float ln_var(float sq, float mean, int D) {
 // product into an fma with the second.
 __device__ __forceinline__ float resid_sq_pair(float h0, float h1) { return fmaf(h0, h0, h1 * h1); }
 
+// adaLN-Zero modulation folded into a norm: the reference adds the timestep embedding to the
+// modulation vector in place (add_bf16(mod, temb, mod, 3D), transformer.cpp:407) before the
+// norm reads shift and scale from it, then copies the gate out (:424). The *_temb entry points
+// read mod and temb directly: each modulation value is bf16(float(mod) + float(temb)), the
+// add_bf16 rounding (elementwise.cu:49-52), and CTA 0 writes this set's gate to gate_out.
+struct TembFold {
+    const anima_bf16 *tsc = nullptr, *tsh = nullptr;  // temb slices added to scale and shift
+    const anima_bf16 *gmod = nullptr, *gtemb = nullptr;  // this set's gate: mod and temb slices
+    anima_bf16 *gate_out = nullptr;                       // nullptr: no fold
+};
+
+__device__ __forceinline__ float bf16_add(float a, float b) { return bf16_round(a + b); }
+
+// gate_out[d] = bf16(mod_gate[d] + temb_gate[d]) for d < D, spread over the whole grid (at
+// most one 16-byte chunk or one element per thread, so it costs one memory round trip).
+__device__ __forceinline__ void fold_gate(const TembFold &t, int D) {
+    if (!t.gate_out) return;
+    const int64_t tid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    const int64_t nthr = (int64_t)gridDim.x * blockDim.x;
+    if (aligned16(t.gmod) && aligned16(t.gtemb) && aligned16(t.gate_out) && D % 8 == 0) {
+        for (int64_t c = tid; c < D / 8; c += nthr) {
+            float a[8], b[8];
+            unpack8(ld_cached(t.gmod + 8 * c), a);
+            unpack8(ld_cached(t.gtemb + 8 * c), b);
+#pragma unroll
+            for (int e = 0; e < 8; ++e) a[e] = bf16_add(a[e], b[e]);
+            st_vec(t.gate_out + 8 * c, pack8(a));
+        }
+    } else {
+        for (int64_t d = tid; d < D; d += nthr) {
+            const float g = bf16_add(__bfloat162float(reinterpret_cast<const __nv_bfloat16 *>(t.gmod)[d]),
+                                     __bfloat162float(reinterpret_cast<const __nv_bfloat16 *>(t.gtemb)[d]));
+            reinterpret_cast<__nv_bfloat16 *>(t.gate_out)[d] = __float2bfloat16_rn(g);
+        }
+    }
+}
+
 // ------------------------------------------------ segment kernels (fast path)
 //
 // A row of D elements (D % 64 == 0, D <= 2048) is NW = D/64 "segments" of 64 elements:
@@ -194,7 +231,9 @@ struct LayerNormOp {  // layer_norm.cu:26-59
     }
 };
 
-template <bool kRoundFirst>  // false: adaLN (layer_norm.cu:83-125); true: LN -> bf16 -> modulate
+// kRoundFirst false: adaLN (layer_norm.cu:83-125); true: LN -> bf16 -> modulate.
+// kTemb: the adaLN-Zero modulation fold (TembFold) is applied.
+template <bool kRoundFirst, bool kTemb = false>
 struct AdaLNOp {
     static constexpr int NIN = 1, NOUT = 1, NB = 2;
     const anima_bf16 *x, *scale, *shift;
@@ -202,8 +241,11 @@ struct AdaLNOp {
     float eps;
     __device__ const anima_bf16 *src(int) const { return x; }
     __device__ anima_bf16 *dst(int) const { return out; }
+    TembFold fold = {};
+    static constexpr bool kFold = kTemb;
     static constexpr unsigned kPlusOne = 1u;  // the reference's (1.0f + scale[d]), rounded to fp32
     __device__ const anima_bf16 *bvec(int i) const { return i == 0 ? scale : shift; }
+    __device__ const anima_bf16 *btemb(int i) const { return i == 0 ? fold.tsc : fold.tsh; }
     template <int NW>
     __device__ void segment(Vec8 *slot, const float *bc, int lane, int seg, int D) const {
         Vec8 v[8];
@@ -226,6 +268,7 @@ struct AdaLNOp {
     }
 };
 
+template <bool kTemb = false>
 struct ResGateAdaLNOp {  // layer_norm.cu:146-196
     static constexpr int NIN = 2, NOUT = 2, NB = 3;
     anima_bf16 *hidden;
@@ -234,8 +277,11 @@ struct ResGateAdaLNOp {  // layer_norm.cu:146-196
     float eps;
     __device__ const anima_bf16 *src(int i) const { return i == 0 ? hidden : sub_out; }
     __device__ anima_bf16 *dst(int o) const { return o == 0 ? hidden : normed; }
+    TembFold fold = {};  // the gate is the previous set's, already summed
+    static constexpr bool kFold = kTemb;
     static constexpr unsigned kPlusOne = 2u;
     __device__ const anima_bf16 *bvec(int i) const { return i == 0 ? gate : (i == 1 ? scale : shift); }
+    __device__ const anima_bf16 *btemb(int i) const { return i == 0 ? nullptr : (i == 1 ? fold.tsc : fold.tsh); }
     template <int NW>
     __device__ void segment(Vec8 *slot, const float *bc, int lane, int seg, int D) const {
         Vec8 x[8], y[8];
@@ -291,8 +337,11 @@ struct RmsOp {  // rms_norm.cu:9-67
     float eps;
     __device__ const anima_bf16 *src(int) const { return x; }
     __device__ anima_bf16 *dst(int) const { return out; }
+    TembFold fold = {};
+    static constexpr bool kFold = false;
     static constexpr unsigned kPlusOne = 0u;
     __device__ const anima_bf16 *bvec(int) const { return weight; }
+    __device__ const anima_bf16 *btemb(int) const { return nullptr; }
     template <int NW>
     __device__ void segment(Vec8 *slot, const float *bc, int lane, int seg, int D) const {
         Vec8 v[8];
@@ -358,7 +407,7 @@ template <class Op>
 struct BcastStage {
     static constexpr int kThreads = SegShape<Op::NIN>::kThreads;
     static constexpr int kPer = (Op::NB * 256 + kThreads - 1) / kThreads;  // D <= 2048: <= 256 chunks per vector
-    Vec8 v[kPer];
+    Vec8 v[kPer], t[kPer];
 
     __device__ __forceinline__ void load(const Op &op, int D) {
         const int nch = D >> 3;
@@ -367,8 +416,11 @@ struct BcastStage {
             const int i = threadIdx.x + k * kThreads;
             if (i < Op::NB * nch) {
                 const int b = i / nch;
-                const anima_bf16 *src = op.bvec(b);
-                if (aligned16(src)) v[k] = ld_cached(src + 8 * (i - b * nch));
+                const anima_bf16 *src = op.bvec(b), *add = Op::kFold ? op.btemb(b) : nullptr;
+                if (aligned16(src) && (!add || aligned16(add))) {
+                    v[k] = ld_cached(src + 8 * (i - b * nch));
+                    if (add) t[k] = ld_cached(add + 8 * (i - b * nch));
+                }
             }
         }
     }
@@ -379,13 +431,19 @@ struct BcastStage {
             const int i = threadIdx.x + k * kThreads;
             if (i < Op::NB * nch) {
                 const int b = i / nch, c = i - b * nch;
-                const anima_bf16 *src = op.bvec(b);
+                const anima_bf16 *src = op.bvec(b), *add = Op::kFold ? op.btemb(b) : nullptr;
                 float f[8];
-                if (aligned16(src)) {
+                if (aligned16(src) && (!add || aligned16(add))) {
                     unpack8(v[k], f);
+                    if (add) {
+                        float g[8];
+                        unpack8(t[k], g);
+#pragma unroll
+                        for (int e = 0; e < 8; ++e) f[e] = bf16_add(f[e], g[e]);
+                    }
                 } else {
 #pragma unroll
-                    for (int e = 0; e < 8; ++e) f[e] = bf(src, 8 * c + e);
+                    for (int e = 0; e < 8; ++e) f[e] = add ? bf16_add(bf(src, 8 * c + e), bf(add, 8 * c + e)) : bf(src, 8 * c + e);
                 }
                 if ((Op::kPlusOne >> b) & 1u) {
 #pragma unroll
@@ -441,6 +499,7 @@ __global__ void __launch_bounds__(SegShape<Op::NIN>::kThreads, SegShape<Op::NIN>
         bcs.load(op, D);
 #pragma unroll
         for (int st = 0; st < NST; ++st) issue(first + st * nwarps, st);
+        if constexpr (Op::kFold) fold_gate(op.fold, D);  // its loads overlap the vectors' and rows'
         bcs.store(op, bc, D);
         __syncthreads();
     } else {
@@ -548,11 +607,18 @@ struct GenArgs {
     anima_bf16 *out;
     int D;
     float eps;
+    TembFold fold = {};
 };
+
+// scale[d] or shift[d], with the folded temb added when there is one.
+__device__ __forceinline__ float modv(const anima_bf16 *v, const anima_bf16 *t, int d) {
+    return t ? bf16_add(ldb(v + d), ldb(t + d)) : ldb(v + d);
+}
 
 template <GenKind KIND>
 __global__ void row_generic(GenArgs a, int64_t N) {
     pdl_wait();
+    fold_gate(a.fold, a.D);
     __shared__ float red[33];
     const int D2 = a.D / 2, T = blockDim.x;
     for (int64_t row = blockIdx.x; row < N; row += gridDim.x) {
@@ -598,13 +664,14 @@ __global__ void row_generic(GenArgs a, int64_t N) {
                 if constexpr (KIND == GenKind::LayerNorm) {
                     o = (ldb(a.x + e) - mean) * inv;
                 } else if constexpr (KIND == GenKind::AdaLN) {
-                    o = fmaf((ldb(a.x + e) - mean) * inv, 1.0f + ldb(a.scale + d), ldb(a.shift + d));
+                    o = fmaf((ldb(a.x + e) - mean) * inv, 1.0f + modv(a.scale, a.fold.tsc, d),
+                             modv(a.shift, a.fold.tsh, d));
                 } else if constexpr (KIND == GenKind::LnModulate) {
                     o = fmaf(bf16_round((ldb(a.x + e) - mean) * inv), 1.0f + ldb(a.scale + d),
                              ldb(a.shift + d));
                 } else if constexpr (KIND == GenKind::ResGate) {
-                    o = fmaf((ldb(a.hidden + e) - mean) * inv, 1.0f + ldb(a.scale + d),
-                             ldb(a.shift + d));
+                    o = fmaf((ldb(a.hidden + e) - mean) * inv, 1.0f + modv(a.scale, a.fold.tsc, d),
+                             modv(a.shift, a.fold.tsh, d));
                 } else if constexpr (KIND == GenKind::Rms) {
                     o = ldb(a.x + e) * inv;
                     if (a.weight) o = o * ldb(a.weight + d);
@@ -719,6 +786,30 @@ extern "C" int anima_adaln_layernorm_bf16(const anima_bf16 *x, const anima_bf16 
     return launch_status();
 }
 
+extern "C" int anima_adaln_layernorm_temb_bf16(const anima_bf16 *x, const anima_bf16 *mod,
+                                               const anima_bf16 *temb, anima_bf16 *gate_out, anima_bf16 *out,
+                                               int N, int D, float eps, anima_stream_t stream) {
+    if (int e = check_row_args(N, D)) return e;
+    if (N == 0) return ANIMA_OK;
+    if (!x || !mod || !temb || !gate_out || !out) return ANIMA_ERR_NULL_POINTER;
+    if (!bf16_ok(x) || !bf16_ok(mod) || !bf16_ok(temb) || !bf16_ok(gate_out) || !bf16_ok(out))
+        return ANIMA_ERR_MISALIGNED;
+    const int64_t n = (int64_t)N * D * 2, nv = (int64_t)D * 2;
+    if (partial_overlap(x, n, out, n)) return ANIMA_ERR_OVERLAP;
+    if (overlaps(gate_out, nv, mod, 3 * nv) || overlaps(gate_out, nv, temb, 3 * nv) ||
+        overlaps(gate_out, nv, x, n) || overlaps(gate_out, nv, out, n) || overlaps(out, n, mod, 3 * nv) ||
+        overlaps(out, n, temb, 3 * nv))
+        return ANIMA_ERR_OVERLAP;
+    const TembFold fold{temb + D, temb, mod + 2 * D, temb + 2 * D, gate_out};
+    int st;
+    if (aligned16(x) && aligned16(out) && aligned16(mod) && aligned16(temb) && D % 8 == 0 &&
+        dispatch_seg(AdaLNOp<false, true>{x, mod + D, mod, out, eps, fold}, N, D, stream, st))
+        return st;
+    GenArgs a{x, nullptr, nullptr, nullptr, mod + D, mod, nullptr, out, D, eps, fold};
+    launch(row_generic<GenKind::AdaLN>, generic_grid(N), ref_row_threads(D), 0, stream, a, N);
+    return launch_status();
+}
+
 extern "C" int anima_layer_norm_modulate_bf16(const anima_bf16 *x, const anima_bf16 *scale,
                                               const anima_bf16 *shift, anima_bf16 *out, int N,
                                               int D, float eps, anima_stream_t stream) {
@@ -755,9 +846,42 @@ extern "C" int anima_residual_gate_adaln_bf16(anima_bf16 *hidden, const anima_bf
     int st;
     if (aligned16(hidden) && aligned16(sub_out) && aligned16(gate) && aligned16(scale) && aligned16(shift) &&
         aligned16(normed) &&
-        dispatch_seg(ResGateAdaLNOp{hidden, sub_out, gate, scale, shift, normed, eps}, N, D, stream, st))
+        dispatch_seg(ResGateAdaLNOp<>{hidden, sub_out, gate, scale, shift, normed, eps}, N, D, stream, st))
         return st;
     GenArgs a{hidden, hidden, sub_out, gate, scale, shift, nullptr, normed, D, eps};
+    launch(row_generic<GenKind::ResGate>, generic_grid(N), ref_row_threads(D), 0, stream, a, N);
+    return launch_status();
+}
+
+extern "C" int anima_residual_gate_adaln_temb_bf16(anima_bf16 *hidden, const anima_bf16 *sub_out,
+                                                   const anima_bf16 *gate_in, const anima_bf16 *mod,
+                                                   const anima_bf16 *temb, anima_bf16 *gate_out,
+                                                   anima_bf16 *normed, int N, int D, float eps,
+                                                   anima_stream_t stream) {
+    if (int e = check_row_args(N, D)) return e;
+    if (N == 0) return ANIMA_OK;
+    if (!hidden || !sub_out || !gate_in || !mod || !temb || !gate_out || !normed) return ANIMA_ERR_NULL_POINTER;
+    if (!bf16_ok(hidden) || !bf16_ok(sub_out) || !bf16_ok(gate_in) || !bf16_ok(mod) || !bf16_ok(temb) ||
+        !bf16_ok(gate_out) || !bf16_ok(normed))
+        return ANIMA_ERR_MISALIGNED;
+    const int64_t n = (int64_t)N * D * 2, nv = (int64_t)D * 2;
+    if (partial_overlap(hidden, n, normed, n) || hidden == normed) return ANIMA_ERR_OVERLAP;
+    if (partial_overlap(sub_out, n, hidden, n) || partial_overlap(sub_out, n, normed, n))
+        return ANIMA_ERR_OVERLAP;
+    // gate_out is written while gate_in, mod and temb are read: it must overlap none of them
+    if (overlaps(gate_out, nv, gate_in, nv) || overlaps(gate_out, nv, mod, 3 * nv) ||
+        overlaps(gate_out, nv, temb, 3 * nv) || overlaps(gate_out, nv, hidden, n) ||
+        overlaps(gate_out, nv, sub_out, n) || overlaps(gate_out, nv, normed, n) ||
+        overlaps(hidden, n, mod, 3 * nv) || overlaps(hidden, n, temb, 3 * nv) || overlaps(hidden, n, gate_in, nv) ||
+        overlaps(normed, n, mod, 3 * nv) || overlaps(normed, n, temb, 3 * nv) || overlaps(normed, n, gate_in, nv))
+        return ANIMA_ERR_OVERLAP;
+    const TembFold fold{temb + D, temb, mod + 2 * D, temb + 2 * D, gate_out};
+    int st;
+    if (aligned16(hidden) && aligned16(sub_out) && aligned16(gate_in) && aligned16(mod) && aligned16(temb) &&
+        aligned16(normed) && D % 8 == 0 &&
+        dispatch_seg(ResGateAdaLNOp<true>{hidden, sub_out, gate_in, mod + D, mod, normed, eps, fold}, N, D, stream, st))
+        return st;
+    GenArgs a{hidden, hidden, sub_out, gate_in, mod + D, mod, nullptr, normed, D, eps, fold};
     launch(row_generic<GenKind::ResGate>, generic_grid(N), ref_row_threads(D), 0, stream, a, N);
     return launch_status();
 }

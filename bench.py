@@ -127,6 +127,13 @@ class AnimaOps:
     def qk_norm_rope(self, x, w, c, sn, B, S, H, HD, eps, s):
         self._ck("qk_norm_rope", self.L.anima_qk_norm_rope_bf16(x, w, c, sn, B, S, H, HD, eps, s))
 
+    def adaln_layernorm_temb(self, x, mod, temb, gate_out, o, N, D, eps, s):
+        self._ck("adaln_temb", self.L.anima_adaln_layernorm_temb_bf16(x, mod, temb, gate_out, o, N, D, eps, s))
+
+    def residual_gate_adaln_temb(self, h, y, g_in, mod, temb, g_out, o, N, D, eps, s):
+        self._ck("resgate_temb", self.L.anima_residual_gate_adaln_temb_bf16(h, y, g_in, mod, temb, g_out, o, N, D,
+                                                                            eps, s))
+
 
 class RefOps:
     """The reference's kernels.h launchers from oracle/_ref (C++ linkage, void)."""
@@ -233,6 +240,8 @@ class Chain:
             ops._sin_tensor = self.ts_sin.view(torch.int16)
         self.ts_rng = np.random.default_rng(seed)
         self.launches_per_block = 14
+        self.gates = [torch.empty((D,), dtype=torch.bfloat16, device=device) for _ in range(2)]
+        self.launches_per_block_fused = 9
 
     def timestep(self, stream):
         t = float(np.float32(self.ts_rng.uniform()) * np.float32(1000.0))
@@ -274,9 +283,36 @@ class Chain:
         run("residual_gate_bcast", o.residual_gate_bcast, P(bs["hidden"]), P(bs["sub"]), gate3, P(bs["hidden"]), R,
             D, st)
 
+    def block_fused(self, i, stream):
+        """The same block through the opt-in fused entry points (one-line caller changes, see
+        INTEGRATION.md): mod += temb and the gate copy folded into the adaLN / residual-gate
+        norms (two gate buffers alternate), QK RMSNorm + RoPE in one pass. 9 launches."""
+        o, st = self.ops, stream
+        bs = self.sets[i % NSETS]
+        R, D, H, HD, B, S = self.R, self.D, self.H, self.HD, self.B, self.S
+        w = self.qk_w[i]
+        P = lambda t: t.data_ptr()  # noqa: E731
+        ga, gb = P(self.gates[0]), P(self.gates[1])
+        temb = P(self.temb)
+        o.adaln_layernorm_temb(P(bs["hidden"]), P(self.mod_raw[i, 0]), temb, ga, P(bs["normed"]), R, D, self.eps, st)
+        o.qk_norm_rope(P(bs["q"]), P(w[0]), P(self.cos), P(self.sin), B, S, H, HD, self.eps, st)
+        o.qk_norm_rope(P(bs["k"]), P(w[1]), P(self.cos), P(self.sin), B, S, H, HD, self.eps, st)
+        o.residual_gate_adaln_temb(P(bs["hidden"]), P(bs["sub"]), ga, P(self.mod_raw[i, 1]), temb, gb,
+                                   P(bs["normed"]), R, D, self.eps, st)
+        o.rms_norm(P(bs["qc"]), P(w[2]), P(bs["qc"]), R * H, HD, self.eps, st)
+        o.rms_norm(P(bs["kc"]), P(w[3]), P(bs["kc"]), B * self.T * H, HD, self.eps, st)
+        o.residual_gate_adaln_temb(P(bs["hidden"]), P(bs["sub"]), gb, P(self.mod_raw[i, 2]), temb, ga,
+                                   P(bs["normed"]), R, D, self.eps, st)
+        o.gelu_tanh(P(bs["ff"]), P(bs["ff_out"]), R * self.M, st)
+        o.residual_gate_bcast(P(bs["hidden"]), P(bs["sub"]), ga, P(bs["hidden"]), R, D, st)
+
     def blocks(self, stream, only=None):
         for i in range(self.NB):
             self.block(i, stream, only)
+
+    def blocks_fused(self, stream):
+        for i in range(self.NB):
+            self.block_fused(i, stream)
 
 
 # ---------------------------------------------------------------- clocks
@@ -822,6 +858,21 @@ def main():
     h2d = h_in.numel() * 2 + m_in.numel() * 2 + (0 if args.impl == "anima" else CFG["ts_dim"] * 2)
     d2h = h_out.numel() * 2
 
+    # the same step through the opt-in fused entry points (anima only)
+    fused = None
+    if args.impl == "anima" and not args.eager:
+        fgraph = capture(lambda s: chain.blocks_fused(s))
+        for _ in range(2):
+            fgraph.replay()
+        torch.cuda.synchronize()
+        fsteps = max(3, min(args.steps, 50))
+        fms = reduce_max(time_steps(chain, fsteps, stream, fgraph), dist, device) / fsteps
+        del fgraph
+        fused = {"ms_per_step": round(fms, 4), "launches_per_step": CFG["blocks"] * chain.launches_per_block_fused + 1,
+                 "speedup_vs_drop_in": round(ms_per_step / fms, 3),
+                 "note": "same step with mod+=temb and the gate copy folded into the adaLN/residual-gate norms "
+                         "and QK RMSNorm+RoPE fused (opt-in entry points); fewer bytes cross HBM"}
+
     headline = None
     if not args.no_headline and rank == 0:
         headline = headline_kernels(ops, device, peak)
@@ -869,6 +920,7 @@ def main():
         "kernels": kernels,
         "headline_4096x2048": headline,
         "other_ops": other,
+        "fused_step": fused,
     }
     if args.impl == "reference":
         line["impl"] = "reference"

@@ -193,6 +193,30 @@ ANIMA_API int anima_layer_norm_modulate_bf16(const anima_bf16 *x, const anima_bf
                                    const anima_bf16 *shift, anima_bf16 *out, int N, int D,
                                    float eps, anima_stream_t stream);
 
+/* adaLN-Zero modulation folded into adaLN LayerNorm. One launch replaces the chain
+ *   add_bf16(mod, temb, mod, 3*D); adaln_layernorm_bf16(x, mod + D, mod, out, N, D, eps);
+ *   cudaMemcpyAsync(gate, mod + 2*D, 2*D, DeviceToDevice)            (transformer.cpp:404-425)
+ * mod = [shift | scale | gate] as the modulation Linear wrote it (before the temb add),
+ * temb = [3*D]. out is the chain's normed output and gate_out[D] receives
+ * bf16(mod_gate + temb_gate), bit for bit; mod itself is left unchanged. gate_out may not
+ * overlap any other argument. */
+ANIMA_API int anima_adaln_layernorm_temb_bf16(const anima_bf16 *x, const anima_bf16 *mod,
+                                   const anima_bf16 *temb, anima_bf16 *gate_out, anima_bf16 *out,
+                                   int N, int D, float eps, anima_stream_t stream);
+
+/* The same fold for the fused residual gate: one launch replaces
+ *   add_bf16(mod, temb, mod, 3*D);
+ *   residual_gate_adaln_bf16(hidden, sub_out, gate, mod + D, mod, normed, N, D, eps);
+ *   cudaMemcpyAsync(gate, mod + 2*D, 2*D, DeviceToDevice)            (transformer.cpp:433-456)
+ * gate_in is the previous set's gate (the chain's `gate` buffer before the copy);
+ * gate_out receives this set's, so the caller alternates two gate buffers. gate_out may
+ * not overlap any other argument. */
+ANIMA_API int anima_residual_gate_adaln_temb_bf16(anima_bf16 *hidden, const anima_bf16 *sub_out,
+                                       const anima_bf16 *gate_in, const anima_bf16 *mod,
+                                       const anima_bf16 *temb, anima_bf16 *gate_out,
+                                       anima_bf16 *normed, int N, int D, float eps,
+                                       anima_stream_t stream);
+
 /* Timestep embedding on the GPU: writes the flip_sin_to_cos sinusoid of `timestep`
  * (cos of t*f_i in [0, dim/2), sin in [dim/2, dim), f_i = exp(-ln(1e4) i / (dim/2)))
  * as bf16 to sinusoid_out[dim], and, when normed_out is non-NULL, its RMSNorm times

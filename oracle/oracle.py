@@ -239,6 +239,21 @@ def layer_norm_modulate(x, scale, shift, N, D, eps=1e-6):
     return scale_shift_bcast(layer_norm(x, N, D, eps), scale, shift, N, D)
 
 
+def adaln_layernorm_temb(x, mod, temb, N, D, eps=1e-6):
+    """transformer.cpp:404-425: mod += temb, adaLN with shift = mod[:D], scale = mod[D:2D];
+    returns (normed, gate = mod[2D:3D])."""
+    m = add(mod, temb)
+    return adaln_layernorm(x, m[D:2 * D], m[:D], N, D, eps), m[2 * D:]
+
+
+def residual_gate_adaln_temb(hidden, sub_out, gate_in, mod, temb, N, D, eps=1e-6):
+    """transformer.cpp:433-456: mod += temb, residual gate with the previous gate, adaLN with
+    this set's shift/scale; returns (hidden, normed, gate = mod[2D:3D])."""
+    m = add(mod, temb)
+    h, n = residual_gate_adaln(hidden, sub_out, gate_in, m[D:2 * D], m[:D], N, D, eps)
+    return h, n, m[2 * D:]
+
+
 def timestep_sinusoid(t, dim):
     out = np.zeros(dim, np.uint16)
     lib.oracle_timestep_sinusoid(float(t), dim, _p(out))

@@ -104,6 +104,11 @@ X, Y, Z = 0x10000, 0x20000, 0x30000  # never dereferenced: every call below fail
     (("anima_qk_norm_rope_bf16", X, None, Y, Z, 1, 4, 2, 128, 1e-6, None), -1),
     (("anima_swiglu_bf16", X, Y, Z + 1, 10, None), -3),
     (("anima_layer_norm_modulate_bf16", X, Y, Z, X + 4, 4, 128, 1e-6, None), -5),
+    (("anima_adaln_layernorm_temb_bf16", X, Y, Z, None, X + 0x8000, 4, 128, 1e-6, None), -1),
+    (("anima_adaln_layernorm_temb_bf16", X, Y, Z, Y + 2, X + 0x8000, 4, 128, 1e-6, None), -5),
+    (("anima_adaln_layernorm_temb_bf16", X, Y, Z, X + 0x8100, X + 0x8000, 4, 128, 1e-6, None), -5),
+    (("anima_residual_gate_adaln_temb_bf16", X, Y, Z, Z + 0x1000, Z + 0x2000, Z, X + 0x8000, 4, 128, 1e-6, None), -5),
+    (("anima_residual_gate_adaln_temb_bf16", X, Y, Z, Z + 0x1000, Z + 0x2000, Z + 0x3000, X + 0x8000, 4, 127, 1e-6, None), -2),
     (("anima_timestep_embedding_bf16", 1.0, None, X, None, 255, 1e-6, None), -2),
     (("anima_timestep_embedding_bf16", 1.0, None, None, None, 256, 1e-6, None), -1),
     (("anima_timestep_embedding_bf16", 1.0, None, X, X, 256, 1e-6, None), -5),

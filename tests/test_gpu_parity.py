@@ -103,6 +103,75 @@ def test_residual_gate_adaln(anima, ref, rng, N, D):
         assert_one_ulp(host(out), on, "residual_gate_adaln normed vs oracle")
 
 
+# adaLN-Zero modulation folded into the norms (transformer.cpp:404-456): each fused call
+# against the reference's own chain add_bf16 + norm + gate copy, on the same buffers.
+TEMB_SHAPES = [(64, 2048), (37, 1024), (5, 512), (16, 96), (3, 130)]
+
+
+def _temb_inputs(rng, D, offset):
+    """mod [3D] as the modulation Linear writes it and temb [3D]; `offset` elements into a
+    larger buffer so that offset 1 exercises the 2-byte-aligned (generic) path."""
+    mod, temb = _modvec(rng, 3 * D), _modvec(rng, 3 * D)
+    mbuf, tbuf = torch.zeros(3 * D + 8, dtype=torch.int16, device="cuda"), torch.zeros(
+        3 * D + 8, dtype=torch.int16, device="cuda")
+    mbuf[offset:offset + 3 * D] = dev(mod)
+    tbuf[offset:offset + 3 * D] = dev(temb)
+    return mod, temb, mbuf, tbuf, mbuf[offset:offset + 3 * D], tbuf[offset:offset + 3 * D]
+
+
+@pytest.mark.parametrize("offset", [0, 1])
+@pytest.mark.parametrize("N,D", TEMB_SHAPES)
+def test_adaln_layernorm_temb_matches_reference_chain(anima, ref, rng, N, D, offset):
+    x = O.randn_bf16(rng, (N, D))
+    mod, temb, mbuf, tbuf, dm, dt = _temb_inputs(rng, D, offset)
+    dx = dev(x)
+    out, gate = empty_bf16((N, D)), empty_bf16(D)
+    mod_before = host(dm).copy()
+    anima.adaln_layernorm_temb(dx, dm, dt, gate, out, N, D, 1e-6)
+    # reference chain: mod += temb in place, adaLN, gate copy. Its bf16x2 loads need 4-byte
+    # alignment, so it always gets fresh (aligned) copies of mod and temb.
+    m, t_ref = dev(mod), dev(temb)
+    out_ref = empty_bf16((N, D))
+    ref.add_bf16(m.data_ptr(), t_ref.data_ptr(), m.data_ptr(), 3 * D, stream_ptr())
+    ref.adaln_layernorm_bf16(dx.data_ptr(), m.data_ptr() + 2 * D, m.data_ptr(), out_ref.data_ptr(), N, D, 1e-6,
+                             stream_ptr())
+    torch.cuda.synchronize()
+    assert_bit_exact(host(out), host(out_ref), "adaln_layernorm_temb normed vs reference chain")
+    assert_bit_exact(host(gate), host(m)[2 * D:], "adaln_layernorm_temb gate vs reference chain")
+    assert np.array_equal(host(dm), mod_before), "mod must be left unchanged"
+    if N * D <= ORACLE_MAX_ELEMS:
+        on, og = O.adaln_layernorm_temb(x, mod, temb, N, D)
+        assert_one_ulp(host(out), on, "adaln_layernorm_temb vs oracle")
+        assert_bit_exact(host(gate), og, "adaln_layernorm_temb gate vs oracle")
+
+
+@pytest.mark.parametrize("offset", [0, 1])
+@pytest.mark.parametrize("N,D", TEMB_SHAPES)
+def test_residual_gate_adaln_temb_matches_reference_chain(anima, ref, rng, N, D, offset):
+    x, y = O.randn_bf16(rng, (N, D)), O.randn_bf16(rng, (N, D))
+    g_prev = _modvec(rng, D)
+    mod, temb, mbuf, tbuf, dm, dt = _temb_inputs(rng, D, offset)
+    dy, dgp = dev(y), dev(g_prev)
+    h, normed, gate = dev(x), empty_bf16((N, D)), empty_bf16(D)
+    anima.residual_gate_adaln_temb(h, dy, dgp, dm, dt, gate, normed, N, D, 1e-6)
+    # reference chain with one gate buffer, on fresh (4-byte aligned) copies
+    m, t_ref, h_ref, gate_ref = dev(mod), dev(temb), dev(x), dev(g_prev)
+    normed_ref = empty_bf16((N, D))
+    ref.add_bf16(m.data_ptr(), t_ref.data_ptr(), m.data_ptr(), 3 * D, stream_ptr())
+    ref.residual_gate_adaln_bf16(h_ref.data_ptr(), dy.data_ptr(), gate_ref.data_ptr(), m.data_ptr() + 2 * D,
+                                 m.data_ptr(), normed_ref.data_ptr(), N, D, 1e-6, stream_ptr())
+    gate_ref.copy_(m[2 * D:])
+    torch.cuda.synchronize()
+    assert_bit_exact(host(h), host(h_ref), "residual_gate_adaln_temb hidden vs reference chain")
+    assert_bit_exact(host(normed), host(normed_ref), "residual_gate_adaln_temb normed vs reference chain")
+    assert_bit_exact(host(gate), host(gate_ref), "residual_gate_adaln_temb gate vs reference chain")
+    if N * D <= ORACLE_MAX_ELEMS:
+        oh, on, og = O.residual_gate_adaln_temb(x, y, g_prev, mod, temb, N, D)
+        assert_bit_exact(host(h), oh, "residual_gate_adaln_temb hidden vs oracle")
+        assert_one_ulp(host(normed), on, "residual_gate_adaln_temb normed vs oracle")
+        assert_bit_exact(host(gate), og, "residual_gate_adaln_temb gate vs oracle")
+
+
 @pytest.mark.parametrize("N,D", [(1, 2048), (65, 2048), (7, 128), (3, 96)])
 def test_adaln_rms_norm(anima, ref, rng, N, D):
     x = O.randn_bf16(rng, (N, D))
