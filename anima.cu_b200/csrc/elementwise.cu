@@ -200,9 +200,9 @@ __device__ __forceinline__ void act_group(const Vec8 (&in)[U][NS], const EwArgs 
 
 // NS = 1: out = F(x). NS = 2 (SwiGLU): out = bf16(F(gate)) * up, as silu_bf16 then mul_bf16.
 template <class F, int NS>
-__global__ void __launch_bounds__(kEwBlock, NS == 1 ? 4 : 2) fast_act_kernel(EwArgs a) {
+__global__ void __launch_bounds__(kEwBlock, NS == 1 ? 6 : 2) fast_act_kernel(EwArgs a) {
     pdl_wait();
-    constexpr int U = 4;
+    constexpr int U = 2;  // chunks per group (x2 in flight); swept 2-4 x 4-8 CTAs per SM
     const int64_t tid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     const int64_t stride = (int64_t)gridDim.x * blockDim.x;
     const int64_t nch = a.vec ? a.n >> 3 : 0;
@@ -233,7 +233,7 @@ __global__ void __launch_bounds__(kEwBlock, NS == 1 ? 4 : 2) fast_act_kernel(EwA
 template <class F, int NS>
 int launch_fast_act(const EwArgs &a, cudaStream_t stream) {
     if (a.n <= 0) return ANIMA_OK;
-    const int64_t work = a.vec ? ((a.n >> 3) + 3) / 4 : a.n;
+    const int64_t work = a.vec ? ((a.n >> 3) + 1) / 2 : a.n;
     int err = ANIMA_OK;
     const unsigned blocks = wave_grid((const void *)fast_act_kernel<F, NS>, kEwBlock, 0, work, &err);
     if (err) return err;
