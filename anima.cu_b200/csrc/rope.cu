@@ -232,6 +232,7 @@ struct QkArgs {
     int S, H;
     int64_t heads;  // B*S*H
     float eps;
+    bool narrow;    // heads < 2^32: token and table row by 32-bit division
 };
 
 __global__ void __launch_bounds__(kRopeBlock) qk_norm_rope_128(QkArgs a) {
@@ -240,7 +241,7 @@ __global__ void __launch_bounds__(kRopeBlock) qk_norm_rope_128(QkArgs a) {
     const int l = threadIdx.x & (LPR - 1);
     const int64_t hid = (int64_t)blockIdx.x * (blockDim.x / LPR) + threadIdx.x / LPR;
     const bool live = hid < a.heads;
-    const int64_t token = hid / a.H;
+    const int64_t token = a.narrow ? (int64_t)((uint32_t)hid / (uint32_t)a.H) : hid / a.H;
     anima_bf16 *p = a.x + hid * HD + l * 8;
     Vec8 v[K] = {Vec8{{0u, 0u, 0u, 0u}}, Vec8{{0u, 0u, 0u, 0u}}};
     Vec8 w[K], cv, sv;
@@ -250,7 +251,7 @@ __global__ void __launch_bounds__(kRopeBlock) qk_norm_rope_128(QkArgs a) {
     }
     w[0] = ld_cached(a.w + l * 8);
     w[1] = ld_cached(a.w + 64 + l * 8);
-    const int64_t s = live ? token % a.S : 0;
+    const int64_t s = !live ? 0 : a.narrow ? (int64_t)((uint32_t)token % (uint32_t)a.S) : token % a.S;
     cv = ld_cached(a.cos_t + s * HD + l * 8);
     sv = ld_cached(a.sin_t + s * HD + l * 8);
 
@@ -358,7 +359,7 @@ extern "C" int anima_qk_norm_rope_bf16(anima_bf16 *x, const anima_bf16 *weight,
         if (partial_overlap(x, nx, cos_table, nt) || partial_overlap(x, nx, sin_table, nt) ||
             partial_overlap(x, nx, weight, HD * 2) || x == cos_table || x == sin_table || x == weight)
             return ANIMA_ERR_OVERLAP;
-        QkArgs a{x, weight, cos_table, sin_table, S, H, heads, eps};
+        QkArgs a{x, weight, cos_table, sin_table, S, H, heads, eps, heads < 4294967296LL};
         const int64_t per_block = kRopeBlock / 8;
         launch(qk_norm_rope_128, (unsigned)((heads + per_block - 1) / per_block), kRopeBlock, 0, stream, a);
         return launch_status();
