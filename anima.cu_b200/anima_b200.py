@@ -34,6 +34,7 @@ SIGNATURES = {
     "anima_silu_bias_bf16": (P, P, P, I64, I32, P),
     "anima_add_bf16": (P, P, P, I64, P),
     "anima_mul_bf16": (P, P, P, I64, P),
+    "anima_bias_add_bf16": (P, P, P, I32, I32, P),
     "anima_scale_shift_bcast_bf16": (P, P, P, P, I32, I32, P),
     "anima_residual_gate_bcast_bf16": (P, P, P, P, I32, I32, P),
     "anima_gated_gelu_bf16": (P, P, P, I64, P),
@@ -162,6 +163,10 @@ def add(a, b, out, N, stream=None):
 
 def mul(a, b, out, N, stream=None):
     call("anima_mul_bf16", _ptr(a), _ptr(b), _ptr(out), N, _stream(stream))
+
+
+def bias_add(x, bias, out, M, D, stream=None):
+    call("anima_bias_add_bf16", _ptr(x), _ptr(bias), _ptr(out), M, D, _stream(stream))
 
 
 def scale_shift_bcast(x, scale, shift, out, M, D, stream=None):

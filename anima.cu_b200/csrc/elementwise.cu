@@ -60,6 +60,10 @@ struct OpGatedGelu {  // gemma_ops.cu:5-22 (scalar formula; nvcc folds the cubic
         return (0.5f * g * (1.0f + tanhf(inner))) * s[1];
     }
 };
+struct OpBiasAdd {  // elementwise.cu:184-213: x + bias[d]
+    static constexpr int NS = 1, NB = 1;
+    __device__ float operator()(const float (&s)[2], const float (&b)[2]) const { return s[0] + b[0]; }
+};
 struct OpScaleShift {  // elementwise.cu:216-236: fma(x, 1+scale[d], shift[d])
     static constexpr int NS = 1, NB = 2;
     __device__ float operator()(const float (&s)[2], const float (&b)[2]) const {
@@ -342,6 +346,11 @@ extern "C" int anima_gated_gelu_bf16(const anima_bf16 *gate, const anima_bf16 *u
     EwArgs a{gate, up, nullptr, nullptr, out, N, 0, false};
     a.vec = aligned16(gate) && aligned16(up) && aligned16(out);
     return launch_ew<OpGatedGelu>(a, stream);
+}
+
+extern "C" int anima_bias_add_bf16(const anima_bf16 *x, const anima_bf16 *bias, anima_bf16 *out, int M, int D,
+                                   anima_stream_t stream) {
+    return bcast_op<OpBiasAdd>(x, nullptr, bias, nullptr, out, M, D, stream);
 }
 
 extern "C" int anima_scale_shift_bcast_bf16(const anima_bf16 *x, const anima_bf16 *scale,

@@ -87,6 +87,11 @@ void mul_bf16(const __nv_bfloat16 *a, const __nv_bfloat16 *b, __nv_bfloat16 *out
     record(anima_mul_bf16(in(a), in(b), io(out), N, stream));
 }
 
+void bias_add_bf16(const __nv_bfloat16 *x, const __nv_bfloat16 *bias, __nv_bfloat16 *out, int M, int D,
+                   cudaStream_t stream) {
+    record(anima_bias_add_bf16(in(x), in(bias), io(out), M, D, stream));
+}
+
 void scale_shift_bcast_bf16(const __nv_bfloat16 *x, const __nv_bfloat16 *scale,
                             const __nv_bfloat16 *shift, __nv_bfloat16 *out, int M, int D,
                             cudaStream_t stream) {

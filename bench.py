@@ -655,11 +655,13 @@ def other_ops(ops, device, peak, reps=96):
                               ops.call("rms_norm_channel", P(xs[i]), P(gm), P(ys[i]), 1, C, sp, eps, S()),
                               ops.call("silu", P(ys[i]), P(ys[i]), C * sp, S())))(xs, ys, gm, C, sp)))
 
-    # ---- cfg2: final LayerNorm + modulate, QK RMSNorm + RoPE on q
+    # ---- cfg2: bias add after a Linear, final LayerNorm + modulate, QK RMSNorm + RoPE on q
     R, D, H, HD = 8192, 2048, 16, 128
     xl = [bf((R, D)) for _ in range(4)]
     ol = [torch.empty_like(x) for x in xl]
     mv = bf((2 * D,), std=0.1)
+    cases.append(("cfg2_bias_add_8192x2048", 4 * R * D + 2 * D, 1, 4,
+                  lambda i: ops.call("bias_add", P(xl[i]), P(mv), P(ol[i]), R, D, S())))
     cases.append(("cfg2_layer_norm_modulate_8192x2048", 4 * R * D + 4 * D, 1 if ops.kind == "anima" else 2, 4,
                   lambda i: ops.layer_norm_modulate(P(xl[i]), P(mv), P(mv) + 2 * D, P(ol[i]), R, D, eps, S())))
     if ops.kind == "anima":

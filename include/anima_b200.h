@@ -114,6 +114,12 @@ ANIMA_API int anima_add_bf16(const anima_bf16 *a, const anima_bf16 *b, anima_bf1
 ANIMA_API int anima_mul_bf16(const anima_bf16 *a, const anima_bf16 *b, anima_bf16 *out, int64_t N,
                    anima_stream_t stream);
 
+/* out[m,d] = x[m,d] + bias[d] on [M, D], D even. Replaces bias_add_bf16
+ * (kernels.h:81-83, elementwise.cu:184-213; after every biased Linear, linear.cpp:78).
+ * out may alias x. */
+ANIMA_API int anima_bias_add_bf16(const anima_bf16 *x, const anima_bf16 *bias, anima_bf16 *out, int M, int D,
+                        anima_stream_t stream);
+
 /* out[m,d] = x[m,d] * (1 + scale[d]) + shift[d]. Replaces scale_shift_bcast_bf16,
  * kernels.h:87-89 (elementwise.cu:238-247). */
 ANIMA_API int anima_scale_shift_bcast_bf16(const anima_bf16 *x, const anima_bf16 *scale,

@@ -55,6 +55,9 @@ void add_bf16(const __nv_bfloat16 *a, const __nv_bfloat16 *b, __nv_bfloat16 *out
               cudaStream_t stream = 0);
 void mul_bf16(const __nv_bfloat16 *a, const __nv_bfloat16 *b, __nv_bfloat16 *out, int64_t N,
               cudaStream_t stream = 0);
+// kernels.h:81-83
+void bias_add_bf16(const __nv_bfloat16 *x, const __nv_bfloat16 *bias, __nv_bfloat16 *out, int M, int D,
+                   cudaStream_t stream = 0);
 // kernels.h:87-92
 void scale_shift_bcast_bf16(const __nv_bfloat16 *x, const __nv_bfloat16 *scale,
                             const __nv_bfloat16 *shift, __nv_bfloat16 *out, int M, int D,

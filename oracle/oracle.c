@@ -327,6 +327,16 @@ void oracle_scale_shift_bcast(const uint16_t *x, const uint16_t *scale, const ui
         }
 }
 
+/* elementwise.cu:184-213 */
+void oracle_bias_add(const uint16_t *x, const uint16_t *bias, uint16_t *out, int M, int D) {
+    int D2 = D / 2;
+    for (int64_t m = 0; m < M; ++m)
+        for (int d = 0; d < 2 * D2; ++d) {
+            int64_t e = m * (2 * D2) + d;
+            out[e] = F2B(B2F(x[e]) + B2F(bias[d]));
+        }
+}
+
 /* elementwise.cu:249-269 */
 void oracle_residual_gate_bcast(const uint16_t *x, const uint16_t *y, const uint16_t *gate,
                                 uint16_t *out, int M, int D) {

@@ -81,6 +81,7 @@ void oracle_add(const uint16_t *a, const uint16_t *b, uint16_t *out, int64_t N);
 void oracle_mul(const uint16_t *a, const uint16_t *b, uint16_t *out, int64_t N);
 
 /* elementwise.cu:216-236 -- fma(x, 1+scale[d], shift[d]). */
+void oracle_bias_add(const uint16_t *x, const uint16_t *bias, uint16_t *out, int M, int D);
 void oracle_scale_shift_bcast(const uint16_t *x, const uint16_t *scale, const uint16_t *shift,
                               uint16_t *out, int M, int D);
 

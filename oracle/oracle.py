@@ -27,6 +27,7 @@ _SIGS = {
     "oracle_gated_gelu": (P, P, P, I64),
     "oracle_add": (P, P, P, I64),
     "oracle_mul": (P, P, P, I64),
+    "oracle_bias_add": (P, P, P, I32, I32),
     "oracle_scale_shift_bcast": (P, P, P, P, I32, I32),
     "oracle_residual_gate_bcast": (P, P, P, P, I32, I32),
     "oracle_rope_cosmos_strided": (P, P, P, I32, I32, I32, I32),
@@ -187,6 +188,12 @@ def mul(a, b):
 
 def swiglu(gate, up):
     return mul(silu(gate), up)
+
+
+def bias_add(x, bias, M, D):
+    out = np.zeros_like(x)
+    lib.oracle_bias_add(_p(x), _p(bias), _p(out), M, D)
+    return out
 
 
 def scale_shift_bcast(x, scale, shift, M, D):

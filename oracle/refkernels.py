@@ -39,6 +39,7 @@ LAUNCHERS = {
                             (P, P, P, P, I32, I32, F32, P)),  # :60-63
     "add_bf16": ("_Z8add_bf16PK13__nv_bfloat16S1_PS_lP11CUstream_st", (P, P, P, I64, P)),  # :69-71
     "mul_bf16": ("_Z8mul_bf16PK13__nv_bfloat16S1_PS_lP11CUstream_st", (P, P, P, I64, P)),  # :78-80
+    "bias_add_bf16": ("_Z13bias_add_bf16PK13__nv_bfloat16S1_PS_iiP11CUstream_st", (P, P, P, I32, I32, P)),  # :81-83
     "scale_shift_bcast_bf16": ("_Z22scale_shift_bcast_bf16PK13__nv_bfloat16S1_S1_PS_iiP11CUstream_st",
                                (P, P, P, P, I32, I32, P)),  # :87-89
     "residual_gate_bcast_bf16": ("_Z24residual_gate_bcast_bf16PK13__nv_bfloat16S1_S1_PS_iiP11CUstream_st",

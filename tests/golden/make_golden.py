@@ -81,6 +81,7 @@ def craft_rope_standard_pin(rng):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--out", default=os.path.dirname(os.path.abspath(__file__)))
+    ap.add_argument("--only", nargs="*", default=None, help="write only these fixtures (names without .npz)")
     args = ap.parse_args()
     os.makedirs(args.out, exist_ok=True)
     R = refkernels.load_reference()
@@ -203,6 +204,18 @@ def main():
         torch.cuda.synchronize()
         put(f"rms_norm_channel_{B}x{C}x{sp}", x=x, gamma=g, out=host(out))
 
+    # ---- broadcast bias add (elementwise.cu:184-213); its own seed, so earlier fixtures
+    # do not change when it was added
+    rng2 = np.random.default_rng(20261)
+    M, D = 8, 2048
+    x, b = O.randn_bf16(rng2, (M, D)), O.randn_bf16(rng2, D)
+    out = torch.empty((M, D), dtype=torch.int16, device="cuda")
+    R.bias_add_bf16(dev(x).data_ptr(), dev(b).data_ptr(), out.data_ptr(), M, D, s)
+    torch.cuda.synchronize()
+    put("bias_add", x=x, bias=b, out=host(out))
+
+    if args.only:
+        fx = {k: v for k, v in fx.items() if k in args.only}
     for name, arrays in fx.items():
         np.savez_compressed(os.path.join(args.out, name + ".npz"), **arrays)
     print(f"wrote {len(fx)} fixtures to {args.out}")

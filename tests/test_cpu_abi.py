@@ -92,6 +92,9 @@ X, Y, Z = 0x10000, 0x20000, 0x30000  # never dereferenced: every call below fail
     (("anima_add_bf16", X, Y, X + 2, 100, None), -5),
     (("anima_mul_bf16", X, None, Z, 100, None), -1),
     (("anima_scale_shift_bcast_bf16", X, Y, Z, X, 4, 7, None), -2),
+    (("anima_bias_add_bf16", X, None, X, 4, 8, None), -1),
+    (("anima_bias_add_bf16", X, Y, Z, 4, 7, None), -2),
+    (("anima_bias_add_bf16", X, Y, X + 2, 4, 8, None), -5),
     (("anima_residual_gate_bcast_bf16", X, Y, None, X, 4, 8, None), -1),
     (("anima_rope_cosmos_strided_bf16", X, Y, Z, 1, 4, 2, 7, None), -2),
     (("anima_rope_cosmos_strided_bf16", X, X, Z, 1, 4, 2, 8, None), -5),

@@ -115,6 +115,9 @@ def test_broadcast_ops():
     exact(O.scale_shift_bcast(z["x"], z["scale"], z["shift"], M, D), z["out"], "scale_shift_bcast")
     z = load("residual_gate_bcast")
     exact(O.residual_gate_bcast(z["x"], z["y"], z["gate"], M, D), z["out"], "residual_gate_bcast")
+    z = load("bias_add")
+    M, D = z["x"].shape
+    exact(O.bias_add(z["x"], z["bias"], M, D), z["out"], "bias_add")
 
 
 def test_rope_cosmos_strided():

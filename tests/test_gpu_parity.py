@@ -377,6 +377,22 @@ def test_gated_gelu(anima, ref, rng, N):
     assert_one_ulp(host(out), O.gated_gelu(g, u), "gated_gelu vs oracle")
 
 
+@pytest.mark.parametrize("M,D", [(1, 2048), (300, 2048), (7, 1024), (3, 96), (5, 10), (4096, 3072)])
+def test_bias_add(anima, ref, rng, M, D):
+    x, b = O.randn_bf16(rng, (M, D)), _modvec(rng, D, std=1.0)
+    dx, db = dev(x), dev(b)
+    out, out_ref = empty_bf16((M, D)), empty_bf16((M, D))
+    anima.bias_add(dx, db, out, M, D)
+    ref.bias_add_bf16(dx.data_ptr(), db.data_ptr(), out_ref.data_ptr(), M, D, stream_ptr())
+    xi = dev(x)
+    anima.bias_add(xi, db, xi, M, D)  # in place (linear.cpp:78)
+    torch.cuda.synchronize()
+    assert_bit_exact(host(out), host(out_ref), "bias_add vs reference")
+    assert_bit_exact(host(xi), host(out_ref), "bias_add in place")
+    if M * D <= ORACLE_MAX_ELEMS:
+        assert_bit_exact(host(out), O.bias_add(x, b, M, D), "bias_add vs oracle")
+
+
 @pytest.mark.parametrize("M,D", [(1, 2048), (8192, 2048), (33, 96), (5, 10)])
 def test_scale_shift_bcast(anima, ref, rng, M, D):
     x, sc, sh = O.randn_bf16(rng, (M, D)), _modvec(rng, D), _modvec(rng, D)
