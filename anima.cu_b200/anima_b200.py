@@ -35,6 +35,12 @@ SIGNATURES = {
     "anima_add_bf16": (P, P, P, I64, P),
     "anima_mul_bf16": (P, P, P, I64, P),
     "anima_bias_add_bf16": (P, P, P, I32, I32, P),
+    "anima_cfg_euler_step_bf16": (P, P, P, P, F32, F32, F32, I64, P),
+    "anima_cfg_euler_a_rf_step_bf16": (P, P, P, P, P) + (F32,) * 5 + (I64, P),
+    "anima_cfg_er_sde_full_step_bf16": (P,) * 8 + (F32,) * 9 + (I64, P),
+    "anima_patchify_3d_bf16": (P, P) + (I32,) * 8 + (P,),
+    "anima_unpatchify_3d_bf16": (P, P) + (I32,) * 8 + (P,),
+    "anima_channel_scale_shift_bf16": (P, P, P, P, I32, I32, I32, P),
     "anima_scale_shift_bcast_bf16": (P, P, P, P, I32, I32, P),
     "anima_residual_gate_bcast_bf16": (P, P, P, P, I32, I32, P),
     "anima_gated_gelu_bf16": (P, P, P, I64, P),
@@ -219,6 +225,38 @@ def swiglu(gate, up, out, N, stream=None):
 
 def layer_norm_modulate(x, scale, shift, out, N, D, eps=1e-6, stream=None):
     call("anima_layer_norm_modulate_bf16", _ptr(x), _ptr(scale), _ptr(shift), _ptr(out), N, D, eps,
+         _stream(stream))
+
+
+def cfg_euler_step(sample, noise_pos, noise_neg, out, cfg_scale, sigma, sigma_next, N, stream=None):
+    call("anima_cfg_euler_step_bf16", _ptr(sample), _ptr(noise_pos), _ptr(noise_neg), _ptr(out), cfg_scale, sigma,
+         sigma_next, N, _stream(stream))
+
+
+def cfg_euler_a_rf_step(sample, noise_pos, noise_neg, rand_noise, out, cfg_scale, sigma, sigma_next, eta, s_noise,
+                        N, stream=None):
+    call("anima_cfg_euler_a_rf_step_bf16", _ptr(sample), _ptr(noise_pos), _ptr(noise_neg), _ptr(rand_noise),
+         _ptr(out), cfg_scale, sigma, sigma_next, eta, s_noise, N, _stream(stream))
+
+
+def cfg_er_sde_full_step(x, noise_pos, noise_neg, denoised_out, old_denoised, denoised_d_out, old_denoised_d,
+                         rand_noise, cfg_scale, sigma, A, B, d_scale, coeff2, u_scale, coeff3, noise_coeff, N,
+                         stream=None):
+    call("anima_cfg_er_sde_full_step_bf16", _ptr(x), _ptr(noise_pos), _ptr(noise_neg), _ptr(denoised_out),
+         _ptr(old_denoised), _ptr(denoised_d_out), _ptr(old_denoised_d), _ptr(rand_noise), cfg_scale, sigma, A, B,
+         d_scale, coeff2, u_scale, coeff3, noise_coeff, N, _stream(stream))
+
+
+def patchify_3d(src, dst, B, C, T, H, W, pT, pH, pW, stream=None):
+    call("anima_patchify_3d_bf16", _ptr(src), _ptr(dst), B, C, T, H, W, pT, pH, pW, _stream(stream))
+
+
+def unpatchify_3d(src, dst, B, C, T, H, W, pT, pH, pW, stream=None):
+    call("anima_unpatchify_3d_bf16", _ptr(src), _ptr(dst), B, C, T, H, W, pT, pH, pW, _stream(stream))
+
+
+def channel_scale_shift(x, scale, shift, out, B, C, spatial, stream=None):
+    call("anima_channel_scale_shift_bf16", _ptr(x), _ptr(scale), _ptr(shift), _ptr(out), B, C, spatial,
          _stream(stream))
 
 

@@ -130,3 +130,44 @@ void rms_norm_channel_bf16(const __nv_bfloat16 *x, const __nv_bfloat16 *gamma, _
                            int B, int C, int spatial, float eps, cudaStream_t stream) {
     record(anima_rms_norm_channel_bf16(in(x), in(gamma), io(out), B, C, spatial, eps, stream));
 }
+
+void channel_scale_shift_bf16(const __nv_bfloat16 *x, const __nv_bfloat16 *scale, const __nv_bfloat16 *shift,
+                              __nv_bfloat16 *out, int B, int C, int spatial, cudaStream_t stream) {
+    record(anima_channel_scale_shift_bf16(in(x), in(scale), in(shift), io(out), B, C, spatial, stream));
+}
+
+void patchify_3d_bf16(const __nv_bfloat16 *src, __nv_bfloat16 *dst, int B, int C, int T, int H, int W, int pT,
+                      int pH, int pW, cudaStream_t stream) {
+    record(anima_patchify_3d_bf16(in(src), io(dst), B, C, T, H, W, pT, pH, pW, stream));
+}
+
+void unpatchify_3d_bf16(const __nv_bfloat16 *src, __nv_bfloat16 *dst, int B, int C, int T, int H, int W, int pT,
+                        int pH, int pW, cudaStream_t stream) {
+    record(anima_unpatchify_3d_bf16(in(src), io(dst), B, C, T, H, W, pT, pH, pW, stream));
+}
+
+void cfg_euler_step_bf16(const __nv_bfloat16 *sample, const __nv_bfloat16 *noise_pos,
+                         const __nv_bfloat16 *noise_neg, __nv_bfloat16 *out, float cfg_scale, float sigma,
+                         float sigma_next, int64_t N, cudaStream_t stream) {
+    record(anima_cfg_euler_step_bf16(in(sample), in(noise_pos), in(noise_neg), io(out), cfg_scale, sigma,
+                                     sigma_next, N, stream));
+}
+
+void cfg_euler_a_rf_step_bf16(const __nv_bfloat16 *sample, const __nv_bfloat16 *noise_pos,
+                              const __nv_bfloat16 *noise_neg, const __nv_bfloat16 *rand_noise,
+                              __nv_bfloat16 *out, float cfg_scale, float sigma, float sigma_next, float eta,
+                              float s_noise, int64_t N, cudaStream_t stream) {
+    record(anima_cfg_euler_a_rf_step_bf16(in(sample), in(noise_pos), in(noise_neg), in(rand_noise), io(out),
+                                          cfg_scale, sigma, sigma_next, eta, s_noise, N, stream));
+}
+
+void cfg_er_sde_full_step_bf16(__nv_bfloat16 *x, const __nv_bfloat16 *noise_pos, const __nv_bfloat16 *noise_neg,
+                               __nv_bfloat16 *denoised_out, const __nv_bfloat16 *old_denoised,
+                               __nv_bfloat16 *denoised_d_out, const __nv_bfloat16 *old_denoised_d,
+                               const __nv_bfloat16 *rand_noise, float cfg_scale, float sigma, float A, float B,
+                               float d_scale, float coeff2, float u_scale, float coeff3, float noise_coeff,
+                               int64_t N, cudaStream_t stream) {
+    record(anima_cfg_er_sde_full_step_bf16(io(x), in(noise_pos), in(noise_neg), io(denoised_out), in(old_denoised),
+                                           io(denoised_d_out), in(old_denoised_d), in(rand_noise), cfg_scale, sigma,
+                                           A, B, d_scale, coeff2, u_scale, coeff3, noise_coeff, N, stream));
+}

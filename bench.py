@@ -638,6 +638,24 @@ def other_ops(ops, device, peak, reps=96):
                       lambda i: (ops.call("silu", P(gt[i]), P(st_[i]), T * F, S()),
                                  ops.call("mul", P(st_[i]), P(ut[i]), P(st_[i]), T * F, S()))))
 
+    # ---- cfg2 denoising-loop I/O: CFG + Euler step, patchify / unpatchify, latent denorm
+    Cl, Hl = 16, 128
+    nl = Cl * Hl * Hl
+    lat = [bf((nl,)) for _ in range(8)]
+    npos, nneg = [bf((nl,)) for _ in range(8)], [bf((nl,)) for _ in range(8)]
+    cases.append(("cfg2_cfg_euler_step_16x128x128", 8 * nl, 1, 8,
+                  lambda i: ops.call("cfg_euler_step", P(lat[i]), P(npos[i]), P(nneg[i]), P(lat[i]), 4.5, 0.73, 0.61,
+                                     nl, S())))
+    ptok = [torch.empty((4096, 64), dtype=torch.bfloat16, device=device) for _ in range(8)]
+    cases.append(("cfg2_patchify_3d_16x128x128", 4 * nl, 1, 8,
+                  lambda i: ops.call("patchify_3d", P(lat[i]), P(ptok[i]), 1, Cl, 1, Hl, Hl, 1, 2, 2, S())))
+    cases.append(("cfg2_unpatchify_3d_16x128x128", 4 * nl, 1, 8,
+                  lambda i: ops.call("unpatchify_3d", P(ptok[i]), P(npos[i]), 1, Cl, 1, Hl, Hl, 1, 2, 2, S())))
+    lsc, lsh = bf((Cl,), mean=1.0, std=0.3), bf((Cl,), std=0.5)
+    cases.append(("cfg2_channel_scale_shift_16x128x128", 4 * nl + 4 * Cl, 1, 8,
+                  lambda i: ops.call("channel_scale_shift", P(nneg[i]), P(lsc), P(lsh), P(nneg[i]), 1, Cl, Hl * Hl,
+                                     S())))
+
     # ---- cfg4: VAE channel RMSNorm + SiLU, NCHW
     for (C, Hs) in ((512, 128), (512, 256), (256, 512), (128, 1024)):
         sp = Hs * Hs

@@ -199,6 +199,55 @@ ANIMA_API int anima_layer_norm_modulate_bf16(const anima_bf16 *x, const anima_bf
                                    const anima_bf16 *shift, anima_bf16 *out, int N, int D,
                                    float eps, anima_stream_t stream);
 
+/* ---- sampler steps and latent I/O (kernels.h:186-190, 215-223, 244-276) ----------------- */
+
+/* Fused CFG + Euler step over N elements: noise = neg + cfg*(pos - neg);
+ * out = sample - sigma*noise when sigma_next == 0, else sample + d*(sigma_next - sigma)
+ * with d = (sample - denoised)/sigma. Replaces cfg_euler_step_bf16 (transpose.cu:250-291).
+ * out may alias sample. */
+ANIMA_API int anima_cfg_euler_step_bf16(const anima_bf16 *sample, const anima_bf16 *noise_pos,
+                             const anima_bf16 *noise_neg, anima_bf16 *out, float cfg_scale,
+                             float sigma, float sigma_next, int64_t N, anima_stream_t stream);
+
+/* Fused CFG + Euler-ancestral rectified-flow step; the coefficients are derived from sigma,
+ * sigma_next, eta on the host as the reference does. rand_noise (N(0,1) bf16) is read only
+ * when eta > 0 and the re-noise coefficient is positive, and may be NULL otherwise.
+ * Replaces cfg_euler_a_rf_step_bf16 (transpose.cu:306-364). out may alias sample. */
+ANIMA_API int anima_cfg_euler_a_rf_step_bf16(const anima_bf16 *sample, const anima_bf16 *noise_pos,
+                                  const anima_bf16 *noise_neg, const anima_bf16 *rand_noise,
+                                  anima_bf16 *out, float cfg_scale, float sigma, float sigma_next,
+                                  float eta, float s_noise, int64_t N, anima_stream_t stream);
+
+/* Fused CFG + ER-SDE multi-stage step, x updated in place; writes denoised_out, and
+ * denoised_d_out when it and old_denoised are non-NULL. old_denoised, old_denoised_d and
+ * rand_noise are nullable exactly as in the reference. Replaces cfg_er_sde_full_step_bf16
+ * (transpose.cu:386-465). */
+ANIMA_API int anima_cfg_er_sde_full_step_bf16(anima_bf16 *x, const anima_bf16 *noise_pos,
+                                   const anima_bf16 *noise_neg, anima_bf16 *denoised_out,
+                                   const anima_bf16 *old_denoised, anima_bf16 *denoised_d_out,
+                                   const anima_bf16 *old_denoised_d, const anima_bf16 *rand_noise,
+                                   float cfg_scale, float sigma, float A, float B, float d_scale,
+                                   float coeff2, float u_scale, float coeff3, float noise_coeff,
+                                   int64_t N, anima_stream_t stream);
+
+/* [B, C, T, H, W] -> [B, S, C*pT*pH*pW], patch element order (c, pt, ph, pw), S over
+ * whole patches only. Replaces patchify_3d_bf16 (transpose.cu:132-185), one launch for all
+ * B (the reference launches per item). */
+ANIMA_API int anima_patchify_3d_bf16(const anima_bf16 *src, anima_bf16 *dst, int B, int C, int T, int H,
+                          int W, int pT, int pH, int pW, anima_stream_t stream);
+
+/* [B, S, patch_dim] -> [B, C, T, H, W] with the Cosmos projection's (ph, pw, pt, c) patch
+ * element order; volume positions outside whole patches are left unwritten. Replaces
+ * unpatchify_3d_bf16 (transpose.cu:191-243). */
+ANIMA_API int anima_unpatchify_3d_bf16(const anima_bf16 *src, anima_bf16 *dst, int B, int C, int T, int H,
+                            int W, int pT, int pH, int pW, anima_stream_t stream);
+
+/* out[b,c,s] = x[b,c,s]*scale[c] + shift[c] on NCHW. Replaces channel_scale_shift_bf16
+ * (vae_kernels.cu:174-206; the latent denormalisation, vae.cpp:406). out may alias x. */
+ANIMA_API int anima_channel_scale_shift_bf16(const anima_bf16 *x, const anima_bf16 *scale,
+                                  const anima_bf16 *shift, anima_bf16 *out, int B, int C, int spatial,
+                                  anima_stream_t stream);
+
 /* adaLN-Zero modulation folded into adaLN LayerNorm. One launch replaces the chain
  *   add_bf16(mod, temb, mod, 3*D); adaln_layernorm_bf16(x, mod + D, mod, out, N, D, eps);
  *   cudaMemcpyAsync(gate, mod + 2*D, 2*D, DeviceToDevice)            (transformer.cpp:404-425)

@@ -77,5 +77,27 @@ void gemma_rms_norm_bf16(const __nv_bfloat16 *x, const __nv_bfloat16 *weight, __
 // kernels.h:177-180
 void rms_norm_channel_bf16(const __nv_bfloat16 *x, const __nv_bfloat16 *gamma, __nv_bfloat16 *out,
                            int B, int C, int spatial, float eps = 1e-6f, cudaStream_t stream = 0);
+// kernels.h:189-192
+void channel_scale_shift_bf16(const __nv_bfloat16 *x, const __nv_bfloat16 *scale, const __nv_bfloat16 *shift,
+                              __nv_bfloat16 *out, int B, int C, int spatial, cudaStream_t stream = 0);
+// kernels.h:215-223
+void patchify_3d_bf16(const __nv_bfloat16 *src, __nv_bfloat16 *dst, int B, int C, int T, int H, int W, int pT,
+                      int pH, int pW, cudaStream_t stream = 0);
+void unpatchify_3d_bf16(const __nv_bfloat16 *src, __nv_bfloat16 *dst, int B, int C, int T, int H, int W, int pT,
+                        int pH, int pW, cudaStream_t stream = 0);
+// kernels.h:244-276
+void cfg_euler_step_bf16(const __nv_bfloat16 *sample, const __nv_bfloat16 *noise_pos,
+                         const __nv_bfloat16 *noise_neg, __nv_bfloat16 *out, float cfg_scale, float sigma,
+                         float sigma_next, int64_t N, cudaStream_t stream = 0);
+void cfg_euler_a_rf_step_bf16(const __nv_bfloat16 *sample, const __nv_bfloat16 *noise_pos,
+                              const __nv_bfloat16 *noise_neg, const __nv_bfloat16 *rand_noise,
+                              __nv_bfloat16 *out, float cfg_scale, float sigma, float sigma_next, float eta,
+                              float s_noise, int64_t N, cudaStream_t stream = 0);
+void cfg_er_sde_full_step_bf16(__nv_bfloat16 *x, const __nv_bfloat16 *noise_pos, const __nv_bfloat16 *noise_neg,
+                               __nv_bfloat16 *denoised_out, const __nv_bfloat16 *old_denoised,
+                               __nv_bfloat16 *denoised_d_out, const __nv_bfloat16 *old_denoised_d,
+                               const __nv_bfloat16 *rand_noise, float cfg_scale, float sigma, float A, float B,
+                               float d_scale, float coeff2, float u_scale, float coeff3, float noise_coeff,
+                               int64_t N, cudaStream_t stream = 0);
 
 extern "C" int anima_compat_last_error(void);

@@ -510,3 +510,120 @@ void oracle_standard_rope_tables(int T, int HD, float theta, float *cos_out, flo
             sin_out[t * half + d] = sinf(angle);
         }
 }
+
+/* ---------------------------------------------------- latent I/O and sampler steps */
+
+/* vae_kernels.cu:174-206 */
+void oracle_channel_scale_shift(const uint16_t *x, const uint16_t *scale, const uint16_t *shift,
+                                uint16_t *out, int B, int C, int spatial) {
+    for (int64_t b = 0; b < B; ++b)
+        for (int c = 0; c < C; ++c)
+            for (int64_t s = 0; s < spatial; ++s) {
+                int64_t e = (b * C + c) * spatial + s;
+                out[e] = F2B(fmaf(B2F(x[e]), B2F(scale[c]), B2F(shift[c])));
+            }
+}
+
+/* transpose.cu:132-185 */
+void oracle_patchify_3d(const uint16_t *src, uint16_t *dst, int B, int C, int T, int H, int W,
+                        int pT, int pH, int pW) {
+    int pe_t = T / pT, pe_h = H / pH, pe_w = W / pW;
+    int64_t S = (int64_t)pe_t * pe_h * pe_w, pd = (int64_t)C * pT * pH * pW, vol = (int64_t)C * T * H * W;
+    for (int64_t b = 0; b < B; ++b)
+        for (int64_t tok = 0; tok < S; ++tok) {
+            int64_t fw = tok % pe_w, fh = (tok / pe_w) % pe_h, ft = tok / ((int64_t)pe_w * pe_h);
+            for (int c = 0; c < C; ++c)
+                for (int pt = 0; pt < pT; ++pt)
+                    for (int ph = 0; ph < pH; ++ph)
+                        for (int pw = 0; pw < pW; ++pw) {
+                            int64_t d = ((int64_t)(c * pT + pt) * pH + ph) * pW + pw;
+                            int64_t t = ft * pT + pt, h = fh * pH + ph, w = fw * pW + pw;
+                            dst[(b * S + tok) * pd + d] = src[b * vol + (((int64_t)c * T + t) * H + h) * W + w];
+                        }
+        }
+}
+
+/* transpose.cu:191-243 */
+void oracle_unpatchify_3d(const uint16_t *src, uint16_t *dst, int B, int C, int T, int H, int W,
+                          int pT, int pH, int pW) {
+    int pe_t = T / pT, pe_h = H / pH, pe_w = W / pW;
+    int64_t S = (int64_t)pe_t * pe_h * pe_w, pd = (int64_t)C * pT * pH * pW, vol = (int64_t)C * T * H * W;
+    for (int64_t b = 0; b < B; ++b)
+        for (int64_t tok = 0; tok < S; ++tok) {
+            int64_t fw = tok % pe_w, fh = (tok / pe_w) % pe_h, ft = tok / ((int64_t)pe_w * pe_h);
+            for (int64_t d = 0; d < pd; ++d) {
+                int64_t r = d;
+                int c = (int)(r % C);
+                r /= C;
+                int pt = (int)(r % pT);
+                r /= pT;
+                int pw = (int)(r % pW);
+                int ph = (int)(r / pW);
+                int64_t t = ft * pT + pt, h = fh * pH + ph, w = fw * pW + pw;
+                dst[b * vol + (((int64_t)c * T + t) * H + h) * W + w] = src[(b * S + tok) * pd + d];
+            }
+        }
+}
+
+/* transpose.cu:250-276 */
+void oracle_cfg_euler_step(const uint16_t *sample, const uint16_t *pos, const uint16_t *neg,
+                           uint16_t *out, float cfg, float sigma, float sigma_next, int64_t n) {
+    for (int64_t i = 0; i < n; ++i) {
+        float s = B2F(sample[i]), np = B2F(pos[i]), nn = B2F(neg[i]);
+        float noise = fmaf(cfg, np - nn, nn), r;
+        if (sigma_next == 0.0f) {
+            r = fmaf(-sigma, noise, s);
+        } else {
+            float den = fmaf(-sigma, noise, s);
+            float d = (s - den) / sigma;
+            r = fmaf(d, sigma_next - sigma, s);
+        }
+        out[i] = F2B(r);
+    }
+}
+
+/* transpose.cu:306-364 */
+void oracle_cfg_euler_a_rf_step(const uint16_t *sample, const uint16_t *pos, const uint16_t *neg,
+                                const uint16_t *rand_noise, uint16_t *out, float cfg, float sigma,
+                                float sigma_next, float eta, float s_noise, int64_t n) {
+    float downstep_ratio = 1.0f + (sigma_next / sigma - 1.0f) * eta;
+    float sigma_down = sigma_next * downstep_ratio;
+    float alpha_ip1 = 1.0f - sigma_next;
+    float alpha_down = 1.0f - sigma_down;
+    float renoise_sq = sigma_next * sigma_next -
+                       sigma_down * sigma_down * alpha_ip1 * alpha_ip1 / (alpha_down * alpha_down);
+    float renoise_coeff = (renoise_sq > 0.0f) ? sqrtf(renoise_sq) : 0.0f;
+    float sdr = sigma_down / sigma, alpha_ratio = alpha_ip1 / alpha_down;
+    for (int64_t i = 0; i < n; ++i) {
+        float s = B2F(sample[i]), np = B2F(pos[i]), nn = B2F(neg[i]);
+        float noise_pred = fmaf(cfg, np - nn, nn);
+        float den = fmaf(-sigma, noise_pred, s);
+        float r = fmaf(sdr, s, (1.0f - sdr) * den);
+        if (eta > 0.0f && renoise_coeff > 0.0f)
+            r = fmaf(alpha_ratio, r, B2F(rand_noise[i]) * s_noise * renoise_coeff);
+        out[i] = F2B(r);
+    }
+}
+
+/* transpose.cu:386-465 */
+void oracle_cfg_er_sde_full_step(uint16_t *x, const uint16_t *pos, const uint16_t *neg,
+                                 uint16_t *den_out, const uint16_t *old_den, uint16_t *dd_out,
+                                 const uint16_t *old_dd, const uint16_t *rand_noise, float cfg,
+                                 float sigma, float A, float B, float d_scale, float coeff2,
+                                 float u_scale, float coeff3, float noise_coeff, int64_t n) {
+    for (int64_t i = 0; i < n; ++i) {
+        float s = B2F(x[i]), np = B2F(pos[i]), nn = B2F(neg[i]);
+        float vel = fmaf(cfg, np - nn, nn);
+        float den = fmaf(-sigma, vel, s);
+        float r = fmaf(A, s, B * den), dd = 0.0f;
+        if (old_den) {
+            dd = (den - B2F(old_den[i])) * d_scale;
+            r = fmaf(coeff2, dd, r);
+            if (old_dd) r = fmaf(coeff3, (dd - B2F(old_dd[i])) * u_scale, r);
+        }
+        if (noise_coeff > 0.0f && rand_noise) r = fmaf(noise_coeff, B2F(rand_noise[i]), r);
+        x[i] = F2B(r);
+        den_out[i] = F2B(den);
+        if (dd_out && old_den) dd_out[i] = F2B(dd);
+    }
+}

@@ -108,6 +108,34 @@ void oracle_embedding_lookup(const uint16_t *table, const int32_t *ids, uint16_t
 void oracle_rms_norm_channel(const uint16_t *x, const uint16_t *gamma, uint16_t *out, int B,
                              int C, int spatial, float eps);
 
+/* vae_kernels.cu:174-206 -- out[b,c,s] = x*scale[c] + shift[c] (one fma). */
+void oracle_channel_scale_shift(const uint16_t *x, const uint16_t *scale, const uint16_t *shift,
+                                uint16_t *out, int B, int C, int spatial);
+
+/* transpose.cu:132-243 -- 3-D patchify ([B,C,T,H,W] -> [B,S,C*pT*pH*pW], element order
+ * c,pt,ph,pw) and unpatchify ([B,S,pd] -> [B,C,T,H,W], element order ph,pw,pt,c; volume
+ * positions outside whole patches are left as they are). */
+void oracle_patchify_3d(const uint16_t *src, uint16_t *dst, int B, int C, int T, int H, int W,
+                        int pT, int pH, int pW);
+void oracle_unpatchify_3d(const uint16_t *src, uint16_t *dst, int B, int C, int T, int H, int W,
+                          int pT, int pH, int pW);
+
+/* transpose.cu:250-465 -- the fused CFG sampler steps. Products that nvcc fuses into an fma
+ * are written as fmaf; in a sum of two products the first product is fused (a choice that
+ * small fixtures cannot distinguish from the other: compared within 1 bf16 ulp). The
+ * Euler-ancestral coefficients are derived in host float arithmetic as the launcher does
+ * (transpose.cu:345-354). Pointers the reference treats as nullable may be NULL here. */
+void oracle_cfg_euler_step(const uint16_t *sample, const uint16_t *pos, const uint16_t *neg,
+                           uint16_t *out, float cfg, float sigma, float sigma_next, int64_t n);
+void oracle_cfg_euler_a_rf_step(const uint16_t *sample, const uint16_t *pos, const uint16_t *neg,
+                                const uint16_t *rand_noise, uint16_t *out, float cfg, float sigma,
+                                float sigma_next, float eta, float s_noise, int64_t n);
+void oracle_cfg_er_sde_full_step(uint16_t *x, const uint16_t *pos, const uint16_t *neg,
+                                 uint16_t *den_out, const uint16_t *old_den, uint16_t *dd_out,
+                                 const uint16_t *old_dd, const uint16_t *rand_noise, float cfg,
+                                 float sigma, float A, float B, float d_scale, float coeff2,
+                                 float u_scale, float coeff3, float noise_coeff, int64_t n);
+
 /* transformer.cpp:182-197 -- flip_sin_to_cos sinusoid of one timestep, bf16 [dim]. */
 void oracle_timestep_sinusoid(float t, int dim, uint16_t *out);
 

@@ -28,6 +28,12 @@ _SIGS = {
     "oracle_add": (P, P, P, I64),
     "oracle_mul": (P, P, P, I64),
     "oracle_bias_add": (P, P, P, I32, I32),
+    "oracle_channel_scale_shift": (P, P, P, P, I32, I32, I32),
+    "oracle_patchify_3d": (P, P) + (I32,) * 8,
+    "oracle_unpatchify_3d": (P, P) + (I32,) * 8,
+    "oracle_cfg_euler_step": (P, P, P, P, F32, F32, F32, I64),
+    "oracle_cfg_euler_a_rf_step": (P, P, P, P, P) + (F32,) * 5 + (I64,),
+    "oracle_cfg_er_sde_full_step": (P,) * 8 + (F32,) * 9 + (I64,),
     "oracle_scale_shift_bcast": (P, P, P, P, I32, I32),
     "oracle_residual_gate_bcast": (P, P, P, P, I32, I32),
     "oracle_rope_cosmos_strided": (P, P, P, I32, I32, I32, I32),
@@ -259,6 +265,50 @@ def residual_gate_adaln_temb(hidden, sub_out, gate_in, mod, temb, N, D, eps=1e-6
     m = add(mod, temb)
     h, n = residual_gate_adaln(hidden, sub_out, gate_in, m[D:2 * D], m[:D], N, D, eps)
     return h, n, m[2 * D:]
+
+
+def channel_scale_shift(x, scale, shift, B, C, spatial):
+    out = np.zeros_like(x)
+    lib.oracle_channel_scale_shift(_p(x), _p(scale), _p(shift), _p(out), B, C, spatial)
+    return out
+
+
+def patchify_3d(src, B, C, T, H, W, pT, pH, pW):
+    S = (T // pT) * (H // pH) * (W // pW)
+    out = np.zeros((B, S, C * pT * pH * pW), np.uint16)
+    lib.oracle_patchify_3d(_p(np.ascontiguousarray(src)), _p(out), B, C, T, H, W, pT, pH, pW)
+    return out
+
+
+def unpatchify_3d(src, B, C, T, H, W, pT, pH, pW, init=None):
+    out = np.zeros((B, C, T, H, W), np.uint16) if init is None else np.array(init, np.uint16).reshape(B, C, T, H, W)
+    lib.oracle_unpatchify_3d(_p(np.ascontiguousarray(src)), _p(out), B, C, T, H, W, pT, pH, pW)
+    return out
+
+
+def cfg_euler_step(sample, pos, neg, cfg, sigma, sigma_next):
+    out = np.zeros_like(sample)
+    lib.oracle_cfg_euler_step(_p(sample), _p(pos), _p(neg), _p(out), cfg, sigma, sigma_next, sample.size)
+    return out
+
+
+def cfg_euler_a_rf_step(sample, pos, neg, rand_noise, cfg, sigma, sigma_next, eta, s_noise):
+    out = np.zeros_like(sample)
+    lib.oracle_cfg_euler_a_rf_step(_p(sample), _p(pos), _p(neg), None if rand_noise is None else _p(rand_noise),
+                                   _p(out), cfg, sigma, sigma_next, eta, s_noise, sample.size)
+    return out
+
+
+def cfg_er_sde_full_step(x, pos, neg, old_den, old_dd, rand_noise, cfg, sigma, A, B, d_scale, coeff2, u_scale,
+                         coeff3, noise_coeff, want_dd=True):
+    """Returns (x, denoised, dd); dd is None unless want_dd and old_den is given."""
+    xo, den = np.array(x, np.uint16), np.zeros_like(x)
+    dd = np.zeros_like(x) if want_dd else None
+    opt = lambda a: None if a is None else _p(a)  # noqa: E731
+    lib.oracle_cfg_er_sde_full_step(_p(xo), _p(pos), _p(neg), _p(den), opt(old_den), opt(dd), opt(old_dd),
+                                    opt(rand_noise), cfg, sigma, A, B, d_scale, coeff2, u_scale, coeff3, noise_coeff,
+                                    x.size)
+    return xo, den, (dd if want_dd and old_den is not None else None)
 
 
 def timestep_sinusoid(t, dim):

@@ -53,6 +53,18 @@ LAUNCHERS = {
                             (P, P, P, I32, I32, F32, P)),  # :151-153
     "rms_norm_channel_bf16": ("_Z21rms_norm_channel_bf16PK13__nv_bfloat16S1_PS_iiifP11CUstream_st",
                               (P, P, P, I32, I32, I32, F32, P)),  # :177-180
+    "channel_scale_shift_bf16": ("_Z24channel_scale_shift_bf16PK13__nv_bfloat16S1_S1_PS_iiiP11CUstream_st",
+                                 (P, P, P, P, I32, I32, I32, P)),  # :189-192
+    "patchify_3d_bf16": ("_Z16patchify_3d_bf16PK13__nv_bfloat16PS_iiiiiiiiP11CUstream_st",
+                         (P, P) + (I32,) * 8 + (P,)),  # :215-218
+    "unpatchify_3d_bf16": ("_Z18unpatchify_3d_bf16PK13__nv_bfloat16PS_iiiiiiiiP11CUstream_st",
+                           (P, P) + (I32,) * 8 + (P,)),  # :221-223
+    "cfg_euler_step_bf16": ("_Z19cfg_euler_step_bf16PK13__nv_bfloat16S1_S1_PS_ffflP11CUstream_st",
+                            (P, P, P, P, F32, F32, F32, I64, P)),  # :244-250
+    "cfg_euler_a_rf_step_bf16": ("_Z24cfg_euler_a_rf_step_bf16PK13__nv_bfloat16S1_S1_S1_PS_ffffflP11CUstream_st",
+                                 (P, P, P, P, P) + (F32,) * 5 + (I64, P)),  # :253-260
+    "cfg_er_sde_full_step_bf16": ("_Z25cfg_er_sde_full_step_bf16P13__nv_bfloat16PKS_S2_S0_S2_S0_S2_S2_ffffffffflP11CUstream_st",
+                                  (P,) * 8 + (F32,) * 9 + (I64, P)),  # :264-276
 }
 
 

@@ -214,6 +214,51 @@ def main():
     torch.cuda.synchronize()
     put("bias_add", x=x, bias=b, out=host(out))
 
+    # ---- sampler steps and latent I/O (transpose.cu, vae_kernels.cu); own seed as well
+    rng3 = np.random.default_rng(20262)
+    N = 4096
+    smp, pos, neg, rn, od, odd = (O.randn_bf16(rng3, N) for _ in range(6))
+    for name, sn in (("cfg_euler_step", 0.61), ("cfg_euler_step_last", 0.0)):
+        out = torch.zeros(N, dtype=torch.int16, device="cuda")
+        R.cfg_euler_step_bf16(dev(smp).data_ptr(), dev(pos).data_ptr(), dev(neg).data_ptr(), out.data_ptr(), 4.5,
+                              0.73, sn, N, s)
+        torch.cuda.synchronize()
+        put(name, sample=smp, pos=pos, neg=neg, out=host(out), params=np.array([4.5, 0.73, sn], np.float32))
+    out = torch.zeros(N, dtype=torch.int16, device="cuda")
+    R.cfg_euler_a_rf_step_bf16(dev(smp).data_ptr(), dev(pos).data_ptr(), dev(neg).data_ptr(), dev(rn).data_ptr(),
+                               out.data_ptr(), 3.5, 0.8, 0.55, 1.0, 1.0, N, s)
+    torch.cuda.synchronize()
+    put("cfg_euler_a_rf_step", sample=smp, pos=pos, neg=neg, rand=rn, out=host(out),
+        params=np.array([3.5, 0.8, 0.55, 1.0, 1.0], np.float32))
+    coeffs = [4.0, 0.7, 0.93, 0.051, 1.7, 0.02, 2.3, 0.004, 0.3]
+    x, den, dd = dev(smp), torch.zeros(N, dtype=torch.int16, device="cuda"), torch.zeros(N, dtype=torch.int16,
+                                                                                         device="cuda")
+    R.cfg_er_sde_full_step_bf16(x.data_ptr(), dev(pos).data_ptr(), dev(neg).data_ptr(), den.data_ptr(),
+                                dev(od).data_ptr(), dd.data_ptr(), dev(odd).data_ptr(), dev(rn).data_ptr(), *coeffs,
+                                N, s)
+    torch.cuda.synchronize()
+    put("cfg_er_sde_full_step", x=smp, pos=pos, neg=neg, old_den=od, old_dd=odd, rand=rn, x_out=host(x),
+        den_out=host(den), dd_out=host(dd), params=np.array(coeffs, np.float32))
+    shape = (2, 4, 3, 8, 6, 1, 2, 2)
+    B_, C_, T_, H_, W_, pT_, pH_, pW_ = shape
+    vol = O.randn_bf16(rng3, (B_, C_, T_, H_, W_))
+    S_, pd_ = (T_ // pT_) * (H_ // pH_) * (W_ // pW_), C_ * pT_ * pH_ * pW_
+    pout = torch.zeros((B_, S_, pd_), dtype=torch.int16, device="cuda")
+    R.patchify_3d_bf16(dev(vol).data_ptr(), pout.data_ptr(), *shape, s)
+    pin = O.randn_bf16(rng3, (B_, S_, pd_))
+    uout = torch.zeros((B_, C_, T_, H_, W_), dtype=torch.int16, device="cuda")
+    R.unpatchify_3d_bf16(dev(pin).data_ptr(), uout.data_ptr(), *shape, s)
+    torch.cuda.synchronize()
+    put("patchify_3d", x=vol, out=host(pout), shape=np.array(shape, np.int32))
+    put("unpatchify_3d", x=pin, out=host(uout), shape=np.array(shape, np.int32))
+    cx = O.randn_bf16(rng3, (2, 16, 96))
+    csc, csh = O.randn_bf16(rng3, 16, mean=1.0, std=0.3), O.randn_bf16(rng3, 16, std=0.5)
+    cout = torch.zeros((2, 16, 96), dtype=torch.int16, device="cuda")
+    R.channel_scale_shift_bf16(dev(cx).data_ptr(), dev(csc).data_ptr(), dev(csh).data_ptr(), cout.data_ptr(), 2, 16,
+                               96, s)
+    torch.cuda.synchronize()
+    put("channel_scale_shift", x=cx, scale=csc, shift=csh, out=host(cout))
+
     if args.only:
         fx = {k: v for k, v in fx.items() if k in args.only}
     for name, arrays in fx.items():

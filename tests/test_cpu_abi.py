@@ -93,6 +93,13 @@ X, Y, Z = 0x10000, 0x20000, 0x30000  # never dereferenced: every call below fail
     (("anima_mul_bf16", X, None, Z, 100, None), -1),
     (("anima_scale_shift_bcast_bf16", X, Y, Z, X, 4, 7, None), -2),
     (("anima_bias_add_bf16", X, None, X, 4, 8, None), -1),
+    (("anima_cfg_euler_step_bf16", X, Y, None, Z, 1.0, 0.5, 0.2, 100, None), -1),
+    (("anima_cfg_euler_step_bf16", X, Y, Z, X + 2, 1.0, 0.5, 0.2, 100, None), -5),
+    (("anima_cfg_euler_a_rf_step_bf16", X, Y, Z, None, X, 1.0, 0.8, 0.5, 1.0, 1.0, 100, None), -1),
+    (("anima_cfg_er_sde_full_step_bf16", X, Y, Z, X + 4, None, None, None, None) + (1.0,) * 9 + (100, None), -5),
+    (("anima_patchify_3d_bf16", X, Y, 1, 4, 1, 8, 8, 1, 0, 2, None), -2),
+    (("anima_unpatchify_3d_bf16", X, X + 8, 1, 4, 1, 8, 8, 1, 2, 2, None), -5),
+    (("anima_channel_scale_shift_bf16", X, Y, Z, X + 2, 1, 4, 16, None), -5),
     (("anima_bias_add_bf16", X, Y, Z, 4, 7, None), -2),
     (("anima_bias_add_bf16", X, Y, X + 2, 4, 8, None), -5),
     (("anima_residual_gate_bcast_bf16", X, Y, None, X, 4, 8, None), -1),

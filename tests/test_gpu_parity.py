@@ -565,3 +565,143 @@ def test_timestep_embedding(anima, ref, rng, dim):
         # the host loop of transformer.cpp:182-197, restated in oracle.c
         assert_one_ulp(host(sin_out), O.timestep_sinusoid(t, dim), f"sinusoid t={t}")
         assert_bit_exact(host(normed), host(normed_ref), f"timestep rms_norm t={t}")
+
+
+# ---------------------------------------------------------------- sampler steps and latent I/O
+# transpose.cu:128-465, vae_kernels.cu:174-206. The reference kernels use 2-byte accesses, so
+# they also take the offset (unaligned) buffers.
+def _bf_at(a, offset):
+    """a on the device, `offset` elements into a larger buffer (offset 1: 2-byte aligned)."""
+    buf = torch.zeros(a.size + 8, dtype=torch.int16, device="cuda")
+    buf[offset:offset + a.size] = dev(a.reshape(-1))
+    return buf[offset:offset + a.size]
+
+
+@pytest.mark.parametrize("B,C,sp", [(1, 16, 128 * 128), (2, 16, 4096 + 3), (1, 3, 10), (3, 5, 8)])
+def test_channel_scale_shift(anima, ref, rng, B, C, sp):
+    x = O.randn_bf16(rng, (B, C, sp))
+    sc, sh = O.randn_bf16(rng, C, mean=1.0, std=0.3), O.randn_bf16(rng, C, std=0.5)
+    dx, dsc, dsh = dev(x), dev(sc), dev(sh)
+    out, out_ref = empty_bf16((B, C, sp)), empty_bf16((B, C, sp))
+    anima.channel_scale_shift(dx, dsc, dsh, out, B, C, sp)
+    ref.channel_scale_shift_bf16(dx.data_ptr(), dsc.data_ptr(), dsh.data_ptr(), out_ref.data_ptr(), B, C, sp,
+                                 stream_ptr())
+    xi = dev(x)
+    anima.channel_scale_shift(xi, dsc, dsh, xi, B, C, sp)  # in place (vae.cpp:406)
+    torch.cuda.synchronize()
+    assert_bit_exact(host(out), host(out_ref), "channel_scale_shift vs reference")
+    assert_bit_exact(host(xi), host(out_ref), "channel_scale_shift in place")
+    assert_bit_exact(host(out), O.channel_scale_shift(x, sc, sh, B, C, sp).reshape(-1), "channel_scale_shift vs oracle")
+
+
+PATCH_SHAPES = [(1, 16, 1, 128, 128, 1, 2, 2), (2, 4, 3, 8, 6, 1, 2, 2), (1, 3, 4, 6, 9, 2, 3, 3),
+                (1, 2, 1, 5, 7, 1, 2, 2), (2, 16, 2, 16, 16, 2, 2, 2)]
+
+
+@pytest.mark.parametrize("shape", PATCH_SHAPES)
+def test_patchify_3d(anima, ref, rng, shape):
+    B, C, T, H, W, pT, pH, pW = shape
+    S, pd = (T // pT) * (H // pH) * (W // pW), C * pT * pH * pW
+    x = O.randn_bf16(rng, (B, C, T, H, W))
+    dx = dev(x)
+    out, out_ref = torch.zeros((B, S, pd), dtype=torch.int16, device="cuda"), torch.zeros(
+        (B, S, pd), dtype=torch.int16, device="cuda")
+    anima.patchify_3d(dx, out, *shape)
+    ref.patchify_3d_bf16(dx.data_ptr(), out_ref.data_ptr(), *shape, stream_ptr())
+    torch.cuda.synchronize()
+    assert_bit_exact(host(out), host(out_ref), "patchify_3d vs reference")
+    assert_bit_exact(host(out), O.patchify_3d(x, *shape), "patchify_3d vs oracle")
+
+
+@pytest.mark.parametrize("shape", PATCH_SHAPES)
+def test_unpatchify_3d(anima, ref, rng, shape):
+    B, C, T, H, W, pT, pH, pW = shape
+    S, pd = (T // pT) * (H // pH) * (W // pW), C * pT * pH * pW
+    p = O.randn_bf16(rng, (B, S, pd))
+    fill = O.randn_bf16(rng, (B, C, T, H, W))  # positions outside whole patches keep this
+    dp = dev(p)
+    out, out_ref = dev(fill), dev(fill)
+    anima.unpatchify_3d(dp, out, *shape)
+    ref.unpatchify_3d_bf16(dp.data_ptr(), out_ref.data_ptr(), *shape, stream_ptr())
+    torch.cuda.synchronize()
+    assert_bit_exact(host(out), host(out_ref), "unpatchify_3d vs reference")
+    assert_bit_exact(host(out), O.unpatchify_3d(p, *shape, init=fill), "unpatchify_3d vs oracle")
+
+
+SAMPLER_N = [262144, 1000003, 4 * 1024 * 1024]
+
+
+@pytest.mark.parametrize("offset", [0, 1])
+@pytest.mark.parametrize("sigma_next", [0.0, 0.61])
+@pytest.mark.parametrize("N", SAMPLER_N)
+def test_cfg_euler_step(anima, ref, rng, N, sigma_next, offset):
+    s, p, q = (O.randn_bf16(rng, N) for _ in range(3))
+    ds, dp, dq = _bf_at(s, offset), _bf_at(p, offset), _bf_at(q, offset)
+    args = (4.5, 0.73, sigma_next, N)
+    out = _bf_at(np.zeros(N, np.uint16), offset)
+    anima.cfg_euler_step(ds, dp, dq, out, *args)
+    out_ref = _bf_at(np.zeros(N, np.uint16), offset)
+    ref.cfg_euler_step_bf16(ds.data_ptr(), dp.data_ptr(), dq.data_ptr(), out_ref.data_ptr(), *args, stream_ptr())
+    xi = _bf_at(s, offset)
+    anima.cfg_euler_step(xi, dp, dq, xi, *args)  # in place (pipeline.cpp:433)
+    torch.cuda.synchronize()
+    assert_bit_exact(host(out), host(out_ref), "cfg_euler_step vs reference")
+    assert_bit_exact(host(xi), host(out_ref), "cfg_euler_step in place")
+    if N <= ORACLE_MAX_ELEMS:
+        assert_one_ulp(host(out), O.cfg_euler_step(s, p, q, 4.5, 0.73, sigma_next), "cfg_euler_step vs oracle")
+
+
+@pytest.mark.parametrize("eta", [0.0, 1.0, 0.5])
+@pytest.mark.parametrize("N", SAMPLER_N)
+def test_cfg_euler_a_rf_step(anima, ref, rng, N, eta):
+    s, p, q, r = (O.randn_bf16(rng, N) for _ in range(4))
+    ds, dp, dq, dr = dev(s), dev(p), dev(q), dev(r)
+    args = (3.5, 0.8, 0.55, eta, 1.0, N)
+    out, out_ref = empty_bf16(N), empty_bf16(N)
+    anima.cfg_euler_a_rf_step(ds, dp, dq, dr, out, *args)
+    ref.cfg_euler_a_rf_step_bf16(ds.data_ptr(), dp.data_ptr(), dq.data_ptr(), dr.data_ptr(), out_ref.data_ptr(), *args,
+                                 stream_ptr())
+    xi = dev(s)
+    anima.cfg_euler_a_rf_step(xi, dp, dq, dr, xi, *args)  # in place (pipeline.cpp:426)
+    torch.cuda.synchronize()
+    assert_bit_exact(host(out), host(out_ref), "cfg_euler_a_rf_step vs reference")
+    assert_bit_exact(host(xi), host(out_ref), "cfg_euler_a_rf_step in place")
+    if N <= ORACLE_MAX_ELEMS:
+        assert_one_ulp(host(out), O.cfg_euler_a_rf_step(s, p, q, r, 3.5, 0.8, 0.55, eta, 1.0),
+                       "cfg_euler_a_rf_step vs oracle")
+
+
+# (old_denoised, old_denoised_d, rand_noise, noise_coeff, denoised_d_out) as pipeline.cpp:400-418 passes them
+ER_SDE_CASES = [(False, False, False, 0.0, False), (True, False, False, 0.0, True), (True, True, True, 0.3, True),
+                (True, True, False, 0.0, True), (False, False, True, 0.25, False), (True, False, True, 0.2, False)]
+
+
+@pytest.mark.parametrize("case", ER_SDE_CASES)
+@pytest.mark.parametrize("N", [262144, 1000003])
+def test_cfg_er_sde_full_step(anima, ref, rng, N, case):
+    use_od, use_odd, use_rand, noise_coeff, use_ddo = case
+    x, p, q, od, odd, rn = (O.randn_bf16(rng, N) for _ in range(6))
+    dp, dq = dev(p), dev(q)
+    dod, dodd, drn = (dev(a) if u else None for a, u in ((od, use_od), (odd, use_odd), (rn, use_rand)))
+    coeffs = (4.0, 0.7, 0.93, 0.051, 1.7, 0.02, 2.3, 0.004, noise_coeff, N)
+    outs = {}
+    for who in ("anima", "ref"):
+        dx, den = dev(x), torch.zeros(N, dtype=torch.int16, device="cuda")
+        ddo = torch.zeros(N, dtype=torch.int16, device="cuda") if use_ddo else None
+        if who == "anima":
+            anima.cfg_er_sde_full_step(dx, dp, dq, den, dod, ddo, dodd, drn, *coeffs)
+        else:
+            P = lambda t: None if t is None else t.data_ptr()  # noqa: E731
+            ref.cfg_er_sde_full_step_bf16(dx.data_ptr(), dp.data_ptr(), dq.data_ptr(), den.data_ptr(), P(dod), P(ddo),
+                                          P(dodd), P(drn), *coeffs, stream_ptr())
+        outs[who] = (dx, den, ddo)
+    torch.cuda.synchronize()
+    for k, name in enumerate(("x", "denoised", "denoised_d")):
+        if outs["anima"][k] is not None:
+            assert_bit_exact(host(outs["anima"][k]), host(outs["ref"][k]), f"cfg_er_sde {name} vs reference")
+    ox, oden, odd_o = O.cfg_er_sde_full_step(x, p, q, od if use_od else None, odd if use_odd else None,
+                                            rn if use_rand else None, *coeffs[:-1], want_dd=use_ddo)
+    assert_one_ulp(host(outs["anima"][0]), ox, "cfg_er_sde x vs oracle")
+    assert_one_ulp(host(outs["anima"][1]), oden, "cfg_er_sde denoised vs oracle")
+    if odd_o is not None:
+        assert_one_ulp(host(outs["anima"][2]), odd_o, "cfg_er_sde denoised_d vs oracle")
