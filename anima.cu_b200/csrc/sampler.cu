@@ -219,6 +219,35 @@ __device__ __forceinline__ void unpatchify_elem(const PatchArgs &a, I j) {
     a.dst[j] = a.src[(int64_t)b * a.per_item + (int64_t)tok * a.pd + d];
 }
 
+// The DiT's patches (pT = 1, pH = pW = 2, T a multiple of 1, H and W even): one thread per
+// (item, token, channel) moves the 2x2 patch as two 4-byte row pieces on the volume side and
+// 8 contiguous bytes (patchify: c-major patch order) or 4 channel-strided values (unpatchify)
+// on the token side.
+template <bool kUnpatch>
+__global__ void __launch_bounds__(kSmpBlock) patch_kernel_122(PatchArgs a, int64_t items) {
+    pdl_wait();
+    const int64_t tid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x, stride = (int64_t)gridDim.x * blockDim.x;
+    for (int64_t q = tid; q < items; q += stride) {  // q = (b * S + tok) * C + c
+        const int64_t bt = q / a.C;
+        const int c = (int)(q - bt * a.C);
+        const int64_t b = bt / a.S, tok = bt - b * a.S;
+        const int fw = (int)(tok % a.pe_w), fh = (int)((tok / a.pe_w) % a.pe_h), t = (int)(tok / ((int64_t)a.pe_w * a.pe_h));
+        const int64_t row0 = (((int64_t)b * a.C + c) * a.T + t) * a.H + 2 * fh;
+        uint32_t *v0 = reinterpret_cast<uint32_t *>(kUnpatch ? a.dst : const_cast<anima_bf16 *>(a.src)) +
+                       (row0 * a.W + 2 * fw) / 2;
+        uint32_t *v1 = v0 + a.W / 2;
+        if constexpr (!kUnpatch) {  // d = c*4 + ph*2 + pw
+            const uint2 o = make_uint2(*v0, *v1);
+            *reinterpret_cast<uint2 *>(a.dst + ((int64_t)b * a.S + tok) * a.pd + 4 * c) = o;
+        } else {  // d = (ph*2 + pw)*C + c
+            const anima_bf16 *sp = a.src + ((int64_t)b * a.S + tok) * a.pd + c;
+            *v0 = (uint32_t)sp[0] | (uint32_t)sp[a.C] << 16;
+            *v1 = (uint32_t)sp[2 * a.C] | (uint32_t)sp[3 * a.C] << 16;
+        }
+    }
+    pdl_launch();
+}
+
 template <bool kUnpatch>
 __global__ void __launch_bounds__(kSmpBlock) patch_kernel(PatchArgs a) {
     pdl_wait();
@@ -402,6 +431,16 @@ int patch_op(const anima_bf16 *src, anima_bf16 *dst, int B, int C, int T, int H,
     const int64_t ns = (int64_t)B * (kUnpatch ? a.per_item : a.vol) * 2, nd = a.total * 2;
     if (overlaps(src, ns, dst, nd)) return ANIMA_ERR_OVERLAP;
     int err = ANIMA_OK;
+    // 2x2 spatial patches over whole rows: every row piece is 4-byte aligned when the
+    // volume is, and the 8-byte token-side store (patchify) is aligned when the tokens are
+    if (pT == 1 && pH == 2 && pW == 2 && H % 2 == 0 && W % 2 == 0 && aligned_to(kUnpatch ? dst : src, 4) &&
+        (kUnpatch || aligned_to(dst, 8))) {
+        const int64_t items = (int64_t)B * a.S * C;
+        const unsigned grid = wave_grid((const void *)patch_kernel_122<kUnpatch>, kSmpBlock, 0, items, &err);
+        if (err) return err;
+        launch(patch_kernel_122<kUnpatch>, grid, kSmpBlock, 0, stream, a, items);
+        return launch_status();
+    }
     const unsigned grid = wave_grid((const void *)patch_kernel<kUnpatch>, kSmpBlock, 0, a.total, &err);
     if (err) return err;
     launch(patch_kernel<kUnpatch>, grid, kSmpBlock, 0, stream, a);
