@@ -705,3 +705,47 @@ def test_cfg_er_sde_full_step(anima, ref, rng, N, case):
     assert_one_ulp(host(outs["anima"][1]), oden, "cfg_er_sde denoised vs oracle")
     if odd_o is not None:
         assert_one_ulp(host(outs["anima"][2]), odd_o, "cfg_er_sde denoised_d vs oracle")
+
+
+# ---------------------------------------------------------------- random row shapes
+def _random_row_shapes(n=24, seed=7):
+    r = np.random.default_rng(seed)
+    out = []
+    for _ in range(n):
+        D = int(2 * r.integers(1, 2049))          # any even width up to 4096
+        if r.random() < 0.4:
+            D = int(64 * r.integers(1, 33))        # the segment widths
+        N = int(r.integers(1, max(2, min(3000, (1 << 22) // D))))
+        out.append((N, D))
+    return out
+
+
+@pytest.mark.parametrize("N,D", _random_row_shapes())
+def test_row_norms_random_shapes(anima, ref, rng, N, D):
+    """Every row norm against the reference kernel on a seeded sweep of (N, D)."""
+    x, y = O.randn_bf16(rng, (N, D)), O.randn_bf16(rng, (N, D))
+    w, g, sc, sh = _weight(rng, D), _modvec(rng, D), _modvec(rng, D), _modvec(rng, D)
+    dx, dy, dw, dg, dsc, dsh = dev(x), dev(y), dev(w), dev(g), dev(sc), dev(sh)
+    S = stream_ptr()
+    pairs = []
+    o, r_ = empty_bf16((N, D)), empty_bf16((N, D))
+    anima.rms_norm(dx, dw, o, N, D, 1e-6)
+    ref.rms_norm_bf16(dx.data_ptr(), dw.data_ptr(), r_.data_ptr(), N, D, 1e-6, S)
+    pairs.append(("rms_norm", o, r_))
+    o, r_ = empty_bf16((N, D)), empty_bf16((N, D))
+    anima.layer_norm(dx, o, N, D, 1e-6)
+    ref.layer_norm_bf16(dx.data_ptr(), r_.data_ptr(), N, D, 1e-6, S)
+    pairs.append(("layer_norm", o, r_))
+    o, r_ = empty_bf16((N, D)), empty_bf16((N, D))
+    anima.adaln_layernorm(dx, dsc, dsh, o, N, D, 1e-6)
+    ref.adaln_layernorm_bf16(dx.data_ptr(), dsc.data_ptr(), dsh.data_ptr(), r_.data_ptr(), N, D, 1e-6, S)
+    pairs.append(("adaln_layernorm", o, r_))
+    h, hr = dev(x), dev(x)
+    o, r_ = empty_bf16((N, D)), empty_bf16((N, D))
+    anima.residual_gate_adaln(h, dy, dg, dsc, dsh, o, N, D, 1e-6)
+    ref.residual_gate_adaln_bf16(hr.data_ptr(), dy.data_ptr(), dg.data_ptr(), dsc.data_ptr(), dsh.data_ptr(),
+                                 r_.data_ptr(), N, D, 1e-6, S)
+    pairs += [("residual_gate_adaln hidden", h, hr), ("residual_gate_adaln normed", o, r_)]
+    torch.cuda.synchronize()
+    for name, got, want in pairs:
+        assert_bit_exact(host(got), host(want), f"{name} [{N}, {D}] vs reference")
