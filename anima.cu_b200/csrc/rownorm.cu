@@ -464,7 +464,7 @@ __global__ void __launch_bounds__(SegShape<Op::NIN>::kThreads, SegShape<Op::NIN>
     constexpr int NIN = Op::NIN, NOUT = Op::NOUT, NB = Op::NB;
     constexpr int G = 32 / NW;  // rows per unit
     constexpr int NST = SegShape<NIN>::kStages;
-    constexpr int kSegWarps = SegShape<NIN>::kWarps, kSegThreads = SegShape<NIN>::kThreads;
+    constexpr int kSegWarps = SegShape<NIN>::kWarps;
     constexpr int kRowChunks = NW * 8;
     extern __shared__ __align__(16) unsigned char seg_smem[];
     float *bc = reinterpret_cast<float *>(seg_smem);
