@@ -962,7 +962,14 @@ def main():
         n_cores = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else (os.cpu_count() or 1)
         v1, sample1 = cpu_baseline_sample(blocks=2, threads=1)
         vn, samplen = cpu_baseline_sample(blocks=4 if n_cores >= 8 else 2, threads=n_cores)
+        cpu_model = None
+        try:
+            with open("/proc/cpuinfo") as f:
+                cpu_model = next((l.split(":", 1)[1].strip() for l in f if l.startswith("model name")), None)
+        except OSError:
+            pass
         cpu = {"value": round(vn, 3), "unit": "GB/s", "cores": n_cores, "kind": "port", "sample": samplen,
+               "cpu_model": cpu_model, "host_threads": os.cpu_count(),
                "single_thread": {"value": round(v1, 3), "cores": 1, "sample": sample1},
                "note": "CPU restatement of the reference kernels (oracle/oracle.c, -O2), rows split over the "
                        "host's threads; the reference itself has no CPU implementation of these ops"}
