@@ -267,21 +267,25 @@ __global__ void __launch_bounds__(kRopeBlock) qk_norm_rope_128(QkArgs a) {
     const float r = rsqrtf(__fdiv_rn(sq, (float)HD) + a.eps);
     pdl_launch();
     if (!live) return;
-    float x0[8], x1[8], w0[8], w1[8], c[8], sn[8], o0[8], o1[8];
-    unpack8(v[0], x0);
-    unpack8(v[1], x1);
-    unpack8(w[0], w0);
-    unpack8(w[1], w1);
-    unpack8(cv, c);
-    unpack8(sv, sn);
+    // rms_norm.cu:62-64 ((x*r)*w, stored as bf16) then rope.cu:101-107, on element pairs with
+    // packed fp32x2 ops (each lane rounds as the scalar op does)
+    Vec8 o0, o1;
 #pragma unroll
-    for (int e = 0; e < 8; ++e) {
-        const float n0 = bf16_round((x0[e] * r) * w0[e]);  // rms_norm.cu:62-64, stored as bf16
-        const float n1 = bf16_round((x1[e] * r) * w1[e]);
-        rot_bf16(n0, n1, c[e], sn[e], o0[e], o1[e]);
+    for (int j = 0; j < 4; ++j) {
+        const float2 rr = make_float2(r, r);
+        const float2 n0 = __fmul2_rn(__fmul2_rn(make_float2(bf_lo(v[0].w[j]), bf_hi(v[0].w[j])), rr),
+                                     make_float2(bf_lo(w[0].w[j]), bf_hi(w[0].w[j])));
+        const float2 n1 = __fmul2_rn(__fmul2_rn(make_float2(bf_lo(v[1].w[j]), bf_hi(v[1].w[j])), rr),
+                                     make_float2(bf_lo(w[1].w[j]), bf_hi(w[1].w[j])));
+        const uint32_t p0 = pack_bf2(n0.x, n0.y), p1 = pack_bf2(n1.x, n1.y);
+        float2 a, b;
+        rot_bf16_x2(make_float2(bf_lo(p0), bf_hi(p0)), make_float2(bf_lo(p1), bf_hi(p1)),
+                    make_float2(bf_lo(cv.w[j]), bf_hi(cv.w[j])), make_float2(bf_lo(sv.w[j]), bf_hi(sv.w[j])), a, b);
+        o0.w[j] = pack_bf2(a.x, a.y);
+        o1.w[j] = pack_bf2(b.x, b.y);
     }
-    st_vec(p, pack8(o0));
-    st_vec(p + 64, pack8(o1));
+    st_vec(p, o0);
+    st_vec(p + 64, o1);
 }
 
 bool bf16_ok(const void *p) { return aligned_to(p, 2); }
