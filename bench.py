@@ -915,7 +915,7 @@ def main():
     h_out = torch.empty((chain.R, chain.D), dtype=torch.bfloat16).pin_memory()
     h_in.copy_(chain.sets[0]["hidden"].cpu())
     m_in.copy_(chain.mod_raw.cpu())
-    e2e_steps = max(3, min(args.steps, 20))
+    e2e_steps = max(3, min(args.steps, 50))
     torch.cuda.synchronize()
     a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     a.record()
