@@ -18,11 +18,15 @@
 // shapes put this one first or within 5 % of first everywhere: fewer threads starve the
 // SiLU epilogue, narrower tiles halve the 128-byte channel segments.
 //
+// When the tiles are few, channel_norm_cluster (below) spreads each over a cluster of CTAs.
+//
 // Tensors whose rows are not 16-byte aligned (spatial % 8 != 0) or whose tile would not
 // fit in shared memory use the generic kernel: one thread per pixel, the reference's
 // arithmetic, one launch for all batch items.
 #include "common.cuh"
 #include "activation.cuh"
+
+#include <cooperative_groups.h>
 
 namespace anima {
 namespace {
@@ -130,6 +134,93 @@ __global__ void __launch_bounds__(kCnBlock) channel_norm_tile(CnArgs a) {
     }
 }
 
+// Cluster variant: a 64-pixel tile is spread over a cluster of kCnCluster CTAs, CTA r staging
+// channels [r*Cq, (r+1)*Cq) (Cq = ceil(C / kCnCluster)) into its own shared memory, so loading
+// and the epilogue run on kCnCluster times more threads -- what the small VAE shapes (few tiles
+// per SM) lack. The per-pixel sum stays one serial chain in the reference's channel order: CTA
+// 0 sums its slice, hands the 64 partial sums to CTA 1 through distributed shared memory, CTA 1
+// continues over its slice, and so on; the last CTA forms the rms and writes it into every
+// CTA. Every read of x is local. One cluster barrier per hand-off, reached by every thread of
+// every CTA; the last also keeps each CTA's shared memory alive until all writes into it are
+// done.
+constexpr int kCnCluster = 4;
+
+template <bool kSilu>
+__global__ void __launch_bounds__(kCnBlock) channel_norm_cluster(CnArgs a, int Cq) {
+    namespace cg = cooperative_groups;
+    cg::cluster_group cluster = cg::this_cluster();
+    pdl_wait();
+    constexpr int kVecs = kCnPix / 8;
+    extern __shared__ __align__(16) anima_bf16 tile[];  // [Cq][kCnPix]: this CTA's channel slice
+    __shared__ __align__(16) float rms_s[kCnPix];
+    const unsigned rank = cluster.block_rank();
+    const int64_t t = blockIdx.x / kCnCluster;  // tile index
+    const int b = (int)(t / a.tiles_per_image);
+    const int s_tile = (int)(t - (int64_t)b * a.tiles_per_image) * kCnPix;
+    const int live_vecs = min(kCnPix, a.spatial - s_tile) / 8;
+    const int64_t img = (int64_t)b * a.C * a.spatial;
+    const int c0 = (int)rank * Cq, c1 = min(a.C, c0 + Cq);
+    const int nchunks = max(0, c1 - c0) * kVecs;
+
+    for (int q = threadIdx.x; q < nchunks; q += kCnBlock) {
+        const int c = q / kVecs, v = q % kVecs;
+        if (v < live_vecs)
+            cp_async16(tile + c * kCnPix + v * 8, a.x + img + (int64_t)(c0 + c) * a.spatial + s_tile + v * 8);
+    }
+    cp_async_wait_all();
+    __syncthreads();
+
+    __shared__ float part_s[kCnPix];  // the chain's partial sums, handed over by CTA rank - 1
+    for (int r = 0; r < kCnCluster; ++r) {  // slices in channel order
+        if (rank == (unsigned)r && threadIdx.x < kCnPix) {
+            const int p = threadIdx.x;
+            float q = r == 0 ? 0.0f : part_s[p];
+            if (p < live_vecs * 8) {
+                const __nv_bfloat16 *col = reinterpret_cast<const __nv_bfloat16 *>(tile) + p;
+                const int n = c1 - c0, full = n & ~7;
+                for (int c = 0; c < full; c += 8) {
+                    float f[8];
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) f[j] = __bfloat162float(col[(c + j) * kCnPix]);
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) q = __fmaf_rn(f[j], f[j], q);
+                }
+                for (int c = full; c < n; ++c) {
+                    const float f = __bfloat162float(col[c * kCnPix]);
+                    q = __fmaf_rn(f, f, q);
+                }
+            }
+            if (r + 1 < kCnCluster) {
+                cluster.map_shared_rank(part_s, r + 1)[p] = q;
+            } else {
+                const float rv = rsqrtf(__fdiv_rn(q, (float)a.C) + a.eps);
+                for (int k = 0; k < kCnCluster; ++k) cluster.map_shared_rank(rms_s, k)[p] = rv;
+            }
+        }
+        cluster.sync();
+    }
+    pdl_launch();
+
+    for (int q = threadIdx.x; q < nchunks; q += kCnBlock) {
+        const int c = q / kVecs, v = q % kVecs;
+        if (v >= live_vecs) continue;
+        const Vec8 xv = *reinterpret_cast<const Vec8 *>(tile + c * kCnPix + v * 8);
+        const float4 r0 = reinterpret_cast<const float4 *>(rms_s)[2 * v];
+        const float4 r1 = reinterpret_cast<const float4 *>(rms_s)[2 * v + 1];
+        const float r[8] = {r0.x, r0.y, r0.z, r0.w, r1.x, r1.y, r1.z, r1.w};
+        const float gm = ldb(a.gamma + c0 + c);
+        Vec8 o;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const float2 t2 = __fmul2_rn(make_float2(bf_lo(xv.w[j]), bf_hi(xv.w[j])), make_float2(r[2 * j], r[2 * j + 1]));
+            const float2 u = __fmul2_rn(t2, make_float2(gm, gm));
+            o.w[j] = pack_bf2(u.x, u.y);
+        }
+        if constexpr (kSilu) o = fast_chunk<SiluF>(o);
+        st_vec(a.out + img + (int64_t)(c0 + c) * a.spatial + s_tile + v * 8, o);
+    }
+}
+
 // Reference-order kernel for any shape: one thread per (image, pixel).
 template <bool kSilu>
 __global__ void channel_norm_serial(CnArgs a, int64_t pixels) {
@@ -167,7 +258,16 @@ int channel_norm(const anima_bf16 *x, const anima_bf16 *gamma, anima_bf16 *out, 
     CnArgs a{x, gamma, out, C, spatial, eps, (spatial + kCnPix - 1) / kCnPix};
     const int64_t tiles = (int64_t)B * a.tiles_per_image;
     const int64_t smem = (int64_t)C * kCnPix * 2;
-    if (spatial % 8 == 0 && aligned16(x) && aligned16(out) && smem <= kCnMaxSmem &&
+    const int Cq = (C + kCnCluster - 1) / kCnCluster;
+    // Few tiles (at most two per SM): spread each over a cluster. Many tiles keep every SM busy
+    // already, and the cluster's hand-offs would then only serialise each tile (measured).
+    if (spatial % 8 == 0 && aligned16(x) && aligned16(out) && C >= 64 && (int64_t)Cq * kCnPix * 2 <= kCnMaxSmem &&
+        tiles <= 2 * (int64_t)sm_count()) {
+        auto kern = channel_norm_cluster<kSilu>;
+        if (int e = allow_dynamic_smem((const void *)kern, kCnMaxSmem, kSilu ? 5 : 4)) return e;
+        launch_cluster(kern, kCnCluster, (unsigned)(tiles * kCnCluster), kCnBlock, (size_t)Cq * kCnPix * 2, stream, a,
+                       Cq);
+    } else if (spatial % 8 == 0 && aligned16(x) && aligned16(out) && smem <= kCnMaxSmem &&
         tiles < 2147483647) {
         auto kern = channel_norm_tile<kSilu>;
         if (int e = allow_dynamic_smem((const void *)kern, kCnMaxSmem, kSilu ? 1 : 0)) return e;

@@ -505,7 +505,7 @@ def test_embedding_lookup_bad_ids(anima, rng, D):
 # ---------------------------------------------------------------- VAE channel norm
 @pytest.mark.parametrize("B,C,H,W", [(1, 512, 32, 32), (2, 96, 16, 16), (1, 128, 8, 12), (1, 100, 5, 7),
                                      (3, 16, 4, 4), (1, 1536, 8, 8), (2, 100, 5, 8), (1, 3, 16, 16),
-                                     (1, 4000, 2, 4)])
+                                     (1, 4000, 2, 4), (1, 64, 160, 160), (1, 65, 8, 8)])
 def test_rms_norm_channel(anima, ref, rng, B, C, H, W):
     sp = H * W
     x, g = O.randn_bf16(rng, (B, C, sp)), _weight(rng, C)
@@ -522,7 +522,8 @@ def test_rms_norm_channel(anima, ref, rng, B, C, H, W):
         assert_one_ulp(host(out), O.rms_norm_channel(x, g, B, C, sp), "rms_norm_channel vs oracle")
 
 
-@pytest.mark.parametrize("B,C,H,W", [(1, 512, 32, 32), (1, 96, 10, 10), (2, 100, 5, 8), (1, 256, 64, 64)])
+@pytest.mark.parametrize("B,C,H,W", [(1, 512, 32, 32), (1, 96, 10, 10), (2, 100, 5, 8), (1, 256, 64, 64),
+                                     (1, 64, 160, 160)])
 def test_rms_norm_channel_silu_matches_reference_chain(anima, ref, rng, B, C, H, W):
     sp = H * W
     x, g = O.randn_bf16(rng, (B, C, sp)), _weight(rng, C)
