@@ -41,6 +41,9 @@ SIGNATURES = {
     "anima_patchify_3d_bf16": (P, P) + (I32,) * 8 + (P,),
     "anima_unpatchify_3d_bf16": (P, P) + (I32,) * 8 + (P,),
     "anima_channel_scale_shift_bf16": (P, P, P, P, I32, I32, I32, P),
+    "anima_conv_bias_add_bf16": (P, P, P, I32, I32, I32, P),
+    "anima_conv_bias_residual_add_bf16": (P, P, P, P, I32, I32, I32, P),
+    "anima_conv_bias_rms_norm_channel_silu_bf16": (P, P, P, P, I32, I32, I32, F32, P),
     "anima_scale_shift_bcast_bf16": (P, P, P, P, I32, I32, P),
     "anima_residual_gate_bcast_bf16": (P, P, P, P, I32, I32, P),
     "anima_gated_gelu_bf16": (P, P, P, I64, P),
@@ -253,6 +256,20 @@ def patchify_3d(src, dst, B, C, T, H, W, pT, pH, pW, stream=None):
 
 def unpatchify_3d(src, dst, B, C, T, H, W, pT, pH, pW, stream=None):
     call("anima_unpatchify_3d_bf16", _ptr(src), _ptr(dst), B, C, T, H, W, pT, pH, pW, _stream(stream))
+
+
+def conv_bias_add(x, bias, out, B, C, spatial, stream=None):
+    call("anima_conv_bias_add_bf16", _ptr(x), _ptr(bias), _ptr(out), B, C, spatial, _stream(stream))
+
+
+def conv_bias_residual_add(x, bias, residual, out, B, C, spatial, stream=None):
+    call("anima_conv_bias_residual_add_bf16", _ptr(x), _ptr(bias), _ptr(residual), _ptr(out), B, C, spatial,
+         _stream(stream))
+
+
+def conv_bias_rms_norm_channel_silu(x, bias, gamma, out, B, C, spatial, eps=1e-6, stream=None):
+    call("anima_conv_bias_rms_norm_channel_silu_bf16", _ptr(x), _ptr(bias), _ptr(gamma), _ptr(out), B, C, spatial,
+         eps, _stream(stream))
 
 
 def channel_scale_shift(x, scale, shift, out, B, C, spatial, stream=None):

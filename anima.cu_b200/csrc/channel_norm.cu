@@ -20,6 +20,10 @@
 //
 // When the tiles are few, channel_norm_cluster (below) spreads each over a cluster of CTAs.
 //
+// The conv-bias form (kBias) first adds the convolution's bias[c] to the staged tile in place,
+// rounded to bf16 as the reference's bias launch stores it (causal_conv3d.cu:187-195); the
+// bias is loaded into shared memory while the tile's copies are in flight.
+//
 // Tensors whose rows are not 16-byte aligned (spatial % 8 != 0) or whose tile would not
 // fit in shared memory use the generic kernel: one thread per pixel, the reference's
 // arithmetic, one launch for all batch items.
@@ -47,15 +51,32 @@ __device__ __forceinline__ void cp_async_wait_all() {
     asm volatile("cp.async.commit_group;\ncp.async.wait_group 0;" ::: "memory");
 }
 
+// causal_conv3d.cu:193 on a staged 16-byte chunk in shared memory: x + bias[c], rounded to
+// bf16 as the reference's bias launch stores it. The reference adds in fp32 and rounds to
+// bf16; for two bf16 operands that is the exact sum rounded once (when their exponents are at
+// most 16 apart the fp32 sum is exact, and otherwise the smaller addend lies far below half a
+// bf16 ulp of the larger, which both roundings then return), so a packed bf16 add gives the
+// same bits in a quarter of the instructions.
+__device__ __forceinline__ uint32_t bias_pair(const anima_bf16 *p) {
+    const uint32_t h = *reinterpret_cast<const unsigned short *>(p);
+    return h | (h << 16);
+}
+__device__ __forceinline__ void add_bias8(anima_bf16 *chunk, uint32_t b2) {
+    Vec8 &v = *reinterpret_cast<Vec8 *>(chunk);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) asm("add.rn.bf16x2 %0, %0, %1;" : "+r"(v.w[j]) : "r"(b2));
+}
+
 struct CnArgs {
     const anima_bf16 *x, *gamma;
     anima_bf16 *out;
+    const anima_bf16 *bias;  // the convolution's bias[C], added first (kBias kernels only)
     int C, spatial;
     float eps;
     int tiles_per_image;
 };
 
-template <bool kSilu>
+template <bool kSilu, bool kBias>
 __global__ void __launch_bounds__(kCnBlock) channel_norm_tile(CnArgs a) {
     pdl_wait();
     constexpr int kVecs = kCnPix / 8;  // 16-byte chunks per channel row of the tile
@@ -73,8 +94,19 @@ __global__ void __launch_bounds__(kCnBlock) channel_norm_tile(CnArgs a) {
         if (v < live_vecs)
             cp_async16(tile + c * kCnPix + v * 8, a.x + img + (int64_t)c * a.spatial + s_tile + v * 8);
     }
+    uint32_t *bias_s = reinterpret_cast<uint32_t *>(tile + a.C * kCnPix);  // [C] (b, b) pairs (kBias)
+    if constexpr (kBias) {  // loads in flight with the tile's copies
+        for (int c = threadIdx.x; c < a.C; c += kCnBlock) bias_s[c] = bias_pair(a.bias + c);
+    }
     cp_async_wait_all();
     __syncthreads();
+    if constexpr (kBias) {
+        for (int q = threadIdx.x; q < nchunks; q += kCnBlock) {
+            const int c = q / kVecs, v = q % kVecs;
+            if (v < live_vecs) add_bias8(tile + c * kCnPix + v * 8, bias_s[c]);
+        }
+        __syncthreads();
+    }
 
     // vae_kernels.cu:68-73: serial sum over channels, one thread per pixel.
     if (threadIdx.x < kCnPix) {
@@ -145,7 +177,7 @@ __global__ void __launch_bounds__(kCnBlock) channel_norm_tile(CnArgs a) {
 // done.
 constexpr int kCnCluster = 4;
 
-template <bool kSilu>
+template <bool kSilu, bool kBias>
 __global__ void __launch_bounds__(kCnBlock) channel_norm_cluster(CnArgs a, int Cq) {
     namespace cg = cooperative_groups;
     cg::cluster_group cluster = cg::this_cluster();
@@ -167,8 +199,19 @@ __global__ void __launch_bounds__(kCnBlock) channel_norm_cluster(CnArgs a, int C
         if (v < live_vecs)
             cp_async16(tile + c * kCnPix + v * 8, a.x + img + (int64_t)(c0 + c) * a.spatial + s_tile + v * 8);
     }
+    uint32_t *bias_s = reinterpret_cast<uint32_t *>(tile + Cq * kCnPix);  // [Cq] (b, b) pairs (kBias)
+    if constexpr (kBias) {
+        for (int c = threadIdx.x; c < c1 - c0; c += kCnBlock) bias_s[c] = bias_pair(a.bias + c0 + c);
+    }
     cp_async_wait_all();
     __syncthreads();
+    if constexpr (kBias) {
+        for (int q = threadIdx.x; q < nchunks; q += kCnBlock) {
+            const int c = q / kVecs, v = q % kVecs;
+            if (v < live_vecs) add_bias8(tile + c * kCnPix + v * 8, bias_s[c]);
+        }
+        __syncthreads();
+    }
 
     __shared__ float part_s[kCnPix];  // the chain's partial sums, handed over by CTA rank - 1
     for (int r = 0; r < kCnCluster; ++r) {  // slices in channel order
@@ -222,7 +265,7 @@ __global__ void __launch_bounds__(kCnBlock) channel_norm_cluster(CnArgs a, int C
 }
 
 // Reference-order kernel for any shape: one thread per (image, pixel).
-template <bool kSilu>
+template <bool kSilu, bool kBias>
 __global__ void channel_norm_serial(CnArgs a, int64_t pixels) {
     pdl_wait();
     for (int64_t p = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; p < pixels;
@@ -230,54 +273,61 @@ __global__ void channel_norm_serial(CnArgs a, int64_t pixels) {
         const int64_t b = p / a.spatial, s = p % a.spatial;
         const anima_bf16 *xb = a.x + b * a.C * (int64_t)a.spatial;
         anima_bf16 *ob = a.out + b * a.C * (int64_t)a.spatial;
+        const auto xin = [&](int c) {
+            const float f = ldb(xb + (int64_t)c * a.spatial + s);
+            return kBias ? bf16_round(f + ldb(a.bias + c)) : f;
+        };
         float q = 0.0f;
         for (int c = 0; c < a.C; ++c) {
-            const float f = ldb(xb + (int64_t)c * a.spatial + s);
+            const float f = xin(c);
             q = __fmaf_rn(f, f, q);
         }
         const float r = rsqrtf(__fdiv_rn(q, (float)a.C) + a.eps);
         for (int c = 0; c < a.C; ++c) {
             const int64_t i = (int64_t)c * a.spatial + s;
-            float o = (ldb(xb + i) * r) * ldb(a.gamma + c);
+            float o = (xin(c) * r) * ldb(a.gamma + c);
             if constexpr (kSilu) o = silu_f(bf16_round(o));
             *reinterpret_cast<__nv_bfloat16 *>(ob + i) = __float2bfloat16_rn(o);
         }
     }
 }
 
-template <bool kSilu>
+template <bool kSilu, bool kBias = false>
 int channel_norm(const anima_bf16 *x, const anima_bf16 *gamma, anima_bf16 *out, int B, int C,
-                 int spatial, float eps, cudaStream_t stream) {
+                 int spatial, float eps, cudaStream_t stream, const anima_bf16 *bias = nullptr) {
     if (B < 0 || C <= 0 || spatial < 0) return ANIMA_ERR_BAD_SHAPE;
     const int64_t n = (int64_t)B * C * spatial;
     if (n == 0) return ANIMA_OK;
-    if (!x || !gamma || !out) return ANIMA_ERR_NULL_POINTER;
-    if (!aligned_to(x, 2) || !aligned_to(gamma, 2) || !aligned_to(out, 2)) return ANIMA_ERR_MISALIGNED;
-    if (partial_overlap(x, n * 2, out, n * 2) || partial_overlap(gamma, (int64_t)C * 2, out, n * 2))
+    if (!x || !gamma || !out || (kBias && !bias)) return ANIMA_ERR_NULL_POINTER;
+    if (!aligned_to(x, 2) || !aligned_to(gamma, 2) || !aligned_to(out, 2) || (kBias && !aligned_to(bias, 2)))
+        return ANIMA_ERR_MISALIGNED;
+    if (partial_overlap(x, n * 2, out, n * 2) || partial_overlap(gamma, (int64_t)C * 2, out, n * 2) ||
+        (kBias && overlaps(bias, (int64_t)C * 2, out, n * 2)))
         return ANIMA_ERR_OVERLAP;
-    CnArgs a{x, gamma, out, C, spatial, eps, (spatial + kCnPix - 1) / kCnPix};
+    CnArgs a{x, gamma, out, bias, C, spatial, eps, (spatial + kCnPix - 1) / kCnPix};
     const int64_t tiles = (int64_t)B * a.tiles_per_image;
-    const int64_t smem = (int64_t)C * kCnPix * 2;
+    const int64_t per_ch = kCnPix * 2 + (kBias ? 4 : 0);  // shared bytes per channel: tile row (+ bias)
+    const int64_t smem = (int64_t)C * per_ch;
     const int Cq = (C + kCnCluster - 1) / kCnCluster;
     // Few tiles (at most two per SM): spread each over a cluster. Many tiles keep every SM busy
     // already, and the cluster's hand-offs would then only serialise each tile (measured).
-    if (spatial % 8 == 0 && aligned16(x) && aligned16(out) && C >= 64 && (int64_t)Cq * kCnPix * 2 <= kCnMaxSmem &&
+    if (spatial % 8 == 0 && aligned16(x) && aligned16(out) && C >= 64 && (int64_t)Cq * per_ch <= kCnMaxSmem &&
         tiles <= 2 * (int64_t)sm_count()) {
-        auto kern = channel_norm_cluster<kSilu>;
-        if (int e = allow_dynamic_smem((const void *)kern, kCnMaxSmem, kSilu ? 5 : 4)) return e;
-        launch_cluster(kern, kCnCluster, (unsigned)(tiles * kCnCluster), kCnBlock, (size_t)Cq * kCnPix * 2, stream, a,
+        auto kern = channel_norm_cluster<kSilu, kBias>;
+        if (int e = allow_dynamic_smem((const void *)kern, kCnMaxSmem, kBias ? 7 : kSilu ? 5 : 4)) return e;
+        launch_cluster(kern, kCnCluster, (unsigned)(tiles * kCnCluster), kCnBlock, (size_t)(Cq * per_ch), stream, a,
                        Cq);
     } else if (spatial % 8 == 0 && aligned16(x) && aligned16(out) && smem <= kCnMaxSmem &&
         tiles < 2147483647) {
-        auto kern = channel_norm_tile<kSilu>;
-        if (int e = allow_dynamic_smem((const void *)kern, kCnMaxSmem, kSilu ? 1 : 0)) return e;
+        auto kern = channel_norm_tile<kSilu, kBias>;
+        if (int e = allow_dynamic_smem((const void *)kern, kCnMaxSmem, kBias ? 6 : kSilu ? 1 : 0)) return e;
         launch(kern, (unsigned)tiles, kCnBlock, (size_t)smem, stream, a);
     } else {
         const int64_t pixels = (int64_t)B * spatial;
         int err = ANIMA_OK;
-        const unsigned blocks = wave_grid((const void *)channel_norm_serial<kSilu>, 256, 0, pixels, &err);
+        const unsigned blocks = wave_grid((const void *)channel_norm_serial<kSilu, kBias>, 256, 0, pixels, &err);
         if (err) return err;
-        launch(channel_norm_serial<kSilu>, blocks, 256, 0, stream, a, pixels);
+        launch(channel_norm_serial<kSilu, kBias>, blocks, 256, 0, stream, a, pixels);
     }
     return launch_status();
 }
@@ -297,4 +347,10 @@ extern "C" int anima_rms_norm_channel_silu_bf16(const anima_bf16 *x, const anima
                                                 anima_bf16 *out, int B, int C, int spatial,
                                                 float eps, anima_stream_t stream) {
     return channel_norm<true>(x, gamma, out, B, C, spatial, eps, stream);
+}
+
+extern "C" int anima_conv_bias_rms_norm_channel_silu_bf16(const anima_bf16 *x, const anima_bf16 *bias,
+                                                          const anima_bf16 *gamma, anima_bf16 *out, int B, int C,
+                                                          int spatial, float eps, anima_stream_t stream) {
+    return channel_norm<true, true>(x, gamma, out, B, C, spatial, eps, stream, bias);
 }

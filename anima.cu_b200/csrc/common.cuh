@@ -75,6 +75,33 @@ __device__ __forceinline__ float bf16_round(float f) {
     return __bfloat162float(__float2bfloat16_rn(f));
 }
 
+// Position of unit i in a [rows, per_row] grid and the row's phase row % P (the table
+// row), advanced by the grid stride without divisions: the stride's quotient, remainder
+// and quotient mod P are taken once per thread.
+struct UnitCursor {
+    int64_t row, drow;
+    uint32_t rem, drem, ph, dph;
+    __device__ __forceinline__ UnitCursor(int64_t i, int64_t stride, uint32_t per_row, uint32_t P) {
+        row = i / per_row;
+        rem = (uint32_t)(i - row * per_row);
+        ph = (uint32_t)(row % P);
+        drow = stride / per_row;
+        drem = (uint32_t)(stride - drow * per_row);
+        dph = (uint32_t)(drow % P);
+    }
+    __device__ __forceinline__ void advance(uint32_t per_row, uint32_t P) {
+        row += drow;
+        rem += drem;
+        ph += dph;
+        if (rem >= per_row) {
+            rem -= per_row;
+            ++row;
+            ++ph;
+        }
+        if (ph >= P) ph -= P;  // ph + dph + 1 < 2P
+    }
+};
+
 // ------------------------------------------------- reference reduction replay
 //
 // The reference reduces a row of D2 = D/2 bf16 pairs with one CTA of T = D2 threads

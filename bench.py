@@ -672,6 +672,21 @@ def other_ops(ops, device, peak, reps=96):
                           (lambda xs, ys, gm, C, sp: lambda i: (
                               ops.call("rms_norm_channel", P(xs[i]), P(gm), P(ys[i]), 1, C, sp, eps, S()),
                               ops.call("silu", P(ys[i]), P(ys[i]), C * sp, S())))(xs, ys, gm, C, sp)))
+            # The conv epilogue (causal_conv3d.cu:187-195 and the chains after it, vae.cpp:185-194).
+            # The reference's bias kernel is file-local to causal_conv3d_forward, so there is
+            # no reference-arm timing of it.
+            cb = bf((C,), std=0.5)
+            cases.append((f"cfg4_conv_bias_add_{C}x{Hs}x{Hs}", 4 * C * sp + 2 * C, 1, sets,
+                          (lambda xs, ys, cb, C, sp: lambda i: ops.call(
+                              "conv_bias_add", P(xs[i]), P(cb), P(ys[i]), 1, C, sp, S()))(xs, ys, cb, C, sp)))
+            cases.append((f"cfg4_conv_bias_residual_add_{C}x{Hs}x{Hs}", 6 * C * sp + 2 * C, 1, sets,
+                          (lambda xs, ys, cb, C, sp: lambda i: ops.call(
+                              "conv_bias_residual_add", P(xs[i]), P(cb), P(ys[i]), P(ys[i]), 1, C, sp,
+                              S()))(xs, ys, cb, C, sp)))
+            cases.append((f"cfg4_conv_bias_rms_norm_channel_silu_{C}x{Hs}x{Hs}", 4 * C * sp + 4 * C, 1, sets,
+                          (lambda xs, ys, cb, gm, C, sp: lambda i: ops.call(
+                              "conv_bias_rms_norm_channel_silu", P(xs[i]), P(cb), P(gm), P(ys[i]), 1, C, sp, eps,
+                              S()))(xs, ys, cb, gm, C, sp)))
 
     # ---- cfg2: bias add after a Linear, final LayerNorm + modulate, QK RMSNorm + RoPE on q
     R, D, H, HD = 8192, 2048, 16, 128

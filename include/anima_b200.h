@@ -248,6 +248,27 @@ ANIMA_API int anima_channel_scale_shift_bf16(const anima_bf16 *x, const anima_bf
                                   const anima_bf16 *shift, anima_bf16 *out, int B, int C, int spatial,
                                   anima_stream_t stream);
 
+/* out[b,c,s] = x[b,c,s] + bias[c] on NCHW: the convolution's bias add, the file-local
+ * conv_bias_add_kernel launched by causal_conv3d_forward after every biased conv
+ * (causal_conv3d.cu:187-195, :247-254, :293-299). The caller runs the conv without its bias
+ * and calls this. out may alias x (the reference adds in place). */
+ANIMA_API int anima_conv_bias_add_bf16(const anima_bf16 *x, const anima_bf16 *bias, anima_bf16 *out,
+                            int B, int C, int spatial, anima_stream_t stream);
+
+/* out = (x + bias[c]) + residual in one pass, each sum rounded to bf16: the conv's bias launch
+ * followed by add_bf16(out, residual, out) at vae.cpp:190-194 (residual block) and :277-280
+ * (attention projection). out may alias x or residual. */
+ANIMA_API int anima_conv_bias_residual_add_bf16(const anima_bf16 *x, const anima_bf16 *bias,
+                                     const anima_bf16 *residual, anima_bf16 *out, int B, int C,
+                                     int spatial, anima_stream_t stream);
+
+/* silu(rms_norm_channel(x + bias[c])) in one pass: the conv's bias launch, then
+ * rms_norm_channel_bf16 and silu_bf16 (vae.cpp:185-189, a residual block's conv1 into
+ * norm2). The biased conv output is not stored. out may alias x. */
+ANIMA_API int anima_conv_bias_rms_norm_channel_silu_bf16(const anima_bf16 *x, const anima_bf16 *bias,
+                                              const anima_bf16 *gamma, anima_bf16 *out, int B, int C,
+                                              int spatial, float eps, anima_stream_t stream);
+
 /* adaLN-Zero modulation folded into adaLN LayerNorm. One launch replaces the chain
  *   add_bf16(mod, temb, mod, 3*D); adaln_layernorm_bf16(x, mod + D, mod, out, N, D, eps);
  *   cudaMemcpyAsync(gate, mod + 2*D, 2*D, DeviceToDevice)            (transformer.cpp:404-425)

@@ -513,6 +513,18 @@ void oracle_standard_rope_tables(int T, int HD, float theta, float *cos_out, flo
 
 /* ---------------------------------------------------- latent I/O and sampler steps */
 
+/* causal_conv3d.cu:187-195, then elementwise.cu:37-53 when residual is given */
+void oracle_conv_bias_add(const uint16_t *x, const uint16_t *bias, const uint16_t *residual,
+                          uint16_t *out, int B, int C, int spatial) {
+    for (int64_t b = 0; b < B; ++b)
+        for (int c = 0; c < C; ++c)
+            for (int64_t s = 0; s < spatial; ++s) {
+                int64_t e = (b * C + c) * spatial + s;
+                uint16_t h = F2B(B2F(x[e]) + B2F(bias[c]));
+                out[e] = residual ? F2B(B2F(h) + B2F(residual[e])) : h;
+            }
+}
+
 /* vae_kernels.cu:174-206 */
 void oracle_channel_scale_shift(const uint16_t *x, const uint16_t *scale, const uint16_t *shift,
                                 uint16_t *out, int B, int C, int spatial) {

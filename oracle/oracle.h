@@ -108,6 +108,12 @@ void oracle_embedding_lookup(const uint16_t *table, const int32_t *ids, uint16_t
 void oracle_rms_norm_channel(const uint16_t *x, const uint16_t *gamma, uint16_t *out, int B,
                              int C, int spatial, float eps);
 
+/* causal_conv3d.cu:187-195 -- out[b,c,s] = x + bias[c] (the conv's bias launch, per batch
+ * item there); with residual non-NULL, then out = out + residual[b,c,s] as add_bf16
+ * (elementwise.cu:37-53) does it at vae.cpp:194 and :280. */
+void oracle_conv_bias_add(const uint16_t *x, const uint16_t *bias, const uint16_t *residual,
+                          uint16_t *out, int B, int C, int spatial);
+
 /* vae_kernels.cu:174-206 -- out[b,c,s] = x*scale[c] + shift[c] (one fma). */
 void oracle_channel_scale_shift(const uint16_t *x, const uint16_t *scale, const uint16_t *shift,
                                 uint16_t *out, int B, int C, int spatial);

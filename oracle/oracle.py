@@ -29,6 +29,7 @@ _SIGS = {
     "oracle_mul": (P, P, P, I64),
     "oracle_bias_add": (P, P, P, I32, I32),
     "oracle_channel_scale_shift": (P, P, P, P, I32, I32, I32),
+    "oracle_conv_bias_add": (P, P, P, P, I32, I32, I32),
     "oracle_patchify_3d": (P, P) + (I32,) * 8,
     "oracle_unpatchify_3d": (P, P) + (I32,) * 8,
     "oracle_cfg_euler_step": (P, P, P, P, F32, F32, F32, I64),
@@ -265,6 +266,20 @@ def residual_gate_adaln_temb(hidden, sub_out, gate_in, mod, temb, N, D, eps=1e-6
     m = add(mod, temb)
     h, n = residual_gate_adaln(hidden, sub_out, gate_in, m[D:2 * D], m[:D], N, D, eps)
     return h, n, m[2 * D:]
+
+
+def conv_bias_add(x, bias, B, C, spatial, residual=None):
+    """causal_conv3d.cu:187-195 (+ add_bf16 of the residual, vae.cpp:194)."""
+    out = np.zeros_like(x)
+    res = None if residual is None else _p(np.ascontiguousarray(residual))
+    lib.oracle_conv_bias_add(_p(x), _p(bias), res, _p(out), B, C, spatial)
+    return out
+
+
+def conv_bias_rms_norm_channel_silu(x, bias, gamma, B, C, spatial, eps=1e-6):
+    """vae.cpp:185-189: the conv's bias launch, then rms_norm_channel_bf16 and silu_bf16."""
+    h = conv_bias_add(x, bias, B, C, spatial)
+    return rms_norm_channel_silu(h, gamma, B, C, spatial, eps)
 
 
 def channel_scale_shift(x, scale, shift, B, C, spatial):

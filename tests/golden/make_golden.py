@@ -259,6 +259,29 @@ def main():
     torch.cuda.synchronize()
     put("channel_scale_shift", x=cx, scale=csc, shift=csh, out=host(cout))
 
+    # ---- VAE conv epilogue; own seed. The conv's bias kernel (causal_conv3d.cu:187-195) is
+    # file-local to causal_conv3d_forward and computes bf16(x + bias[c]) per element, the same
+    # fp32 add and RNE rounding as add_bf16 (elementwise.cu:37-53), so the fixtures come from
+    # add_bf16 with the bias broadcast over each channel plane, then the reference's own chain
+    # (vae.cpp:185-194): rms_norm_channel_bf16 + silu_bf16, or add_bf16 of the residual.
+    rng4 = np.random.default_rng(20263)
+    B, C, sp = 2, 24, 40
+    x, b, res = O.randn_bf16(rng4, (B, C, sp)), O.randn_bf16(rng4, C, std=0.5), O.randn_bf16(rng4, (B, C, sp))
+    g = O.randn_bf16(rng4, C, mean=1.0, std=0.02)
+    n = B * C * sp
+    bexp = np.ascontiguousarray(np.broadcast_to(b.reshape(1, C, 1), (B, C, sp)))
+    hb = torch.zeros((B, C, sp), dtype=torch.int16, device="cuda")
+    R.add_bf16(dev(x).data_ptr(), dev(bexp).data_ptr(), hb.data_ptr(), n, s)
+    hr = torch.zeros((B, C, sp), dtype=torch.int16, device="cuda")
+    R.add_bf16(hb.data_ptr(), dev(res).data_ptr(), hr.data_ptr(), n, s)
+    hn = torch.zeros((B, C, sp), dtype=torch.int16, device="cuda")
+    R.rms_norm_channel_bf16(hb.data_ptr(), dev(g).data_ptr(), hn.data_ptr(), B, C, sp, 1e-6, s)
+    R.silu_bf16(hn.data_ptr(), hn.data_ptr(), n, s)
+    torch.cuda.synchronize()
+    put("conv_bias_add", x=x, bias=b, out=host(hb))
+    put("conv_bias_residual_add", x=x, bias=b, residual=res, out=host(hr))
+    put("conv_bias_rms_norm_channel_silu", x=x, bias=b, gamma=g, out=host(hn))
+
     if args.only:
         fx = {k: v for k, v in fx.items() if k in args.only}
     for name, arrays in fx.items():

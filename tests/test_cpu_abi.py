@@ -111,6 +111,13 @@ X, Y, Z = 0x10000, 0x20000, 0x30000  # never dereferenced: every call below fail
     (("anima_embedding_lookup_bf16", None, Y, Z, 4, 8, 10, None, None), -1),
     (("anima_rms_norm_channel_bf16", X, Y, Z, 1, 0, 16, 1e-6, None), -2),
     (("anima_rms_norm_channel_silu_bf16", X, None, Z, 1, 4, 16, 1e-6, None), -1),
+    (("anima_conv_bias_add_bf16", X, Y, Z, 1, 0, 16, None), -2),
+    (("anima_conv_bias_add_bf16", X, Y, X + 2, 1, 4, 16, None), -5),
+    (("anima_conv_bias_add_bf16", X, Z + 2, Z, 1, 4, 16, None), -5),
+    (("anima_conv_bias_residual_add_bf16", X, Y, None, Z, 1, 4, 16, None), -1),
+    (("anima_conv_bias_residual_add_bf16", X, Y, Z + 1, Z, 1, 4, 16, None), -3),
+    (("anima_conv_bias_rms_norm_channel_silu_bf16", X, Y + 1, Z, X, 1, 4, 16, 1e-6, None), -3),
+    (("anima_conv_bias_rms_norm_channel_silu_bf16", X, None, Z, X, 1, 4, 16, 1e-6, None), -1),
     (("anima_qk_norm_rope_bf16", X, None, Y, Z, 1, 4, 2, 128, 1e-6, None), -1),
     (("anima_swiglu_bf16", X, Y, Z + 1, 10, None), -3),
     (("anima_layer_norm_modulate_bf16", X, Y, Z, X + 4, 4, 128, 1e-6, None), -5),

@@ -166,6 +166,19 @@ def test_rms_norm_channel(name):
     close(O.rms_norm_channel(z["x"], z["gamma"], B, C, sp), z["out"], name)
 
 
+def test_conv_epilogue():
+    """causal_conv3d.cu:187-195 and the chains after it (vae.cpp:185-194), from the reference
+    kernels: the bias sums are exact; the fused norm is within the channel norm's 1 ulp."""
+    z = load("conv_bias_add")
+    B, C, sp = z["x"].shape
+    exact(O.conv_bias_add(z["x"], z["bias"], B, C, sp), z["out"], "conv_bias_add")
+    z = load("conv_bias_residual_add")
+    exact(O.conv_bias_add(z["x"], z["bias"], B, C, sp, residual=z["residual"]), z["out"], "conv_bias_residual_add")
+    z = load("conv_bias_rms_norm_channel_silu")
+    close(O.conv_bias_rms_norm_channel_silu(z["x"], z["bias"], z["gamma"], B, C, sp), z["out"],
+          "conv_bias_rms_norm_channel_silu")
+
+
 def test_sampler_steps():
     """transpose.cu:250-465 on the reference's outputs. In a sum of two products the oracle
     fuses the first (which product nvcc fuses is not visible on fixtures this small), so the

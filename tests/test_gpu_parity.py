@@ -595,6 +595,79 @@ def test_channel_scale_shift(anima, ref, rng, B, C, sp):
     assert_bit_exact(host(out), O.channel_scale_shift(x, sc, sh, B, C, sp).reshape(-1), "channel_scale_shift vs oracle")
 
 
+# ---------------------------------------------------------------- VAE conv epilogue
+# The vectorised path (spatial % 8 == 0) at several grid-stride depths, the scalar path
+# (spatial % 8 != 0), and for the fused norm each of its three kernels: cluster (few tiles),
+# tile (many tiles) and the per-pixel kernel.
+CONV_SHAPES = [(1, 512, 32, 32), (1, 96, 10, 10), (2, 100, 5, 8), (1, 256, 64, 64), (1, 64, 160, 160),
+               (1, 128, 256, 256), (2, 3, 3, 6)]
+
+
+def _ref_conv_bias(ref, dx, db, B, C, sp):
+    """The reference's bias launch (causal_conv3d.cu:187-195) stores bf16(x + bias[c]). That
+    kernel is file-local to causal_conv3d_forward, so the reference side runs the same
+    per-element sum through add_bf16 (elementwise.cu:37-53: fp32 add, RNE) with the bias
+    broadcast over each channel plane."""
+    bexp = db.view(1, C, 1).expand(B, C, sp).contiguous()
+    out = empty_bf16((B, C, sp))
+    ref.add_bf16(dx.data_ptr(), bexp.data_ptr(), out.data_ptr(), B * C * sp, stream_ptr())
+    return out
+
+
+@pytest.mark.parametrize("B,C,H,W", CONV_SHAPES)
+def test_conv_bias_add(anima, ref, rng, B, C, H, W):
+    sp = H * W
+    x, b = O.randn_bf16(rng, (B, C, sp)), O.randn_bf16(rng, C, std=0.5)
+    dx, db = dev(x), dev(b)
+    out = empty_bf16((B, C, sp))
+    anima.conv_bias_add(dx, db, out, B, C, sp)
+    r = _ref_conv_bias(ref, dx, db, B, C, sp)
+    xi = dev(x)
+    anima.conv_bias_add(xi, db, xi, B, C, sp)  # in place (causal_conv3d.cu:253)
+    torch.cuda.synchronize()
+    assert_bit_exact(host(out), host(r), "conv_bias_add vs reference")
+    assert_bit_exact(host(xi), host(r), "conv_bias_add in place")
+    if x.size <= ORACLE_MAX_ELEMS:
+        assert_bit_exact(host(out), O.conv_bias_add(x, b, B, C, sp), "conv_bias_add vs oracle")
+
+
+@pytest.mark.parametrize("B,C,H,W", CONV_SHAPES)
+def test_conv_bias_residual_add_matches_reference_chain(anima, ref, rng, B, C, H, W):
+    sp = H * W
+    x, b, res = O.randn_bf16(rng, (B, C, sp)), O.randn_bf16(rng, C, std=0.5), O.randn_bf16(rng, (B, C, sp))
+    dx, db, dres = dev(x), dev(b), dev(res)
+    out = empty_bf16((B, C, sp))
+    anima.conv_bias_residual_add(dx, db, dres, out, B, C, sp)
+    r = _ref_conv_bias(ref, dx, db, B, C, sp)  # vae.cpp:190 then :194
+    ref.add_bf16(r.data_ptr(), dres.data_ptr(), r.data_ptr(), B * C * sp, stream_ptr())
+    xi, ri = dev(x), dev(res)
+    anima.conv_bias_residual_add(xi, db, dres, xi, B, C, sp)  # out aliases x
+    anima.conv_bias_residual_add(dx, db, ri, ri, B, C, sp)  # out aliases the residual
+    torch.cuda.synchronize()
+    assert_bit_exact(host(out), host(r), "conv_bias_residual_add vs bias + add_bf16")
+    assert_bit_exact(host(xi), host(r), "conv_bias_residual_add, out = x")
+    assert_bit_exact(host(ri), host(r), "conv_bias_residual_add, out = residual")
+    if x.size <= ORACLE_MAX_ELEMS:
+        assert_bit_exact(host(out), O.conv_bias_add(x, b, B, C, sp, residual=res), "conv_bias_residual_add vs oracle")
+
+
+@pytest.mark.parametrize("B,C,H,W", CONV_SHAPES)
+def test_conv_bias_rms_norm_channel_silu_matches_reference_chain(anima, ref, rng, B, C, H, W):
+    sp = H * W
+    x, b, g = O.randn_bf16(rng, (B, C, sp)), O.randn_bf16(rng, C, std=0.5), _weight(rng, C)
+    dx, db, dg = dev(x), dev(b), dev(g)
+    out = empty_bf16((B, C, sp))
+    anima.conv_bias_rms_norm_channel_silu(dx, db, dg, out, B, C, sp, 1e-6)
+    r = _ref_conv_bias(ref, dx, db, B, C, sp)  # vae.cpp:185, then :188-189
+    ref.rms_norm_channel_bf16(r.data_ptr(), dg.data_ptr(), r.data_ptr(), B, C, sp, 1e-6, stream_ptr())
+    ref.silu_bf16(r.data_ptr(), r.data_ptr(), B * C * sp, stream_ptr())
+    xi = dev(x)
+    anima.conv_bias_rms_norm_channel_silu(xi, db, dg, xi, B, C, sp, 1e-6)  # in place
+    torch.cuda.synchronize()
+    assert_bit_exact(host(out), host(r), "conv_bias_rms_norm_channel_silu vs bias + rms_norm_channel + silu")
+    assert_bit_exact(host(xi), host(r), "conv_bias_rms_norm_channel_silu in place")
+
+
 PATCH_SHAPES = [(1, 16, 1, 128, 128, 1, 2, 2), (2, 4, 3, 8, 6, 1, 2, 2), (1, 3, 4, 6, 9, 2, 3, 3),
                 (1, 2, 1, 5, 7, 1, 2, 2), (2, 16, 2, 16, 16, 2, 2, 2)]
 
