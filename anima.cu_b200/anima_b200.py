@@ -41,6 +41,15 @@ SIGNATURES = {
     "anima_patchify_3d_bf16": (P, P) + (I32,) * 8 + (P,),
     "anima_unpatchify_3d_bf16": (P, P) + (I32,) * 8 + (P,),
     "anima_channel_scale_shift_bf16": (P, P, P, P, I32, I32, I32, P),
+    "anima_head_transpose_bf16": (P, P, I32, I32, I32, P),
+    "anima_head_untranspose_bf16": (P, P, I32, I32, I32, P),
+    "anima_head_transpose_batched_bf16": (P, P, I32, I32, I32, I32, P),
+    "anima_head_untranspose_batched_bf16": (P, P, I32, I32, I32, I32, P),
+    "anima_expand_kv_bf16": (P, P, I32, I32, I32, I32, I32, P),
+    "anima_causal_mask_bf16": (P, I32, I32, P),
+    "anima_softmax_bf16": (P, P, I32, I32, P),
+    "anima_causal_softmax_bf16": (P, P, I32, I32, P),
+    "anima_softmax_f32_to_bf16": (P, P, I32, I32, P),
     "anima_conv_bias_add_bf16": (P, P, P, I32, I32, I32, P),
     "anima_conv_bias_residual_add_bf16": (P, P, P, P, I32, I32, I32, P),
     "anima_conv_bias_rms_norm_channel_silu_bf16": (P, P, P, P, I32, I32, I32, F32, P),
@@ -256,6 +265,42 @@ def patchify_3d(src, dst, B, C, T, H, W, pT, pH, pW, stream=None):
 
 def unpatchify_3d(src, dst, B, C, T, H, W, pT, pH, pW, stream=None):
     call("anima_unpatchify_3d_bf16", _ptr(src), _ptr(dst), B, C, T, H, W, pT, pH, pW, _stream(stream))
+
+
+def head_transpose(src, dst, H, T, HD, stream=None):
+    call("anima_head_transpose_bf16", _ptr(src), _ptr(dst), H, T, HD, _stream(stream))
+
+
+def head_untranspose(src, dst, H, T, HD, stream=None):
+    call("anima_head_untranspose_bf16", _ptr(src), _ptr(dst), H, T, HD, _stream(stream))
+
+
+def head_transpose_batched(src, dst, B, H, S, HD, stream=None):
+    call("anima_head_transpose_batched_bf16", _ptr(src), _ptr(dst), B, H, S, HD, _stream(stream))
+
+
+def head_untranspose_batched(src, dst, B, H, S, HD, stream=None):
+    call("anima_head_untranspose_batched_bf16", _ptr(src), _ptr(dst), B, H, S, HD, _stream(stream))
+
+
+def expand_kv(kv, out, B, KV_H, Q_H, T, D, stream=None):
+    call("anima_expand_kv_bf16", _ptr(kv), _ptr(out), B, KV_H, Q_H, T, D, _stream(stream))
+
+
+def causal_mask(scores, num_heads, T, stream=None):
+    call("anima_causal_mask_bf16", _ptr(scores), num_heads, T, _stream(stream))
+
+
+def softmax(x, out, N, D, stream=None):
+    call("anima_softmax_bf16", _ptr(x), _ptr(out), N, D, _stream(stream))
+
+
+def causal_softmax(scores, out, num_heads, T, stream=None):
+    call("anima_causal_softmax_bf16", _ptr(scores), _ptr(out), num_heads, T, _stream(stream))
+
+
+def softmax_f32_to_bf16(x, out, N, D, stream=None):
+    call("anima_softmax_f32_to_bf16", _ptr(x), _ptr(out), N, D, _stream(stream))
 
 
 def conv_bias_add(x, bias, out, B, C, spatial, stream=None):

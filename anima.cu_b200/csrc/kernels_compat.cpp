@@ -136,6 +136,42 @@ void channel_scale_shift_bf16(const __nv_bfloat16 *x, const __nv_bfloat16 *scale
     record(anima_channel_scale_shift_bf16(in(x), in(scale), in(shift), io(out), B, C, spatial, stream));
 }
 
+void causal_mask_bf16(__nv_bfloat16 *scores, int num_heads, int T, cudaStream_t stream) {
+    record(anima_causal_mask_bf16(io(scores), num_heads, T, stream));
+}
+
+void softmax_bf16(const __nv_bfloat16 *x, __nv_bfloat16 *out, int N, int D, cudaStream_t stream) {
+    record(anima_softmax_bf16(in(x), io(out), N, D, stream));
+}
+
+void softmax_f32_to_bf16(const float *x, __nv_bfloat16 *out, int N, int D, cudaStream_t stream) {
+    record(anima_softmax_f32_to_bf16(x, io(out), N, D, stream));
+}
+
+void expand_kv_bf16(const __nv_bfloat16 *kv, __nv_bfloat16 *out, int B, int KV_H, int Q_H, int T, int D,
+                    cudaStream_t stream) {
+    record(anima_expand_kv_bf16(in(kv), io(out), B, KV_H, Q_H, T, D, stream));
+}
+
+void head_transpose_bf16(const __nv_bfloat16 *src, __nv_bfloat16 *dst, int H, int T, int HD, cudaStream_t stream) {
+    record(anima_head_transpose_bf16(in(src), io(dst), H, T, HD, stream));
+}
+
+void head_untranspose_bf16(const __nv_bfloat16 *src, __nv_bfloat16 *dst, int H, int T, int HD,
+                           cudaStream_t stream) {
+    record(anima_head_untranspose_bf16(in(src), io(dst), H, T, HD, stream));
+}
+
+void head_transpose_batched_bf16(const __nv_bfloat16 *src, __nv_bfloat16 *dst, int B, int H, int S, int HD,
+                                 cudaStream_t stream) {
+    record(anima_head_transpose_batched_bf16(in(src), io(dst), B, H, S, HD, stream));
+}
+
+void head_untranspose_batched_bf16(const __nv_bfloat16 *src, __nv_bfloat16 *dst, int B, int H, int S, int HD,
+                                   cudaStream_t stream) {
+    record(anima_head_untranspose_batched_bf16(in(src), io(dst), B, H, S, HD, stream));
+}
+
 void patchify_3d_bf16(const __nv_bfloat16 *src, __nv_bfloat16 *dst, int B, int C, int T, int H, int W, int pT,
                       int pH, int pW, cudaStream_t stream) {
     record(anima_patchify_3d_bf16(in(src), io(dst), B, C, T, H, W, pT, pH, pW, stream));

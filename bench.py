@@ -124,6 +124,12 @@ class AnimaOps:
     def layer_norm_modulate(self, x, sc, sh, o, N, D, eps, s):
         self._ck("ln_mod", self.L.anima_layer_norm_modulate_bf16(x, sc, sh, o, N, D, eps, s))
 
+    def causal_softmax(self, sc, o, H, T, s):
+        self._ck("causal_softmax", self.L.anima_causal_softmax_bf16(sc, o, H, T, s))
+
+    def softmax_f32_to_bf16(self, x, o, N, D, s):
+        self._ck("softmax_f32", self.L.anima_softmax_f32_to_bf16(x, o, N, D, s))
+
     def qk_norm_rope(self, x, w, c, sn, B, S, H, HD, eps, s):
         self._ck("qk_norm_rope", self.L.anima_qk_norm_rope_bf16(x, w, c, sn, B, S, H, HD, eps, s))
 
@@ -189,6 +195,13 @@ class RefOps:
     def rms_norm_channel_silu(self, x, gamma, o, B, C, sp, eps, s):  # vae.cpp:148,184
         self.R.rms_norm_channel_bf16(x, gamma, o, B, C, sp, eps, s)
         self.R.silu_bf16(o, o, B * C * sp, s)
+
+    def causal_softmax(self, sc, o, H, T, s):  # qwen3.cpp:205-208
+        self.R.causal_mask_bf16(sc, H, T, s)
+        self.R.softmax_bf16(sc, o, H * T, T, s)
+
+    def softmax_f32_to_bf16(self, x, o, N, D, s):
+        self.R.softmax_f32_to_bf16(x, o, N, D, s)
 
     def layer_norm_modulate(self, x, sc, sh, o, N, D, eps, s):  # transformer.cpp:563-564
         self.R.layer_norm_bf16(x, o, N, D, eps, s)
@@ -637,6 +650,32 @@ def other_ops(ops, device, peak, reps=96):
         cases.append(("cfg3_swiglu_512x3072_as_silu_mul", 6 * T * F, 2, 8,
                       lambda i: (ops.call("silu", P(gt[i]), P(st_[i]), T * F, S()),
                                  ops.call("mul", P(st_[i]), P(ut[i]), P(st_[i]), T * F, S()))))
+
+    # cfg3 attention glue (qwen3.cpp:164-226): head layout, GQA expansion, causal softmax
+    QH, KVH, HDq = 16, 8, 128
+    qb = [bf((T, QH * HDq)) for _ in range(8)]
+    qhd = [torch.empty((QH, T, HDq), dtype=torch.bfloat16, device=device) for _ in range(8)]
+    cases.append(("cfg3_head_transpose_512x16x128", 4 * T * QH * HDq, 1, 8,
+                  lambda i: ops.call("head_transpose", P(qb[i]), P(qhd[i]), QH, T, HDq, S())))
+    cases.append(("cfg3_head_untranspose_16x512x128", 4 * T * QH * HDq, 1, 8,
+                  lambda i: ops.call("head_untranspose", P(qhd[i]), P(qb[i]), QH, T, HDq, S())))
+    kvh = [bf((KVH, T, HDq)) for _ in range(8)]
+    cases.append(("cfg3_expand_kv_8to16x512x128", 2 * (KVH + QH) * T * HDq, 1, 8,
+                  lambda i: ops.call("expand_kv", P(kvh[i]), P(qhd[i]), 1, KVH, QH, T, HDq, S())))
+    scs = [bf((QH, T, T), std=3.0) for _ in range(8)]
+    cases.append(("cfg3_softmax_16x512x512", 4 * QH * T * T, 1, 8,
+                  lambda i: ops.call("softmax", P(scs[i]), P(scs[i]), QH * T, T, S())))
+    cases.append(("cfg3_causal_mask_softmax_16x512x512", 4 * QH * T * T, 1 if ops.kind == "anima" else 2, 8,
+                  lambda i: ops.causal_softmax(P(scs[i]), P(scs[i]), QH, T, S())))
+    if ops.kind == "anima":
+        cases.append(("cfg3_causal_mask_softmax_16x512x512_as_two_calls", 4 * QH * T * T, 2, 8,
+                      lambda i: (ops.call("causal_mask", P(scs[i]), QH, T, S()),
+                                 ops.call("softmax", P(scs[i]), P(scs[i]), QH * T, T, S()))))
+    # cfg4 VAE attention softmax (vae.cpp:262): fp32 scores [512, 512] -> bf16
+    vsc = [torch.randn((512, 512), generator=g, device=device) * 4.0 for _ in range(8)]
+    vsb = [torch.empty((512, 512), dtype=torch.bfloat16, device=device) for _ in range(8)]
+    cases.append(("cfg4_softmax_f32_to_bf16_512x512", 6 * 512 * 512, 1, 8,
+                  lambda i: ops.softmax_f32_to_bf16(P(vsc[i]), P(vsb[i]), 512, 512, S())))
 
     # ---- cfg2 denoising-loop I/O: CFG + Euler step, patchify / unpatchify, latent denorm
     Cl, Hl = 16, 128

@@ -248,6 +248,44 @@ ANIMA_API int anima_channel_scale_shift_bf16(const anima_bf16 *x, const anima_bf
                                   const anima_bf16 *shift, anima_bf16 *out, int B, int C, int spatial,
                                   anima_stream_t stream);
 
+/* Attention glue of the Qwen3 encoder and the LLM adapter (qwen3.cpp:164-226,
+ * llm_adapter.cpp:169-222). Head layout changes: [T, H*HD] <-> [H, T, HD]
+ * (head_transpose_bf16 / head_untranspose_bf16, transpose.cu:13-66) and
+ * [B*S, H*HD] <-> [B, H, S, HD] (the _batched forms, transpose.cu:68-123). src and dst may
+ * not overlap. */
+ANIMA_API int anima_head_transpose_bf16(const anima_bf16 *src, anima_bf16 *dst, int H, int T, int HD,
+                             anima_stream_t stream);
+ANIMA_API int anima_head_untranspose_bf16(const anima_bf16 *src, anima_bf16 *dst, int H, int T, int HD,
+                               anima_stream_t stream);
+ANIMA_API int anima_head_transpose_batched_bf16(const anima_bf16 *src, anima_bf16 *dst, int B, int H, int S,
+                                     int HD, anima_stream_t stream);
+ANIMA_API int anima_head_untranspose_batched_bf16(const anima_bf16 *src, anima_bf16 *dst, int B, int H, int S,
+                                       int HD, anima_stream_t stream);
+
+/* GQA expansion [B, KV_H, T, D] -> [B, Q_H, T, D], q head h reading kv head h / (Q_H / KV_H).
+ * Replaces expand_kv_bf16 (gemma_ops.cu:99-127). Q_H must be a multiple of KV_H (the
+ * reference reads past kv otherwise); rejected with ANIMA_ERR_BAD_SHAPE. */
+ANIMA_API int anima_expand_kv_bf16(const anima_bf16 *kv, anima_bf16 *out, int B, int KV_H, int Q_H, int T,
+                        int D, anima_stream_t stream);
+
+/* scores[h, i, j] = bf16(-1e9) for j > i, in place on [num_heads, T, T]. Replaces
+ * causal_mask_bf16 (softmax.cu:62-80). */
+ANIMA_API int anima_causal_mask_bf16(anima_bf16 *scores, int num_heads, int T, anima_stream_t stream);
+
+/* Row-wise softmax of x[N, D] into out (out may alias x). Replaces softmax_bf16
+ * (softmax.cu:8-60,115-122), bit for bit. */
+ANIMA_API int anima_softmax_bf16(const anima_bf16 *x, anima_bf16 *out, int N, int D, anima_stream_t stream);
+
+/* causal_mask_bf16 followed by softmax_bf16 on [num_heads, T, T] (qwen3.cpp:205-208) in one
+ * pass; wholly masked 16-byte chunks are not read. out may alias scores. No reference
+ * counterpart (opt-in). */
+ANIMA_API int anima_causal_softmax_bf16(const anima_bf16 *scores, anima_bf16 *out, int num_heads, int T,
+                             anima_stream_t stream);
+
+/* Row-wise softmax of fp32 x[N, D] into bf16 out. Replaces softmax_f32_to_bf16
+ * (softmax.cu:153-252; the VAE attention, vae.cpp:262), bit for bit. */
+ANIMA_API int anima_softmax_f32_to_bf16(const float *x, anima_bf16 *out, int N, int D, anima_stream_t stream);
+
 /* out[b,c,s] = x[b,c,s] + bias[c] on NCHW: the convolution's bias add, the file-local
  * conv_bias_add_kernel launched by causal_conv3d_forward after every biased conv
  * (causal_conv3d.cu:187-195, :247-254, :293-299). The caller runs the conv without its bias

@@ -85,6 +85,21 @@ void patchify_3d_bf16(const __nv_bfloat16 *src, __nv_bfloat16 *dst, int B, int C
                       int pH, int pW, cudaStream_t stream = 0);
 void unpatchify_3d_bf16(const __nv_bfloat16 *src, __nv_bfloat16 *dst, int B, int C, int T, int H, int W, int pT,
                         int pH, int pW, cudaStream_t stream = 0);
+// kernels.h:104-117
+void causal_mask_bf16(__nv_bfloat16 *scores, int num_heads, int T, cudaStream_t stream = 0);
+void softmax_bf16(const __nv_bfloat16 *x, __nv_bfloat16 *out, int N, int D, cudaStream_t stream = 0);
+void softmax_f32_to_bf16(const float *x, __nv_bfloat16 *out, int N, int D, cudaStream_t stream = 0);
+// kernels.h:148-150
+void expand_kv_bf16(const __nv_bfloat16 *kv, __nv_bfloat16 *out, int B, int KV_H, int Q_H, int T, int D,
+                    cudaStream_t stream = 0);
+// kernels.h:195-212
+void head_transpose_bf16(const __nv_bfloat16 *src, __nv_bfloat16 *dst, int H, int T, int HD, cudaStream_t stream = 0);
+void head_untranspose_bf16(const __nv_bfloat16 *src, __nv_bfloat16 *dst, int H, int T, int HD,
+                           cudaStream_t stream = 0);
+void head_transpose_batched_bf16(const __nv_bfloat16 *src, __nv_bfloat16 *dst, int B, int H, int S, int HD,
+                                 cudaStream_t stream = 0);
+void head_untranspose_batched_bf16(const __nv_bfloat16 *src, __nv_bfloat16 *dst, int B, int H, int S, int HD,
+                                   cudaStream_t stream = 0);
 // kernels.h:244-276
 void cfg_euler_step_bf16(const __nv_bfloat16 *sample, const __nv_bfloat16 *noise_pos,
                          const __nv_bfloat16 *noise_neg, __nv_bfloat16 *out, float cfg_scale, float sigma,

@@ -513,6 +513,144 @@ void oracle_standard_rope_tables(int T, int HD, float theta, float *cos_out, flo
 
 /* ---------------------------------------------------- latent I/O and sampler steps */
 
+/* ------------------------------------------------------------ attention glue */
+
+/* transpose.cu:17-31, 45-59, 71-89, 100-118 */
+void oracle_head_permute(const uint16_t *src, uint16_t *dst, int B, int H, int S, int HD, int to_heads) {
+    for (int64_t b = 0; b < B; ++b)
+        for (int64_t h = 0; h < H; ++h)
+            for (int64_t t = 0; t < S; ++t)
+                for (int64_t d = 0; d < HD; ++d) {
+                    int64_t heads = ((b * H + h) * S + t) * HD + d; /* [B, H, S, HD] */
+                    int64_t rows = ((b * S + t) * H + h) * HD + d;  /* [B*S, H*HD] */
+                    if (to_heads)
+                        dst[heads] = src[rows];
+                    else
+                        dst[rows] = src[heads];
+                }
+}
+
+/* gemma_ops.cu:101-117 */
+void oracle_expand_kv(const uint16_t *kv, uint16_t *out, int B, int KVH, int QH, int T, int D) {
+    int ratio = QH / KVH;
+    int64_t P = (int64_t)T * D;
+    for (int64_t b = 0; b < B; ++b)
+        for (int64_t q = 0; q < QH; ++q)
+            memcpy(out + (b * QH + q) * P, kv + (b * KVH + q / ratio) * P, (size_t)P * 2);
+}
+
+/* softmax.cu:64-73 */
+void oracle_causal_mask(uint16_t *scores, int H, int T) {
+    uint16_t m = F2B(-1e9f);
+    for (int64_t h = 0; h < H; ++h)
+        for (int64_t i = 0; i < T; ++i)
+            for (int64_t j = i + 1; j < T; ++j) scores[(h * T + i) * T + j] = m;
+}
+
+/* cuda_utils.cuh:46-50: a warp's __shfl_down_sync sum tree; the value lane 0 ends with. */
+static float shfl_down_sum32(const float *in) {
+    float v[32];
+    memcpy(v, in, sizeof v);
+    for (int o = 16; o > 0; o >>= 1)
+        for (int i = 0; i < o; ++i) v[i] = v[i] + v[i + o];
+    return v[0];
+}
+
+static int softmax_threads(int D) { /* softmax.cu:118-119, :248-249 */
+    int t = D <= 1024 ? (D + 31) / 32 * 32 : 1024;
+    return t < 32 ? 32 : t;
+}
+
+/* softmax.cu:8-60 */
+void oracle_softmax(const uint16_t *x, uint16_t *out, int N, int D) {
+    int nt = softmax_threads(D), nw = nt / 32;
+    float *part = (float *)calloc((size_t)nt, sizeof(float));
+    for (int64_t r = 0; r < N; ++r) {
+        const uint16_t *xr = x + r * D;
+        float mx = -1e30f;
+        for (int i = 0; i < D; ++i) mx = fmaxf(mx, B2F(xr[i]));
+        for (int t = 0; t < nt; ++t) {
+            float acc = 0.0f;
+            for (int i = t; i < D; i += nt) acc += expf(B2F(xr[i]) - mx);
+            part[t] = acc;
+        }
+        float warps[32] = {0};
+        for (int w = 0; w < nw; ++w) warps[w] = shfl_down_sum32(part + 32 * w);
+        float inv = 1.0f / shfl_down_sum32(warps);
+        for (int i = 0; i < D; ++i) out[r * D + i] = F2B(expf(B2F(xr[i]) - mx) * inv);
+    }
+    free(part);
+}
+
+/* softmax.cu:160-166 and :185-193 (nvcc contracts a*b + c into one fma there) */
+static void online_add(float xi, float *m, float *s) {
+    if (xi > *m) {
+        *s = fmaf(*s, expf(*m - xi), 1.0f);
+        *m = xi;
+    } else {
+        *s += expf(xi - *m);
+    }
+}
+static void online_merge(float om, float os, float *m, float *s) {
+    if (om > *m) {
+        *s = fmaf(*s, expf(*m - om), os);
+        *m = om;
+    } else {
+        *s = fmaf(os, expf(om - *m), *s);
+    }
+}
+
+/* A warp's __shfl_down_sync merge tree over (m, s); lanes whose source is out of range merge
+ * with themselves, as the shuffle returns their own value. Result: lane 0. */
+static void shfl_down_merge32(float *m, float *s) {
+    for (int o = 16; o > 0; o >>= 1) {
+        float nm[32], ns[32];
+        for (int i = 0; i < 32; ++i) {
+            int src = i + o < 32 ? i + o : i;
+            nm[i] = m[i];
+            ns[i] = s[i];
+            online_merge(m[src], s[src], &nm[i], &ns[i]);
+        }
+        memcpy(m, nm, sizeof nm);
+        memcpy(s, ns, sizeof ns);
+    }
+}
+
+/* softmax.cu:153-245 */
+void oracle_softmax_f32_to_bf16(const float *x, uint16_t *out, int N, int D) {
+    int nt = softmax_threads(D), nw = nt / 32, D4 = D / 4;
+    float *tm = (float *)malloc((size_t)nt * sizeof(float)), *ts = (float *)malloc((size_t)nt * sizeof(float));
+    for (int64_t r = 0; r < N; ++r) {
+        const float *xr = x + r * D;
+        for (int t = 0; t < nt; ++t) {
+            float m = -1e30f, s = 0.0f;
+            for (int i = t; i < D4; i += nt)
+                for (int k = 0; k < 4; ++k) online_add(xr[4 * i + k], &m, &s);
+            for (int i = D4 * 4 + t; i < D; i += nt) online_add(xr[i], &m, &s);
+            tm[t] = m;
+            ts[t] = s;
+        }
+        float wm[32], ws[32];
+        for (int w = 0; w < 32; ++w) {
+            wm[w] = -1e30f;
+            ws[w] = 0.0f;
+        }
+        for (int w = 0; w < nw; ++w) {
+            float m[32], s[32];
+            memcpy(m, tm + 32 * w, sizeof m);
+            memcpy(s, ts + 32 * w, sizeof s);
+            shfl_down_merge32(m, s);
+            wm[w] = m[0];
+            ws[w] = s[0];
+        }
+        shfl_down_merge32(wm, ws);
+        float mx = wm[0], inv = 1.0f / ws[0];
+        for (int i = 0; i < D; ++i) out[r * D + i] = F2B(expf(xr[i] - mx) * inv);
+    }
+    free(tm);
+    free(ts);
+}
+
 /* causal_conv3d.cu:187-195, then elementwise.cu:37-53 when residual is given */
 void oracle_conv_bias_add(const uint16_t *x, const uint16_t *bias, const uint16_t *residual,
                           uint16_t *out, int B, int C, int spatial) {

@@ -108,6 +108,23 @@ void oracle_embedding_lookup(const uint16_t *table, const int32_t *ids, uint16_t
 void oracle_rms_norm_channel(const uint16_t *x, const uint16_t *gamma, uint16_t *out, int B,
                              int C, int spatial, float eps);
 
+/* transpose.cu:13-123 -- [B, S, H, HD] -> [B, H, S, HD] (to_heads = 1, head_transpose) or
+ * back (to_heads = 0, head_untranspose); B = 1 gives the unbatched launchers. */
+void oracle_head_permute(const uint16_t *src, uint16_t *dst, int B, int H, int S, int HD, int to_heads);
+
+/* gemma_ops.cu:99-127 -- out[b, q, :] = kv[b, q / (QH / KVH), :] over [T*D] planes. */
+void oracle_expand_kv(const uint16_t *kv, uint16_t *out, int B, int KVH, int QH, int T, int D);
+
+/* softmax.cu:62-80 -- scores[h, i, j] = bf16(-1e9) for j > i, in place. */
+void oracle_causal_mask(uint16_t *scores, int H, int T);
+
+/* softmax.cu:8-60,115-122 -- row softmax in the reference CTA's summation order. */
+void oracle_softmax(const uint16_t *x, uint16_t *out, int N, int D);
+
+/* softmax.cu:153-252 -- fp32 rows, per-thread running (max, sum) merged along the
+ * reference's shuffle trees; bf16 out. */
+void oracle_softmax_f32_to_bf16(const float *x, uint16_t *out, int N, int D);
+
 /* causal_conv3d.cu:187-195 -- out[b,c,s] = x + bias[c] (the conv's bias launch, per batch
  * item there); with residual non-NULL, then out = out + residual[b,c,s] as add_bf16
  * (elementwise.cu:37-53) does it at vae.cpp:194 and :280. */

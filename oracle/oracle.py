@@ -30,6 +30,11 @@ _SIGS = {
     "oracle_bias_add": (P, P, P, I32, I32),
     "oracle_channel_scale_shift": (P, P, P, P, I32, I32, I32),
     "oracle_conv_bias_add": (P, P, P, P, I32, I32, I32),
+    "oracle_head_permute": (P, P, I32, I32, I32, I32, I32),
+    "oracle_expand_kv": (P, P, I32, I32, I32, I32, I32),
+    "oracle_causal_mask": (P, I32, I32),
+    "oracle_softmax": (P, P, I32, I32),
+    "oracle_softmax_f32_to_bf16": (P, P, I32, I32),
     "oracle_patchify_3d": (P, P) + (I32,) * 8,
     "oracle_unpatchify_3d": (P, P) + (I32,) * 8,
     "oracle_cfg_euler_step": (P, P, P, P, F32, F32, F32, I64),
@@ -266,6 +271,44 @@ def residual_gate_adaln_temb(hidden, sub_out, gate_in, mod, temb, N, D, eps=1e-6
     m = add(mod, temb)
     h, n = residual_gate_adaln(hidden, sub_out, gate_in, m[D:2 * D], m[:D], N, D, eps)
     return h, n, m[2 * D:]
+
+
+def head_transpose(src, B, H, S, HD):
+    """transpose.cu:13-123: [B*S, H*HD] -> [B, H, S, HD]."""
+    out = np.zeros((B, H, S, HD), np.uint16)
+    lib.oracle_head_permute(_p(np.ascontiguousarray(src)), _p(out), B, H, S, HD, 1)
+    return out
+
+
+def head_untranspose(src, B, H, S, HD):
+    """transpose.cu:41-123: [B, H, S, HD] -> [B*S, H*HD]."""
+    out = np.zeros((B * S, H * HD), np.uint16)
+    lib.oracle_head_permute(_p(np.ascontiguousarray(src)), _p(out), B, H, S, HD, 0)
+    return out
+
+
+def expand_kv(kv, B, KVH, QH, T, D):
+    out = np.zeros((B, QH, T, D), np.uint16)
+    lib.oracle_expand_kv(_p(np.ascontiguousarray(kv)), _p(out), B, KVH, QH, T, D)
+    return out
+
+
+def causal_mask(scores, H, T):
+    out = np.array(scores, np.uint16).reshape(H, T, T)
+    lib.oracle_causal_mask(_p(out), H, T)
+    return out
+
+
+def softmax(x, N, D):
+    out = np.zeros((N, D), np.uint16)
+    lib.oracle_softmax(_p(np.ascontiguousarray(x)), _p(out), N, D)
+    return out
+
+
+def softmax_f32_to_bf16(x, N, D):
+    out = np.zeros((N, D), np.uint16)
+    lib.oracle_softmax_f32_to_bf16(_p(np.ascontiguousarray(x, np.float32)), _p(out), N, D)
+    return out
 
 
 def conv_bias_add(x, bias, B, C, spatial, residual=None):

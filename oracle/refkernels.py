@@ -35,6 +35,10 @@ LAUNCHERS = {
     "silu_bias_bf16": ("_Z14silu_bias_bf16PK13__nv_bfloat16S1_PS_liP11CUstream_st", (P, P, P, I64, I32, P)),  # :40-42
     "rope_cosmos_strided_bf16": ("_Z24rope_cosmos_strided_bf16P13__nv_bfloat16PKS_S2_iiiiP11CUstream_st",
                                  (P, P, P, I32, I32, I32, I32, P)),  # :51-53
+    "causal_mask_bf16": ("_Z16causal_mask_bf16P13__nv_bfloat16iiP11CUstream_st", (P, I32, I32, P)),  # :104-106
+    "softmax_bf16": ("_Z12softmax_bf16PK13__nv_bfloat16PS_iiP11CUstream_st", (P, P, I32, I32, P)),  # :109-111
+    "softmax_f32_to_bf16": ("_Z19softmax_f32_to_bf16PKfP13__nv_bfloat16iiP11CUstream_st",
+                            (P, P, I32, I32, P)),  # :115-117
     "adaln_rms_norm_bf16": ("_Z19adaln_rms_norm_bf16PK13__nv_bfloat16S1_S1_PS_iifP11CUstream_st",
                             (P, P, P, P, I32, I32, F32, P)),  # :60-63
     "add_bf16": ("_Z8add_bf16PK13__nv_bfloat16S1_PS_lP11CUstream_st", (P, P, P, I64, P)),  # :69-71
@@ -49,12 +53,22 @@ LAUNCHERS = {
                               (P, P, P, I32, I32, P)),  # :142-144
     "rope_standard_bf16": ("_Z18rope_standard_bf16P13__nv_bfloat16PKfS2_iiiP11CUstream_st",
                            (P, P, P, I32, I32, I32, P)),  # :145-147
+    "expand_kv_bf16": ("_Z14expand_kv_bf16PK13__nv_bfloat16PS_iiiiiP11CUstream_st",
+                       (P, P, I32, I32, I32, I32, I32, P)),  # :148-150
     "gemma_rms_norm_bf16": ("_Z19gemma_rms_norm_bf16PK13__nv_bfloat16S1_PS_iifP11CUstream_st",
                             (P, P, P, I32, I32, F32, P)),  # :151-153
     "rms_norm_channel_bf16": ("_Z21rms_norm_channel_bf16PK13__nv_bfloat16S1_PS_iiifP11CUstream_st",
                               (P, P, P, I32, I32, I32, F32, P)),  # :177-180
     "channel_scale_shift_bf16": ("_Z24channel_scale_shift_bf16PK13__nv_bfloat16S1_S1_PS_iiiP11CUstream_st",
                                  (P, P, P, P, I32, I32, I32, P)),  # :189-192
+    "head_transpose_bf16": ("_Z19head_transpose_bf16PK13__nv_bfloat16PS_iiiP11CUstream_st",
+                            (P, P, I32, I32, I32, P)),  # :195-197
+    "head_untranspose_bf16": ("_Z21head_untranspose_bf16PK13__nv_bfloat16PS_iiiP11CUstream_st",
+                              (P, P, I32, I32, I32, P)),  # :200-202
+    "head_transpose_batched_bf16": ("_Z27head_transpose_batched_bf16PK13__nv_bfloat16PS_iiiiP11CUstream_st",
+                                    (P, P, I32, I32, I32, I32, P)),  # :205-207
+    "head_untranspose_batched_bf16": ("_Z29head_untranspose_batched_bf16PK13__nv_bfloat16PS_iiiiP11CUstream_st",
+                                      (P, P, I32, I32, I32, I32, P)),  # :210-212
     "patchify_3d_bf16": ("_Z16patchify_3d_bf16PK13__nv_bfloat16PS_iiiiiiiiP11CUstream_st",
                          (P, P) + (I32,) * 8 + (P,)),  # :215-218
     "unpatchify_3d_bf16": ("_Z18unpatchify_3d_bf16PK13__nv_bfloat16PS_iiiiiiiiP11CUstream_st",

@@ -282,6 +282,33 @@ def main():
     put("conv_bias_residual_add", x=x, bias=b, residual=res, out=host(hr))
     put("conv_bias_rms_norm_channel_silu", x=x, bias=b, gamma=g, out=host(hn))
 
+    # ---- attention glue (transpose.cu, gemma_ops.cu, softmax.cu); own seed
+    rng5 = np.random.default_rng(20264)
+    H, T, HD = 4, 6, 16
+    x = O.randn_bf16(rng5, (T, H * HD))
+    th = torch.zeros((H, T, HD), dtype=torch.int16, device="cuda")
+    R.head_transpose_bf16(dev(x).data_ptr(), th.data_ptr(), H, T, HD, s)
+    kv = O.randn_bf16(rng5, (1, 2, T, HD))
+    ek = torch.zeros((1, 6, T, HD), dtype=torch.int16, device="cuda")
+    R.expand_kv_bf16(dev(kv).data_ptr(), ek.data_ptr(), 1, 2, 6, T, HD, s)
+    sc = O.randn_bf16(rng5, (3, 40, 40), std=3.0)
+    msk = dev(sc)
+    R.causal_mask_bf16(msk.data_ptr(), 3, 40, s)
+    sm = torch.zeros((3 * 40, 40), dtype=torch.int16, device="cuda")
+    R.softmax_bf16(msk.data_ptr(), sm.data_ptr(), 3 * 40, 40, s)
+    sx = O.randn_bf16(rng5, (4, 1500), std=3.0)
+    sl = torch.zeros((4, 1500), dtype=torch.int16, device="cuda")
+    R.softmax_bf16(dev(sx).data_ptr(), sl.data_ptr(), 4, 1500, s)
+    fx32 = (rng5.standard_normal((8, 96)) * 4.0).astype(np.float32)
+    sf = torch.zeros((8, 96), dtype=torch.int16, device="cuda")
+    R.softmax_f32_to_bf16(torch.from_numpy(fx32).cuda().data_ptr(), sf.data_ptr(), 8, 96, s)
+    torch.cuda.synchronize()
+    put("head_transpose", x=x, out=host(th), shape=np.array([H, T, HD], np.int32))
+    put("expand_kv", x=kv, out=host(ek), shape=np.array([1, 2, 6, T, HD], np.int32))
+    put("causal_mask_softmax", x=sc, masked=host(msk), out=host(sm))
+    put("softmax_1500", x=sx, out=host(sl))
+    put("softmax_f32_to_bf16", x=fx32, out=host(sf))
+
     if args.only:
         fx = {k: v for k, v in fx.items() if k in args.only}
     for name, arrays in fx.items():

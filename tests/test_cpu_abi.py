@@ -111,6 +111,17 @@ X, Y, Z = 0x10000, 0x20000, 0x30000  # never dereferenced: every call below fail
     (("anima_embedding_lookup_bf16", None, Y, Z, 4, 8, 10, None, None), -1),
     (("anima_rms_norm_channel_bf16", X, Y, Z, 1, 0, 16, 1e-6, None), -2),
     (("anima_rms_norm_channel_silu_bf16", X, None, Z, 1, 4, 16, 1e-6, None), -1),
+    (("anima_head_transpose_bf16", X, X + 64, 4, 8, 16, None), -5),
+    (("anima_head_untranspose_batched_bf16", X, None, 1, 4, 8, 16, None), -1),
+    (("anima_expand_kv_bf16", X, Y, 1, 3, 8, 4, 16, None), -2),
+    (("anima_expand_kv_bf16", X, Y + 1, 1, 2, 8, 4, 16, None), -3),
+    (("anima_causal_mask_bf16", None, 2, 8, None), -1),
+    (("anima_causal_mask_bf16", X, -1, 8, None), -2),
+    (("anima_softmax_bf16", X + 1, Y, 4, 16, None), -3),
+    (("anima_softmax_bf16", X, X + 2, 4, 16, None), -5),
+    (("anima_causal_softmax_bf16", X, None, 2, 8, None), -1),
+    (("anima_softmax_f32_to_bf16", X + 2, Y, 4, 16, None), -3),
+    (("anima_softmax_f32_to_bf16", X, X + 8, 4, 16, None), -5),
     (("anima_conv_bias_add_bf16", X, Y, Z, 1, 0, 16, None), -2),
     (("anima_conv_bias_add_bf16", X, Y, X + 2, 1, 4, 16, None), -5),
     (("anima_conv_bias_add_bf16", X, Z + 2, Z, 1, 4, 16, None), -5),

@@ -179,6 +179,26 @@ def test_conv_epilogue():
           "conv_bias_rms_norm_channel_silu")
 
 
+def test_attention_glue():
+    """transpose.cu, gemma_ops.cu:99-127 and softmax.cu on the reference's outputs: the
+    permutations and the mask exactly, the softmaxes within one ulp (libm expf)."""
+    z = load("head_transpose")
+    H, T, HD = (int(v) for v in z["shape"])
+    exact(O.head_transpose(z["x"], 1, H, T, HD), z["out"], "head_transpose")
+    exact(O.head_untranspose(z["out"], 1, H, T, HD), z["x"], "head_untranspose")
+    z = load("expand_kv")
+    B, KVH, QH, T, D = (int(v) for v in z["shape"])
+    exact(O.expand_kv(z["x"], B, KVH, QH, T, D), z["out"], "expand_kv")
+    z = load("causal_mask_softmax")
+    H, T, _ = z["x"].shape
+    exact(O.causal_mask(z["x"], H, T), z["masked"], "causal_mask")
+    close(O.softmax(z["masked"], H * T, T), z["out"], "softmax after causal_mask")
+    z = load("softmax_1500")
+    close(O.softmax(z["x"], *z["x"].shape), z["out"], "softmax D=1500")
+    z = load("softmax_f32_to_bf16")
+    close(O.softmax_f32_to_bf16(z["x"], *z["x"].shape), z["out"], "softmax_f32_to_bf16")
+
+
 def test_sampler_steps():
     """transpose.cu:250-465 on the reference's outputs. In a sum of two products the oracle
     fuses the first (which product nvcc fuses is not visible on fixtures this small), so the
