@@ -10,9 +10,19 @@
 //
 // The per-element arithmetic is the reference's own expression for each op (file:line
 // at each Op), so results are bit-identical to the reference kernels.
+//
+// GELU and SiLU on large tensors: the output is a function of the input's 16 bits, so each
+// has a 65536-entry table of bf16(F(x)) -- the reference formula at every bf16 value, filled
+// on the device by the exact code path -- and the kernel becomes a table lookup from shared
+// memory: one CTA of 1024 threads per SM copies the 128 KB table in (before waiting on the
+// previous kernel) and streams the tensor. This replaced per-element ex2/rcp approximations
+// with an exact-formula fallback: no MUFU work, no divergent fallback lanes, 4 instructions
+// per element. Smaller or unaligned tensors, and calls made while a stream is being captured
+// before the table exists, use the table-free kernel (fast_act_kernel), with the same results.
 #include "common.cuh"
 #include "activation.cuh"
 
+#include <atomic>
 #include <type_traits>
 
 namespace anima {
@@ -245,6 +255,128 @@ int launch_fast_act(const EwArgs &a, cudaStream_t stream) {
     return launch_status();
 }
 
+// ------------------------------------------------------------ activation tables
+// bf16(F(x)) for every bf16 bit pattern x: [0] GELU-tanh, [1] SiLU. Static device memory of
+// the module (one copy per device); filled by fill_act_table on the first table-path call.
+__device__ __align__(256) uint16_t g_act_table[2][65536];
+constexpr int kTabEntries = 65536;
+constexpr int kTabBytes = kTabEntries * 2;
+constexpr int kTabBlock = 1024;   // one CTA per SM: the table takes 128 KB of shared memory
+constexpr int64_t kTabMinElems = 1 << 20;
+
+template <class F>
+__global__ void fill_act_table(uint16_t *table) {
+    const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < kTabEntries) table[i] = (uint16_t)exact_bits<F>(i);
+}
+
+__device__ __forceinline__ void cp_async16(void *smem, const void *gmem) {
+    const unsigned s = (unsigned)__cvta_generic_to_shared(smem);
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(s), "l"(gmem) : "memory");
+}
+
+template <int U>
+__device__ __forceinline__ void lookup_group(const Vec8 (&in)[U][1], const EwArgs &a, const uint16_t *tab,
+                                             int64_t base, int64_t stride, int64_t nch) {
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+        const int64_t i = base + u * stride;
+        if (i >= nch) break;
+        Vec8 o;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const uint32_t w = in[u][0].w[j];
+            o.w[j] = (uint32_t)tab[w & 0xffffu] | ((uint32_t)tab[w >> 16] << 16);
+        }
+        st_vec(a.out + i * 8, o);
+    }
+}
+
+__global__ void __launch_bounds__(kTabBlock, 1) table_act_kernel(EwArgs a, const uint16_t *__restrict__ table) {
+    extern __shared__ __align__(16) uint16_t tab[];
+    // The table does not depend on the previous kernel: copy it in before waiting on it.
+    for (int q = threadIdx.x; q < kTabEntries / 8; q += kTabBlock) cp_async16(tab + q * 8, table + q * 8);
+    asm volatile("cp.async.commit_group;" ::: "memory");
+    pdl_wait();
+    constexpr int U = 2;  // swept 1-4: 2 is best (43.5 us on [8192, 8192])
+    const int64_t tid = (int64_t)blockIdx.x * kTabBlock + threadIdx.x, stride = (int64_t)gridDim.x * kTabBlock;
+    const int64_t nch = a.n >> 3, step = stride * U;
+    Vec8 x0[U][1], x1[U][1];
+    load_group<U, 1>(x0, a, tid, stride, nch);
+    asm volatile("cp.async.wait_group 0;" ::: "memory");
+    __syncthreads();
+    for (int64_t base = tid; base < nch;) {
+        load_group<U, 1>(x1, a, base + step, stride, nch);
+        lookup_group<U>(x0, a, tab, base, stride, nch);
+        base += step;
+        if (base >= nch) break;
+        load_group<U, 1>(x0, a, base + step, stride, nch);
+        lookup_group<U>(x1, a, tab, base, stride, nch);
+        base += step;
+    }
+    pdl_launch();
+    for (int64_t e = (nch << 3) + tid; e < a.n; e += stride)
+        reinterpret_cast<uint16_t *>(a.out)[e] = tab[reinterpret_cast<const uint16_t *>(a.s0)[e]];
+}
+
+constexpr int kTabDevices = 64;
+std::atomic<uintptr_t> g_table_addr[kTabDevices];  // device address of g_act_table (set before a ready bit)
+std::atomic<unsigned> g_table_ready[kTabDevices];  // bit t set = table t filled on that device
+
+// The device's table `t`, filled if it is not yet and the stream is not being captured
+// (filling launches on `stream` and waits for it, once per device). Null: use the
+// table-free kernel. *err receives a CUDA error from the fill. While a capture is under way
+// nothing but the capture query runs here, so a capture is never disturbed.
+template <class F>
+const uint16_t *act_table(int t, cudaStream_t stream, int *err) {
+    *err = ANIMA_OK;
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev >= kTabDevices) {
+        cudaGetLastError();
+        return nullptr;
+    }
+    if (g_table_ready[dev].load(std::memory_order_acquire) & (1u << t))
+        return reinterpret_cast<const uint16_t *>(g_table_addr[dev].load(std::memory_order_acquire)) + t * kTabEntries;
+    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+    if (cudaStreamIsCapturing(stream, &cs) != cudaSuccess || cs != cudaStreamCaptureStatusNone) {
+        cudaGetLastError();
+        return nullptr;
+    }
+    void *p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_act_table) != cudaSuccess) {
+        cudaGetLastError();
+        return nullptr;
+    }
+    g_table_addr[dev].store((uintptr_t)p, std::memory_order_release);
+    uint16_t *table = static_cast<uint16_t *>(p) + t * kTabEntries;
+    fill_act_table<F><<<kTabEntries / 256, 256, 0, stream>>>(table);
+    cudaError_t e = cudaGetLastError();
+    if (e == cudaSuccess) e = cudaStreamSynchronize(stream);
+    if (e != cudaSuccess) {
+        *err = (int)e;
+        return nullptr;
+    }
+    // Concurrent first calls fill the same bits; a reader only starts after its own caller
+    // saw this bit, i.e. after a completed fill.
+    g_table_ready[dev].fetch_or(1u << t, std::memory_order_acq_rel);
+    return table;
+}
+
+template <class F>
+int launch_act(const EwArgs &a, cudaStream_t stream, int t) {
+    if (a.vec && a.n >= kTabMinElems) {
+        int err = ANIMA_OK;
+        const uint16_t *table = act_table<F>(t, stream, &err);
+        if (err) return err;
+        if (table) {
+            if (int e = allow_dynamic_smem((const void *)table_act_kernel, kTabBytes, 8)) return e;
+            launch(table_act_kernel, (unsigned)sm_count(), kTabBlock, kTabBytes, stream, a, table);
+            return launch_status();
+        }
+    }
+    return launch_fast_act<F, 1>(a, stream);
+}
+
 bool bf16_ok(const void *p) { return aligned_to(p, 2); }
 
 // Validates and launches a flat op over n elements (n = 2*floor(N/2), as the reference's
@@ -266,8 +398,8 @@ int flat_op(const anima_bf16 *s0, const anima_bf16 *s1, const anima_bf16 *bias, 
     EwArgs a{s0, NS > 1 ? s1 : nullptr, NB > 0 ? bias : nullptr, nullptr, out, n, NB > 0 ? D : 0, false};
     a.vec = aligned16(s0) && aligned16(out) && (NS < 2 || aligned16(s1)) &&
             (NB == 0 || (aligned16(bias) && D % 8 == 0));
-    if constexpr (std::is_same<Op, OpGelu>::value) return launch_fast_act<GeluF, 1>(a, stream);
-    if constexpr (std::is_same<Op, OpSilu>::value) return launch_fast_act<SiluF, 1>(a, stream);
+    if constexpr (std::is_same<Op, OpGelu>::value) return launch_act<GeluF>(a, stream, 0);
+    if constexpr (std::is_same<Op, OpSilu>::value) return launch_act<SiluF>(a, stream, 1);
     if constexpr (std::is_same<Op, OpSwiGLU>::value) return launch_fast_act<SiluF, 2>(a, stream);
     return launch_ew<Op>(a, stream);
 }

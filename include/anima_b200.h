@@ -91,7 +91,11 @@ ANIMA_API int anima_gemma_rms_norm_bf16(const anima_bf16 *x, const anima_bf16 *w
 /* -------------------------------------------------------------- elementwise */
 
 /* tanh-GELU. The reference processes floor(N/2) element pairs and leaves an odd last
- * element untouched; so does this. Replaces gelu_tanh_bf16, kernels.h:33 (gelu.cu:66-71). */
+ * element untouched; so does this. Replaces gelu_tanh_bf16, kernels.h:33 (gelu.cu:66-71).
+ * On 16-byte-aligned tensors of 2^20 elements or more it reads a 65536-entry table of the
+ * reference's outputs: the first such call on a device fills it and waits for `stream` once
+ * (a call captured into a CUDA graph before then uses the table-free kernel; same bits).
+ * anima_silu_bf16 likewise. */
 ANIMA_API int anima_gelu_tanh_bf16(const anima_bf16 *x, anima_bf16 *out, int64_t N,
                          anima_stream_t stream);
 

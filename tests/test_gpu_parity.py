@@ -269,12 +269,17 @@ def test_unary_extreme_inputs(anima, ref, op):
 
 
 @pytest.mark.parametrize("op", ["gelu_tanh", "silu"])
-def test_unary_exhaustive(anima, ref, op):
+@pytest.mark.parametrize("reps", [1, 8, 9])
+def test_unary_exhaustive(anima, ref, op, reps):
     """GELU and SiLU map one bf16 input to one bf16 output, so all 65536 inputs (both
-    zeros, subnormals, Inf, every NaN payload) settle parity completely -- for the
-    table-driven fast path and its inline-formula fallback alike."""
+    zeros, subnormals, Inf, every NaN payload) settle parity completely. 131072 elements
+    take the table-free kernel (approximation + exact-formula fallback); 2^20 and more take
+    the shared-memory table kernel, whose table the exact formula filled; the extra 6
+    elements at reps = 9 exercise its scalar tail."""
     x = np.arange(65536, dtype=np.uint32).astype(np.uint16)
-    x = np.concatenate([x, x[::-1]])  # both halves of a bf16 pair see every value
+    x = np.tile(np.concatenate([x, x[::-1]]), reps)  # both halves of a bf16 pair see every value
+    if reps == 9:
+        x = np.concatenate([x, x[:6]])
     dx = dev(x)
     n = x.size
     out, out_ref = empty_bf16(n), empty_bf16(n)
