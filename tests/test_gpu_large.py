@@ -128,3 +128,49 @@ def test_sampler_step_beyond_2g_elements(anima, rng, free_memory):
     anima.cfg_euler_step(bs, bp, bq, bs, 4.5, 0.73, 0.61, bs.numel())
     torch.cuda.synchronize()
     assert _same_tiles(bs, ref, reps), "cfg_euler_step beyond 2^31 elements"
+
+
+def test_conv_bias_beyond_2g_elements(anima, rng, free_memory):
+    C, sp = 64, 4096
+    x, b, r = dev(O.randn_bf16(rng, (C, sp))), dev(O.randn_bf16(rng, C, std=0.5)), dev(O.randn_bf16(rng, (C, sp)))
+    reps = -(-BIG // x.numel())  # batch items, each the same image
+    ref_add, ref_res = torch.empty_like(x), torch.empty_like(x)
+    anima.conv_bias_add(x, b, ref_add, 1, C, sp)
+    anima.conv_bias_residual_add(x, b, r, ref_res, 1, C, sp)
+    big = _tile(x.view(1, C, sp), reps)
+    anima.conv_bias_add(big, b, big, reps, C, sp)  # in place
+    torch.cuda.synchronize()
+    assert big.numel() > 2**31
+    assert _same_tiles(big, ref_add.view(1, C, sp), reps), "conv_bias_add beyond 2^31 elements"
+    del big
+    big = _tile(x.view(1, C, sp), reps)
+    anima.conv_bias_residual_add(big, b, _tile(r.view(1, C, sp), reps), big, reps, C, sp)
+    torch.cuda.synchronize()
+    assert _same_tiles(big, ref_res.view(1, C, sp), reps), "conv_bias_residual_add beyond 2^31 elements"
+
+
+def test_softmax_beyond_2g_elements(anima, rng, free_memory):
+    N, D = 64, 512
+    x = dev(O.randn_bf16(rng, (N, D), std=3.0))
+    reps = -(-BIG // x.numel())
+    ref = torch.empty_like(x)
+    anima.softmax(x, ref, N, D)
+    big = _tile(x, reps)
+    anima.softmax(big, big, N * reps, D)  # in place, rows beyond 2^31 / D
+    torch.cuda.synchronize()
+    assert _same_tiles(big, ref, reps), "softmax beyond 2^31 elements"
+
+
+def test_head_transpose_beyond_2g_elements(anima, rng, free_memory):
+    """[B*S, H*HD] -> [B, H, S, HD] with B*H*S*HD > 2^31: batch b of the result must be the
+    transpose of batch b of the input (all batches equal here)."""
+    S, H, HD = 64, 16, 128
+    x = dev(O.randn_bf16(rng, (S, H * HD)))
+    reps = -(-BIG // x.numel())
+    ref = torch.empty((1, H, S, HD), dtype=x.dtype, device=x.device)
+    anima.head_transpose_batched(x, ref, 1, H, S, HD)
+    big = _tile(x, reps)
+    out = torch.empty((reps, H, S, HD), dtype=x.dtype, device=x.device)
+    anima.head_transpose_batched(big, out, reps, H, S, HD)
+    torch.cuda.synchronize()
+    assert _same_tiles(out, ref, reps), "head_transpose_batched beyond 2^31 elements"
