@@ -76,6 +76,59 @@ struct CnArgs {
     int tiles_per_image;
 };
 
+// vae_kernels.cu:68-73: pixel p's serial sum of squares over the C channels of a staged tile
+// ([C][kCnPix] in shared memory), in channel order, with the next 8 channels' loads issued
+// before the current 8 fmas; returns rsqrt(mean + eps). Pixels beyond the tile's live width
+// return the value for a zero sum (unused).
+__device__ __forceinline__ float pixel_rms(const anima_bf16 *tile, int p, int live_vecs, int C, float eps) {
+    float q = 0.0f;
+    if (p < live_vecs * 8) {
+        const __nv_bfloat16 *col = reinterpret_cast<const __nv_bfloat16 *>(tile) + p;
+        const int full = C & ~7;
+        float cur[8];
+        if (full > 0) {
+#pragma unroll
+            for (int j = 0; j < 8; ++j) cur[j] = __bfloat162float(col[j * kCnPix]);
+        }
+        for (int c = 0; c < full; c += 8) {
+            float nxt[8];
+            const bool more = c + 8 < full;
+            if (more) {
+#pragma unroll
+                for (int j = 0; j < 8; ++j) nxt[j] = __bfloat162float(col[(c + 8 + j) * kCnPix]);
+            }
+#pragma unroll
+            for (int j = 0; j < 8; ++j) q = __fmaf_rn(cur[j], cur[j], q);
+            if (more) {
+#pragma unroll
+                for (int j = 0; j < 8; ++j) cur[j] = nxt[j];
+            }
+        }
+        for (int c = full; c < C; ++c) {
+            const float f = __bfloat162float(col[c * kCnPix]);
+            q = __fmaf_rn(f, f, q);
+        }
+    }
+    return rsqrtf(__fdiv_rn(q, (float)C) + eps);
+}
+
+// vae_kernels.cu:75-80 on one staged 16-byte chunk (8 pixels of one channel): (x * rms) * gamma,
+// rounded to bf16.
+__device__ __forceinline__ Vec8 norm_chunk(const anima_bf16 *chunk, const float *rms_s, int v, float gm) {
+    const Vec8 xv = *reinterpret_cast<const Vec8 *>(chunk);
+    const float4 r0 = reinterpret_cast<const float4 *>(rms_s)[2 * v];
+    const float4 r1 = reinterpret_cast<const float4 *>(rms_s)[2 * v + 1];
+    const float r[8] = {r0.x, r0.y, r0.z, r0.w, r1.x, r1.y, r1.z, r1.w};
+    Vec8 o;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        const float2 t = __fmul2_rn(make_float2(bf_lo(xv.w[j]), bf_hi(xv.w[j])), make_float2(r[2 * j], r[2 * j + 1]));
+        const float2 u = __fmul2_rn(t, make_float2(gm, gm));
+        o.w[j] = pack_bf2(u.x, u.y);
+    }
+    return o;
+}
+
 template <bool kSilu, bool kBias>
 __global__ void __launch_bounds__(kCnBlock) channel_norm_tile(CnArgs a) {
     pdl_wait();
@@ -108,39 +161,7 @@ __global__ void __launch_bounds__(kCnBlock) channel_norm_tile(CnArgs a) {
         __syncthreads();
     }
 
-    // vae_kernels.cu:68-73: serial sum over channels, one thread per pixel.
-    if (threadIdx.x < kCnPix) {
-        const int p = threadIdx.x;
-        float q = 0.0f;
-        if (p < live_vecs * 8) {
-            const __nv_bfloat16 *col = reinterpret_cast<const __nv_bfloat16 *>(tile) + p;
-            const int full = a.C & ~7;
-            float cur[8];
-            if (full > 0) {
-#pragma unroll
-                for (int j = 0; j < 8; ++j) cur[j] = __bfloat162float(col[j * kCnPix]);
-            }
-            for (int c = 0; c < full; c += 8) {
-                float nxt[8];
-                const bool more = c + 8 < full;
-                if (more) {
-#pragma unroll
-                    for (int j = 0; j < 8; ++j) nxt[j] = __bfloat162float(col[(c + 8 + j) * kCnPix]);
-                }
-#pragma unroll
-                for (int j = 0; j < 8; ++j) q = __fmaf_rn(cur[j], cur[j], q);
-                if (more) {
-#pragma unroll
-                    for (int j = 0; j < 8; ++j) cur[j] = nxt[j];
-                }
-            }
-            for (int c = full; c < a.C; ++c) {
-                const float f = __bfloat162float(col[c * kCnPix]);
-                q = __fmaf_rn(f, f, q);
-            }
-        }
-        rms_s[p] = rsqrtf(__fdiv_rn(q, (float)a.C) + a.eps);
-    }
+    if (threadIdx.x < kCnPix) rms_s[threadIdx.x] = pixel_rms(tile, threadIdx.x, live_vecs, a.C, a.eps);
     __syncthreads();
     pdl_launch();
 
@@ -149,18 +170,7 @@ __global__ void __launch_bounds__(kCnBlock) channel_norm_tile(CnArgs a) {
     for (int q = threadIdx.x; q < nchunks; q += kCnBlock) {
         const int c = q / kVecs, v = q % kVecs;
         if (v >= live_vecs) continue;
-        const Vec8 xv = *reinterpret_cast<const Vec8 *>(tile + c * kCnPix + v * 8);
-        const float4 r0 = reinterpret_cast<const float4 *>(rms_s)[2 * v];
-        const float4 r1 = reinterpret_cast<const float4 *>(rms_s)[2 * v + 1];
-        const float r[8] = {r0.x, r0.y, r0.z, r0.w, r1.x, r1.y, r1.z, r1.w};
-        const float gm = ldb(a.gamma + c);
-        Vec8 o;
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            const float2 t = __fmul2_rn(make_float2(bf_lo(xv.w[j]), bf_hi(xv.w[j])), make_float2(r[2 * j], r[2 * j + 1]));
-            const float2 u = __fmul2_rn(t, make_float2(gm, gm));
-            o.w[j] = pack_bf2(u.x, u.y);
-        }
+        Vec8 o = norm_chunk(tile + c * kCnPix + v * 8, rms_s, v, ldb(a.gamma + c));
         if constexpr (kSilu) o = fast_chunk<SiluF>(o);
         st_vec(a.out + img + (int64_t)c * a.spatial + s_tile + v * 8, o);
     }
@@ -309,6 +319,7 @@ int channel_norm(const anima_bf16 *x, const anima_bf16 *gamma, anima_bf16 *out, 
     const int64_t per_ch = kCnPix * 2 + (kBias ? 4 : 0);  // shared bytes per channel: tile row (+ bias)
     const int64_t smem = (int64_t)C * per_ch;
     const int Cq = (C + kCnCluster - 1) / kCnCluster;
+    int err = ANIMA_OK;
     // Few tiles (at most two per SM): spread each over a cluster. Many tiles keep every SM busy
     // already, and the cluster's hand-offs would then only serialise each tile (measured).
     if (spatial % 8 == 0 && aligned16(x) && aligned16(out) && C >= 64 && (int64_t)Cq * per_ch <= kCnMaxSmem &&
@@ -324,7 +335,6 @@ int channel_norm(const anima_bf16 *x, const anima_bf16 *gamma, anima_bf16 *out, 
         launch(kern, (unsigned)tiles, kCnBlock, (size_t)smem, stream, a);
     } else {
         const int64_t pixels = (int64_t)B * spatial;
-        int err = ANIMA_OK;
         const unsigned blocks = wave_grid((const void *)channel_norm_serial<kSilu, kBias>, 256, 0, pixels, &err);
         if (err) return err;
         launch(channel_norm_serial<kSilu, kBias>, blocks, 256, 0, stream, a, pixels);
