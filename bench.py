@@ -880,6 +880,9 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-headline", action="store_true")
     ap.add_argument("--no-other-ops", action="store_true", help="skip the cfg3/cfg4/fused-entry measurements")
+    ap.add_argument("--workload", choices=["cfg2", "cfg5"], default="cfg2",
+                    help="cfg2 (default): 8192 rows per GPU, weak scaling. cfg5: BASELINE's throughput sweep, "
+                         "8 image pairs at 1536x1536 (18432 rows each) split 8/N pairs per GPU, strong scaling")
     ap.add_argument("--only", default=None,
                     help="profiling aid: run only this op type of the chain (eager), print its timing, exit")
     args = ap.parse_args()
@@ -904,6 +907,13 @@ def main():
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=device)
     n_gpus = world if dist is not None else 1
+    if args.workload == "cfg5":
+        # 8 images at 1536x1536 -> 192x192 latent -> 96x96 patches = 9216 tokens, x CFG 2; the
+        # image pairs are shared out over the GPUs as extra batch rows (rows are independent)
+        if 8 % n_gpus:
+            raise SystemExit("cfg5 shares 8 image pairs over the GPUs: use 1, 2, 4 or 8")
+        CFG.update(pe=(1, 96, 96), batch=2 * (8 // n_gpus))
+        args.no_headline = args.no_other_ops = args.no_cpu_baseline = True
 
     ops = AnimaOps() if args.impl == "anima" else RefOps()
     chain = Chain(ops, device)
@@ -1034,17 +1044,22 @@ def main():
     line = {
         "metric": METRIC, "value": round(value, 1), "unit": "GB/s", "n_gpus": n_gpus, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(ms_per_step, 4), "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "scaling": "weak" if args.workload == "cfg2" else "strong", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic: seeded N(0,1) activations, N(0,0.1) modulation and temb, 1+N(0,0.02) norm weights, "
                 "t~U(0,1)*1000; GEMM/attention outputs are resident synthetic tensors",
-        "config": {"workload": "cfg2: 1024x1024 image -> 4096 tokens x CFG 2, 28-block DiT elementwise chain",
+        "config": {"workload": ("cfg2: 1024x1024 image -> 4096 tokens x CFG 2, 28-block DiT elementwise chain"
+                                if args.workload == "cfg2" else
+                                f"cfg5: 8 images at 1536x1536 -> 9216 tokens x CFG 2, 28-block DiT elementwise "
+                                f"chain, {8 // n_gpus} image pair(s) per GPU"),
                    "rows": chain.R, "hidden": chain.D, "heads": chain.H, "head_dim": chain.HD, "mlp": chain.M,
                    "text_tokens": chain.T, "blocks": chain.NB, "timestep_dim": CFG["ts_dim"],
                    "algorithmic_bytes_per_step": total_bytes,
-                   "l2": f"{NSETS} rotating activation sets, ~1.4 GB touched per step > 126 MB L2 (no flush)",
+                   "l2": f"{NSETS} rotating activation sets, each >> 126 MB L2 (no flush)",
                    "timing": ("CUDA graph replay of the 28 blocks + eager timestep launch per step"
                               if used_graph else "eager launches"),
-                   "parallelism": f"replicas x{n_gpus} (rows independent; no collective on the data path)"},
+                   "parallelism": (f"replicas x{n_gpus} (rows independent; no collective on the data path)"
+                                   if args.workload == "cfg2" else
+                                   f"{8 // n_gpus} of 8 image pairs per GPU x{n_gpus} (no collective on the data path)")},
         "e2e": {"value": round(aggregate_gbs(n_gpus, total_bytes, 1, e2e_ms), 1), "unit": "GB/s",
                 "ms_per_step": round(e2e_ms, 4), "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                 "method": "pinned host buffers; step k+1's upload and step k's download overlap step k's "
@@ -1075,7 +1090,7 @@ def main():
         # no CPU implementation of these ops); the CPU restatement's figure moves beside it
         line["cpu_restatement"] = line["cpu_baseline"]
         line["cpu_baseline"] = {"value": line["value"], "unit": "GB/s", "kind": "reference", "cores": 1,
-                                "sample": f"{args.steps} full cfg2 steps: the reference's kernels.h launchers driven "
+                                "sample": f"{args.steps} full {args.workload} steps: the reference's kernels.h launchers driven "
                                           "from one host thread, kernels on the B200",
                                 "note": "the reference implements this path only as CUDA kernels"}
     if rank == 0:
