@@ -69,3 +69,16 @@ def test_chain_byte_count_matches_the_survey_figure():
     total, per_block, launches = bench.chain_bytes()
     assert abs(total / 28 / 1e6 - 1049.6) < 1.5  # MB per block at cfg2 (plus the tiny mod adds)
     assert sum(launches.values()) == 14
+
+
+def test_cfg5_byte_count_per_image_pair():
+    """BASELINE's throughput sweep: one image pair (9216 tokens x CFG 2 = 18432 rows) is
+    2351 MB per block; --workload cfg5 gives each GPU 8/N pairs as batch rows."""
+    sys.path.insert(0, ROOT)
+    import bench
+
+    cfg = dict(bench.CFG, pe=(1, 96, 96), batch=2)
+    total, _, _ = bench.chain_bytes(cfg)
+    assert abs(total / 28 / 1e6 - 2351) < 4
+    four_pairs, _, _ = bench.chain_bytes(dict(cfg, batch=8))  # 2 GPUs: 4 pairs each
+    assert abs(four_pairs / total - 4) < 0.01
