@@ -297,8 +297,8 @@ class Chain:
             D, st)
 
     def block_fused(self, i, stream):
-        """The same block through the opt-in fused entry points (one-line caller changes, see
-        INTEGRATION.md): mod += temb and the gate copy folded into the adaLN / residual-gate
+        """The same block through the opt-in fused entry points (one-line caller changes):
+        mod += temb and the gate copy folded into the adaLN / residual-gate
         norms (two gate buffers alternate), QK RMSNorm + RoPE in one pass. 9 launches."""
         o, st = self.ops, stream
         bs = self.sets[i % NSETS]

@@ -62,7 +62,7 @@ def test_reference_arm_runs_on_rank_zero_only(monkeypatch):
     assert bench.main() is None  # returns before touching a GPU
 
 
-def test_chain_byte_count_matches_the_survey_figure():
+def test_chain_byte_count_per_block():
     sys.path.insert(0, ROOT)
     import bench
 
