@@ -84,3 +84,37 @@ def test_reference_archive_as_built_shadows_the_library(archives):
 def test_localized_archive_binds_callers_to_the_b200_library(archives):
     d, _, local = archives
     assert _link_and_run(d, local, "caller_local") == -2
+
+
+CALLERS = ("transformer", "qwen3", "llm_adapter", "vae")
+
+
+def test_reference_callers_resolve_every_launcher(archives):
+    """The reference's own callers (transformer.cpp, qwen3.cpp, llm_adapter.cpp, vae.cpp,
+    compiled unchanged into oracle/_ref/callers by `make -C oracle callers`): every
+    kernels.h launcher they leave undefined must be defined by libanima_b200.so (the
+    replaced launchers) or by the localized reference archive (the launchers this library
+    does not replace), and each replaced one must bind to the library."""
+    import anima_b200
+
+    objs = {c: os.path.join(ROOT, "oracle", "_ref", "callers", c + ".o") for c in CALLERS}
+    if not all(os.path.exists(o) for o in objs.values()):
+        pytest.skip("oracle/_ref/callers not built (make -C oracle callers needs the reference tree)")
+    _, plain, local = archives
+    out = subprocess.run(["nm", "-D", "--defined-only", anima_b200.LIB_PATH], capture_output=True, text=True,
+                         check=True).stdout
+    lib = {line.split()[-1] for line in out.splitlines() if " T " in line}
+    g_plain, g_local = _nm_globals(plain), _nm_globals(local)
+    replaced = {l.strip() for l in open(os.path.join(PKG, "integrate", "replaced_launchers.txt"))
+                if l.strip() and not l.startswith("#")}
+    bound = 0
+    for name, obj in objs.items():
+        und = set(subprocess.run(["nm", "-u", obj], capture_output=True, text=True, check=True).stdout.split())
+        launchers = und & (g_plain | replaced)
+        assert launchers, f"{name}.cpp calls no reference launcher?"
+        unresolved = [s for s in launchers if s not in lib and s not in g_local]
+        assert not unresolved, f"{name}.cpp: unresolved launchers {unresolved}"
+        for s in launchers & replaced:
+            assert s in lib and s not in g_local, f"{name}.cpp: {s} would not bind to the B200 library"
+        bound += len(launchers & replaced)
+    assert bound >= 30  # the four callers reach 35 replaced launchers (some shared)
