@@ -46,6 +46,7 @@ SIGNATURES = {
     "anima_head_transpose_batched_bf16": (P, P, I32, I32, I32, I32, P),
     "anima_head_untranspose_batched_bf16": (P, P, I32, I32, I32, I32, P),
     "anima_expand_kv_bf16": (P, P, I32, I32, I32, I32, I32, P),
+    "anima_head_transpose_qk_norm_rope_bf16": (P, P, P, P, P, I32, I32, I32, F32, P),
     "anima_causal_mask_bf16": (P, I32, I32, P),
     "anima_softmax_bf16": (P, P, I32, I32, P),
     "anima_causal_softmax_bf16": (P, P, I32, I32, P),
@@ -281,6 +282,11 @@ def head_transpose_batched(src, dst, B, H, S, HD, stream=None):
 
 def head_untranspose_batched(src, dst, B, H, S, HD, stream=None):
     call("anima_head_untranspose_batched_bf16", _ptr(src), _ptr(dst), B, H, S, HD, _stream(stream))
+
+
+def head_transpose_qk_norm_rope(src, weight, cos_table, sin_table, dst, H, T, HD, eps=1e-6, stream=None):
+    call("anima_head_transpose_qk_norm_rope_bf16", _ptr(src), _ptr(weight), _ptr(cos_table), _ptr(sin_table),
+         _ptr(dst), H, T, HD, eps, _stream(stream))
 
 
 def expand_kv(kv, out, B, KV_H, Q_H, T, D, stream=None):

@@ -263,6 +263,87 @@ __global__ void __launch_bounds__(kRopeBlock) qk_norm_rope_128(QkArgs a) {
 
 bool bf16_ok(const void *p) { return aligned_to(p, 2); }
 
+// -------------------------- fused head transpose + QK RMSNorm + standard RoPE (Qwen3)
+// qwen3.cpp:164-178: head_transpose_bf16 ([T, H*HD] -> [H, T, HD]), rms_norm_bf16 on each
+// head row (weight nullable), rope_standard_bf16 (fp32 tables [T, HD/2]). One 8-lane team per
+// (token t, head h) with HD = 128, teams in source order (the heads of a token share their
+// table row in L1): lane l holds elements 8l..8l+7 and 64+8l..64+8l+7, i.e. both members of
+// its rotation pairs. The statistics replay the reference's tree (ref_pair_tree_sum<8,2>),
+// the normalised values are rounded to bf16 as rms_norm_bf16 stores them, and the rotation
+// is rope_standard_bf16's own contraction (rot_f32); no tables = no rotation.
+struct HeadArgs {
+    const anima_bf16 *src, *w;
+    const float *cos_t, *sin_t;
+    anima_bf16 *dst;
+    int H, T;
+    int64_t heads;  // T*H
+    float eps;
+};
+
+__global__ void __launch_bounds__(kRopeBlock) head_norm_rope_128(HeadArgs a) {
+    pdl_wait();
+    constexpr int LPR = 8, K = 2, HD = 128;
+    const int l = threadIdx.x & (LPR - 1);
+    const int64_t hid = (int64_t)blockIdx.x * (blockDim.x / LPR) + threadIdx.x / LPR;  // t*H + h
+    const bool live = hid < a.heads;
+    const int64_t t = live ? hid / a.H : 0, h = hid - t * a.H;
+    const anima_bf16 *p = a.src + hid * HD + l * 8;
+    Vec8 v[K] = {Vec8{{0u, 0u, 0u, 0u}}, Vec8{{0u, 0u, 0u, 0u}}};
+    if (live) {
+        v[0] = ld_stream(p);
+        v[1] = ld_stream(p + 64);
+    }
+    Vec8 w[K];
+    if (a.w) {
+        w[0] = ld_cached(a.w + l * 8);
+        w[1] = ld_cached(a.w + 64 + l * 8);
+    }
+    float4 cv[2], sv[2];
+    if (a.cos_t) {
+        const float4 *cp = reinterpret_cast<const float4 *>(a.cos_t + t * 64 + l * 8);
+        const float4 *sp = reinterpret_cast<const float4 *>(a.sin_t + t * 64 + l * 8);
+        cv[0] = __ldg(cp);
+        cv[1] = __ldg(cp + 1);
+        sv[0] = __ldg(sp);
+        sv[1] = __ldg(sp + 1);
+    }
+    float q[K][4];
+#pragma unroll
+    for (int k = 0; k < K; ++k)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const float lo = bf_lo(v[k].w[j]), hi = bf_hi(v[k].w[j]);
+            q[k][j] = fmaf(hi, hi, lo * lo);
+        }
+    const float r = rsqrtf(__fdiv_rn(ref_pair_tree_sum<LPR, K>(q, l, 0xffffffffu), (float)HD) + a.eps);
+    pdl_launch();
+    if (!live) return;
+    // rms_norm.cu:62-64: (x * r) * w, stored as bf16
+    Vec8 n[K];
+#pragma unroll
+    for (int k = 0; k < K; ++k)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            float2 f = __fmul2_rn(make_float2(bf_lo(v[k].w[j]), bf_hi(v[k].w[j])), make_float2(r, r));
+            if (a.w) f = __fmul2_rn(f, make_float2(bf_lo(w[k].w[j]), bf_hi(w[k].w[j])));
+            n[k].w[j] = pack_bf2(f.x, f.y);
+        }
+    anima_bf16 *o = a.dst + (h * a.T + t) * HD + l * 8;
+    if (a.cos_t) {  // gemma_ops.cu:80-86 on the bf16 values
+        const float c[8] = {cv[0].x, cv[0].y, cv[0].z, cv[0].w, cv[1].x, cv[1].y, cv[1].z, cv[1].w};
+        const float sn[8] = {sv[0].x, sv[0].y, sv[0].z, sv[0].w, sv[1].x, sv[1].y, sv[1].z, sv[1].w};
+        float f1[8], f2[8], o1[8], o2[8];
+        unpack8(n[0], f1);
+        unpack8(n[1], f2);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) rot_f32(f1[e], f2[e], c[e], sn[e], o1[e], o2[e]);
+        n[0] = pack8(o1);
+        n[1] = pack8(o2);
+    }
+    st_vec(o, n[0]);
+    st_vec(o + 64, n[1]);
+}
+
 }  // namespace
 }  // namespace anima
 
@@ -345,4 +426,33 @@ extern "C" int anima_qk_norm_rope_bf16(anima_bf16 *x, const anima_bf16 *weight,
     if (heads > 2147483647) return ANIMA_ERR_TOO_LARGE;
     if (int e = anima_rms_norm_bf16(x, weight, x, (int)heads, HD, eps, stream)) return e;
     return anima_rope_cosmos_strided_bf16(x, cos_table, sin_table, B, S, H, HD, stream);
+}
+
+extern "C" int anima_head_transpose_qk_norm_rope_bf16(const anima_bf16 *src, const anima_bf16 *weight,
+                                                      const float *cos_table, const float *sin_table,
+                                                      anima_bf16 *dst, int H, int T, int HD, float eps,
+                                                      anima_stream_t stream) {
+    if (H < 0 || T < 0 || HD <= 0 || (HD & 1)) return ANIMA_ERR_BAD_SHAPE;
+    const int64_t heads = (int64_t)T * H, n = heads * HD;
+    if (n == 0) return ANIMA_OK;
+    if (!src || !dst || (!cos_table != !sin_table)) return ANIMA_ERR_NULL_POINTER;
+    if (!bf16_ok(src) || !bf16_ok(dst) || (weight && !bf16_ok(weight)) ||
+        (cos_table && (!aligned_to(cos_table, 4) || !aligned_to(sin_table, 4))))
+        return ANIMA_ERR_MISALIGNED;
+    if (overlaps(src, n * 2, dst, n * 2) || (weight && overlaps(weight, (int64_t)HD * 2, dst, n * 2)) ||
+        (cos_table && (overlaps(cos_table, (int64_t)T * HD * 2, dst, n * 2) ||
+                       overlaps(sin_table, (int64_t)T * HD * 2, dst, n * 2))))
+        return ANIMA_ERR_OVERLAP;
+    if (HD == 128 && aligned16(src) && aligned16(dst) && (!weight || aligned16(weight)) &&
+        (!cos_table || (aligned16(cos_table) && aligned16(sin_table)))) {
+        HeadArgs a{src, weight, cos_table, sin_table, dst, H, T, heads, eps};
+        const int64_t per_block = kRopeBlock / 8;
+        launch(head_norm_rope_128, (unsigned)((heads + per_block - 1) / per_block), kRopeBlock, 0, stream, a);
+        return launch_status();
+    }
+    // Other head sizes: the reference's three steps, back to back.
+    if (heads > 2147483647) return ANIMA_ERR_TOO_LARGE;
+    if (int e = anima_head_transpose_bf16(src, dst, H, T, HD, stream)) return e;
+    if (int e = anima_rms_norm_bf16(dst, weight, dst, (int)heads, HD, eps, stream)) return e;
+    return cos_table ? anima_rope_standard_bf16(dst, cos_table, sin_table, (int)heads, T, HD, stream) : ANIMA_OK;
 }

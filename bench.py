@@ -127,6 +127,9 @@ class AnimaOps:
     def causal_softmax(self, sc, o, H, T, s):
         self._ck("causal_softmax", self.L.anima_causal_softmax_bf16(sc, o, H, T, s))
 
+    def head_qk_norm_rope(self, src, w, c, sn, dst, H, T, HD, eps, s):
+        self._ck("head_qk_norm_rope", self.L.anima_head_transpose_qk_norm_rope_bf16(src, w, c, sn, dst, H, T, HD, eps, s))
+
     def softmax_f32_to_bf16(self, x, o, N, D, s):
         self._ck("softmax_f32", self.L.anima_softmax_f32_to_bf16(x, o, N, D, s))
 
@@ -195,6 +198,11 @@ class RefOps:
     def rms_norm_channel_silu(self, x, gamma, o, B, C, sp, eps, s):  # vae.cpp:148,184
         self.R.rms_norm_channel_bf16(x, gamma, o, B, C, sp, eps, s)
         self.R.silu_bf16(o, o, B * C * sp, s)
+
+    def head_qk_norm_rope(self, src, w, c, sn, dst, H, T, HD, eps, s):  # qwen3.cpp:164-178
+        self.R.head_transpose_bf16(src, dst, H, T, HD, s)
+        self.R.rms_norm_bf16(dst, w, dst, H * T, HD, eps, s)
+        self.R.rope_standard_bf16(dst, c, sn, H * T, T, HD, s)
 
     def causal_softmax(self, sc, o, H, T, s):  # qwen3.cpp:205-208
         self.R.causal_mask_bf16(sc, H, T, s)
@@ -659,6 +667,15 @@ def other_ops(ops, device, peak, reps=96):
                   lambda i: ops.call("head_transpose", P(qb[i]), P(qhd[i]), QH, T, HDq, S())))
     cases.append(("cfg3_head_untranspose_16x512x128", 4 * T * QH * HDq, 1, 8,
                   lambda i: ops.call("head_untranspose", P(qhd[i]), P(qb[i]), QH, T, HDq, S())))
+    cases.append(("cfg3_head_transpose_qk_norm_rope_512x16x128", 4 * T * QH * HDq + 2 * HDq + 4 * T * HDq,
+                  1 if ops.kind == "anima" else 3, 8,
+                  lambda i: ops.head_qk_norm_rope(P(qb[i]), P(wh), P(cs_d), P(sn_d), P(qhd[i]), QH, T, HDq, eps, S())))
+    if ops.kind == "anima":
+        cases.append(("cfg3_head_transpose_qk_norm_rope_512x16x128_as_three_calls",
+                      4 * T * QH * HDq + 2 * HDq + 4 * T * HDq, 3, 8,
+                      lambda i: (ops.call("head_transpose", P(qb[i]), P(qhd[i]), QH, T, HDq, S()),
+                                 ops.call("rms_norm", P(qhd[i]), P(wh), P(qhd[i]), QH * T, HDq, eps, S()),
+                                 ops.call("rope_standard", P(qhd[i]), P(cs_d), P(sn_d), QH * T, T, HDq, S()))))
     kvh = [bf((KVH, T, HDq)) for _ in range(8)]
     cases.append(("cfg3_expand_kv_8to16x512x128", 2 * (KVH + QH) * T * HDq, 1, 8,
                   lambda i: ops.call("expand_kv", P(kvh[i]), P(qhd[i]), 1, KVH, QH, T, HDq, S())))

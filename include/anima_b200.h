@@ -266,6 +266,16 @@ ANIMA_API int anima_head_transpose_batched_bf16(const anima_bf16 *src, anima_bf1
 ANIMA_API int anima_head_untranspose_batched_bf16(const anima_bf16 *src, anima_bf16 *dst, int B, int H, int S,
                                        int HD, anima_stream_t stream);
 
+/* head_transpose_bf16 + rms_norm_bf16 on each head row + rope_standard_bf16 in one pass:
+ * dst[h, t, :] = rope(bf16(rms_norm(src[t, h*HD : (h+1)*HD]) * weight[:])), the chain at
+ * qwen3.cpp:164-178 for q and k (and llm_adapter.cpp:169-187). weight may be NULL (no
+ * weight), cos_table/sin_table ([T, HD/2] fp32) may both be NULL (no rotation). HD = 128
+ * runs one fused kernel; other head sizes run the three steps. src and dst may not
+ * overlap. No reference counterpart (opt-in). */
+ANIMA_API int anima_head_transpose_qk_norm_rope_bf16(const anima_bf16 *src, const anima_bf16 *weight,
+                                          const float *cos_table, const float *sin_table, anima_bf16 *dst,
+                                          int H, int T, int HD, float eps, anima_stream_t stream);
+
 /* GQA expansion [B, KV_H, T, D] -> [B, Q_H, T, D], q head h reading kv head h / (Q_H / KV_H).
  * Replaces expand_kv_bf16 (gemma_ops.cu:99-127). Q_H must be a multiple of KV_H (the
  * reference reads past kv otherwise); rejected with ANIMA_ERR_BAD_SHAPE. */

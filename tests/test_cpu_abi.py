@@ -113,6 +113,9 @@ X, Y, Z = 0x10000, 0x20000, 0x30000  # never dereferenced: every call below fail
     (("anima_rms_norm_channel_silu_bf16", X, None, Z, 1, 4, 16, 1e-6, None), -1),
     (("anima_head_transpose_bf16", X, X + 64, 4, 8, 16, None), -5),
     (("anima_head_untranspose_batched_bf16", X, None, 1, 4, 8, 16, None), -1),
+    (("anima_head_transpose_qk_norm_rope_bf16", X, Y, Z, None, X + 0x100000, 4, 8, 128, 1e-6, None), -1),
+    (("anima_head_transpose_qk_norm_rope_bf16", X, Y, None, None, X + 0x800, 4, 8, 128, 1e-6, None), -5),
+    (("anima_head_transpose_qk_norm_rope_bf16", X, Y, Z + 2, Z + 0x1002, X + 0x100000, 4, 8, 128, 1e-6, None), -3),
     (("anima_expand_kv_bf16", X, Y, 1, 3, 8, 4, 16, None), -2),
     (("anima_expand_kv_bf16", X, Y + 1, 1, 2, 8, 4, 16, None), -3),
     (("anima_causal_mask_bf16", None, 2, 8, None), -1),

@@ -135,3 +135,27 @@ def test_softmax_f32_to_bf16_ragged_rows(anima, rng, N, D):
     anima.softmax_f32_to_bf16(torch.from_numpy(x).cuda(), out, N, D)
     torch.cuda.synchronize()
     assert_one_ulp(host(out), O.softmax_f32_to_bf16(x, N, D), "softmax_f32_to_bf16 (ragged rows) vs oracle")
+
+
+@pytest.mark.parametrize("H,T,HD,weight,rope", [(16, 512, 128, True, True), (8, 512, 128, True, True),
+                                                (3, 7, 128, False, True), (4, 33, 128, True, False),
+                                                (4, 9, 64, True, True)])
+def test_head_transpose_qk_norm_rope_matches_reference_chain(anima, ref, rng, H, T, HD, weight, rope):
+    """qwen3.cpp:164-178 (rope=False: llm_adapter.cpp:169-177 without tables); HD = 64 takes
+    the three-step path."""
+    x = O.randn_bf16(rng, (T, H * HD))
+    w = O.randn_bf16(rng, HD, mean=1.0, std=0.02)
+    cs, sn = O.standard_rope_tables(T, HD, 1e6)
+    dx, dw = dev(x), dev(w)
+    dc, ds = torch.from_numpy(cs).cuda(), torch.from_numpy(sn).cuda()
+    out = empty_bf16((H, T, HD))
+    anima.head_transpose_qk_norm_rope(dx, dw if weight else None, dc if rope else None, ds if rope else None,
+                                      out, H, T, HD, 1e-6)
+    r = empty_bf16((H, T, HD))
+    s = stream_ptr()
+    ref.head_transpose_bf16(dx.data_ptr(), r.data_ptr(), H, T, HD, s)
+    ref.rms_norm_bf16(r.data_ptr(), dw.data_ptr() if weight else None, r.data_ptr(), H * T, HD, 1e-6, s)
+    if rope:
+        ref.rope_standard_bf16(r.data_ptr(), dc.data_ptr(), ds.data_ptr(), H * T, T, HD, s)
+    torch.cuda.synchronize()
+    assert_bit_exact(host(out), host(r), "head_transpose_qk_norm_rope vs head_transpose + rms_norm + rope_standard")
