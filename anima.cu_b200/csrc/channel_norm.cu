@@ -1,6 +1,8 @@
 // channel_norm.cu -- VAE channel RMSNorm (+ optional fused SiLU) on NCHW bf16 (sm_100a).
 //
 // out[b,c,s] = x[b,c,s] * rsqrt(mean_c x[b,:,s]^2 + eps) * gamma[c]      (vae_kernels.cu:60-81)
+// and its ungated sibling, the pixel norm (kPixel):
+// out[b,c,s] = x[b,c,s] * (1 / sqrt(mean_c x[b,:,s]^2 + eps))              (vae_kernels.cu:15-52)
 //
 // The reduction runs over channels, which sit `spatial` elements apart. The reference
 // gives each pixel a thread that walks the channels with 2-byte strided loads, twice
@@ -76,10 +78,20 @@ struct CnArgs {
     int tiles_per_image;
 };
 
+// The per-pixel scale from the sum of squares q: rsqrtf for the channel norm
+// (vae_kernels.cu:74); 1.0f / sqrtf(...) in IEEE arithmetic for the pixel norm
+// (vae_kernels.cu:30-31).
+template <bool kPixel>
+__device__ __forceinline__ float norm_scale(float q, int C, float eps) {
+    const float m = __fdiv_rn(q, (float)C) + eps;
+    return kPixel ? __fdiv_rn(1.0f, __fsqrt_rn(m)) : rsqrtf(m);
+}
+
 // vae_kernels.cu:68-73: pixel p's serial sum of squares over the C channels of a staged tile
 // ([C][kCnPix] in shared memory), in channel order, with the next 8 channels' loads issued
 // before the current 8 fmas; returns rsqrt(mean + eps). Pixels beyond the tile's live width
 // return the value for a zero sum (unused).
+template <bool kPixel>
 __device__ __forceinline__ float pixel_rms(const anima_bf16 *tile, int p, int live_vecs, int C, float eps) {
     float q = 0.0f;
     if (p < live_vecs * 8) {
@@ -109,7 +121,7 @@ __device__ __forceinline__ float pixel_rms(const anima_bf16 *tile, int p, int li
             q = __fmaf_rn(f, f, q);
         }
     }
-    return rsqrtf(__fdiv_rn(q, (float)C) + eps);
+    return norm_scale<kPixel>(q, C, eps);
 }
 
 // vae_kernels.cu:75-80 on one staged 16-byte chunk (8 pixels of one channel): (x * rms) * gamma,
@@ -129,7 +141,7 @@ __device__ __forceinline__ Vec8 norm_chunk(const anima_bf16 *chunk, const float 
     return o;
 }
 
-template <bool kSilu, bool kBias>
+template <bool kSilu, bool kBias, bool kPixel>
 __global__ void __launch_bounds__(kCnBlock) channel_norm_tile(CnArgs a) {
     pdl_wait();
     constexpr int kVecs = kCnPix / 8;  // 16-byte chunks per channel row of the tile
@@ -161,7 +173,7 @@ __global__ void __launch_bounds__(kCnBlock) channel_norm_tile(CnArgs a) {
         __syncthreads();
     }
 
-    if (threadIdx.x < kCnPix) rms_s[threadIdx.x] = pixel_rms(tile, threadIdx.x, live_vecs, a.C, a.eps);
+    if (threadIdx.x < kCnPix) rms_s[threadIdx.x] = pixel_rms<kPixel>(tile, threadIdx.x, live_vecs, a.C, a.eps);
     __syncthreads();
     pdl_launch();
 
@@ -170,7 +182,8 @@ __global__ void __launch_bounds__(kCnBlock) channel_norm_tile(CnArgs a) {
     for (int q = threadIdx.x; q < nchunks; q += kCnBlock) {
         const int c = q / kVecs, v = q % kVecs;
         if (v >= live_vecs) continue;
-        Vec8 o = norm_chunk(tile + c * kCnPix + v * 8, rms_s, v, ldb(a.gamma + c));
+        // the pixel norm has no gamma: a factor of exactly 1 leaves x * rms as it is
+        Vec8 o = norm_chunk(tile + c * kCnPix + v * 8, rms_s, v, kPixel ? 1.0f : ldb(a.gamma + c));
         if constexpr (kSilu) o = fast_chunk<SiluF>(o);
         st_vec(a.out + img + (int64_t)c * a.spatial + s_tile + v * 8, o);
     }
@@ -187,7 +200,7 @@ __global__ void __launch_bounds__(kCnBlock) channel_norm_tile(CnArgs a) {
 // done.
 constexpr int kCnCluster = 4;
 
-template <bool kSilu, bool kBias>
+template <bool kSilu, bool kBias, bool kPixel>
 __global__ void __launch_bounds__(kCnBlock) channel_norm_cluster(CnArgs a, int Cq) {
     namespace cg = cooperative_groups;
     cg::cluster_group cluster = cg::this_cluster();
@@ -246,7 +259,7 @@ __global__ void __launch_bounds__(kCnBlock) channel_norm_cluster(CnArgs a, int C
             if (r + 1 < kCnCluster) {
                 cluster.map_shared_rank(part_s, r + 1)[p] = q;
             } else {
-                const float rv = rsqrtf(__fdiv_rn(q, (float)a.C) + a.eps);
+                const float rv = norm_scale<kPixel>(q, a.C, a.eps);
                 for (int k = 0; k < kCnCluster; ++k) cluster.map_shared_rank(rms_s, k)[p] = rv;
             }
         }
@@ -261,7 +274,7 @@ __global__ void __launch_bounds__(kCnBlock) channel_norm_cluster(CnArgs a, int C
         const float4 r0 = reinterpret_cast<const float4 *>(rms_s)[2 * v];
         const float4 r1 = reinterpret_cast<const float4 *>(rms_s)[2 * v + 1];
         const float r[8] = {r0.x, r0.y, r0.z, r0.w, r1.x, r1.y, r1.z, r1.w};
-        const float gm = ldb(a.gamma + c0 + c);
+        const float gm = kPixel ? 1.0f : ldb(a.gamma + c0 + c);
         Vec8 o;
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
@@ -275,7 +288,7 @@ __global__ void __launch_bounds__(kCnBlock) channel_norm_cluster(CnArgs a, int C
 }
 
 // Reference-order kernel for any shape: one thread per (image, pixel).
-template <bool kSilu, bool kBias>
+template <bool kSilu, bool kBias, bool kPixel>
 __global__ void channel_norm_serial(CnArgs a, int64_t pixels) {
     pdl_wait();
     for (int64_t p = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; p < pixels;
@@ -292,26 +305,27 @@ __global__ void channel_norm_serial(CnArgs a, int64_t pixels) {
             const float f = xin(c);
             q = __fmaf_rn(f, f, q);
         }
-        const float r = rsqrtf(__fdiv_rn(q, (float)a.C) + a.eps);
+        const float r = norm_scale<kPixel>(q, a.C, a.eps);
         for (int c = 0; c < a.C; ++c) {
             const int64_t i = (int64_t)c * a.spatial + s;
-            float o = (xin(c) * r) * ldb(a.gamma + c);
+            float o = kPixel ? xin(c) * r : (xin(c) * r) * ldb(a.gamma + c);
             if constexpr (kSilu) o = silu_f(bf16_round(o));
             *reinterpret_cast<__nv_bfloat16 *>(ob + i) = __float2bfloat16_rn(o);
         }
     }
 }
 
-template <bool kSilu, bool kBias = false>
+template <bool kSilu, bool kBias = false, bool kPixel = false>
 int channel_norm(const anima_bf16 *x, const anima_bf16 *gamma, anima_bf16 *out, int B, int C,
                  int spatial, float eps, cudaStream_t stream, const anima_bf16 *bias = nullptr) {
     if (B < 0 || C <= 0 || spatial < 0) return ANIMA_ERR_BAD_SHAPE;
     const int64_t n = (int64_t)B * C * spatial;
     if (n == 0) return ANIMA_OK;
-    if (!x || !gamma || !out || (kBias && !bias)) return ANIMA_ERR_NULL_POINTER;
-    if (!aligned_to(x, 2) || !aligned_to(gamma, 2) || !aligned_to(out, 2) || (kBias && !aligned_to(bias, 2)))
+    if (!x || (!kPixel && !gamma) || !out || (kBias && !bias)) return ANIMA_ERR_NULL_POINTER;
+    if (!aligned_to(x, 2) || (!kPixel && !aligned_to(gamma, 2)) || !aligned_to(out, 2) ||
+        (kBias && !aligned_to(bias, 2)))
         return ANIMA_ERR_MISALIGNED;
-    if (partial_overlap(x, n * 2, out, n * 2) || partial_overlap(gamma, (int64_t)C * 2, out, n * 2) ||
+    if (partial_overlap(x, n * 2, out, n * 2) || (!kPixel && partial_overlap(gamma, (int64_t)C * 2, out, n * 2)) ||
         (kBias && overlaps(bias, (int64_t)C * 2, out, n * 2)))
         return ANIMA_ERR_OVERLAP;
     CnArgs a{x, gamma, out, bias, C, spatial, eps, (spatial + kCnPix - 1) / kCnPix};
@@ -324,20 +338,20 @@ int channel_norm(const anima_bf16 *x, const anima_bf16 *gamma, anima_bf16 *out, 
     // already, and the cluster's hand-offs would then only serialise each tile (measured).
     if (spatial % 8 == 0 && aligned16(x) && aligned16(out) && C >= 64 && (int64_t)Cq * per_ch <= kCnMaxSmem &&
         tiles <= 2 * (int64_t)sm_count()) {
-        auto kern = channel_norm_cluster<kSilu, kBias>;
-        if (int e = allow_dynamic_smem((const void *)kern, kCnMaxSmem, kBias ? 7 : kSilu ? 5 : 4)) return e;
+        auto kern = channel_norm_cluster<kSilu, kBias, kPixel>;
+        if (int e = allow_dynamic_smem((const void *)kern, kCnMaxSmem, kPixel ? 13 : kBias ? 7 : kSilu ? 5 : 4)) return e;
         launch_cluster(kern, kCnCluster, (unsigned)(tiles * kCnCluster), kCnBlock, (size_t)(Cq * per_ch), stream, a,
                        Cq);
     } else if (spatial % 8 == 0 && aligned16(x) && aligned16(out) && smem <= kCnMaxSmem &&
         tiles < 2147483647) {
-        auto kern = channel_norm_tile<kSilu, kBias>;
-        if (int e = allow_dynamic_smem((const void *)kern, kCnMaxSmem, kBias ? 6 : kSilu ? 1 : 0)) return e;
+        auto kern = channel_norm_tile<kSilu, kBias, kPixel>;
+        if (int e = allow_dynamic_smem((const void *)kern, kCnMaxSmem, kPixel ? 12 : kBias ? 6 : kSilu ? 1 : 0)) return e;
         launch(kern, (unsigned)tiles, kCnBlock, (size_t)smem, stream, a);
     } else {
         const int64_t pixels = (int64_t)B * spatial;
-        const unsigned blocks = wave_grid((const void *)channel_norm_serial<kSilu, kBias>, 256, 0, pixels, &err);
+        const unsigned blocks = wave_grid((const void *)channel_norm_serial<kSilu, kBias, kPixel>, 256, 0, pixels, &err);
         if (err) return err;
-        launch(channel_norm_serial<kSilu, kBias>, blocks, 256, 0, stream, a, pixels);
+        launch(channel_norm_serial<kSilu, kBias, kPixel>, blocks, 256, 0, stream, a, pixels);
     }
     return launch_status();
 }
@@ -363,4 +377,9 @@ extern "C" int anima_conv_bias_rms_norm_channel_silu_bf16(const anima_bf16 *x, c
                                                           const anima_bf16 *gamma, anima_bf16 *out, int B, int C,
                                                           int spatial, float eps, anima_stream_t stream) {
     return channel_norm<true, true>(x, gamma, out, B, C, spatial, eps, stream, bias);
+}
+
+extern "C" int anima_pixel_norm_bf16(const anima_bf16 *x, anima_bf16 *out, int B, int C, int spatial, float eps,
+                                     anima_stream_t stream) {
+    return channel_norm<false, false, true>(x, nullptr, out, B, C, spatial, eps, stream);
 }

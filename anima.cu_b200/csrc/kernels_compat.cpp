@@ -172,6 +172,11 @@ void head_untranspose_batched_bf16(const __nv_bfloat16 *src, __nv_bfloat16 *dst,
     record(anima_head_untranspose_batched_bf16(in(src), io(dst), B, H, S, HD, stream));
 }
 
+void pixel_norm_bf16(const __nv_bfloat16 *x, __nv_bfloat16 *out, int B, int C, int spatial, float eps,
+                     cudaStream_t stream) {
+    record(anima_pixel_norm_bf16(in(x), io(out), B, C, spatial, eps, stream));
+}
+
 void patchify_3d_bf16(const __nv_bfloat16 *src, __nv_bfloat16 *dst, int B, int C, int T, int H, int W, int pT,
                       int pH, int pW, cudaStream_t stream) {
     record(anima_patchify_3d_bf16(in(src), io(dst), B, C, T, H, W, pT, pH, pW, stream));

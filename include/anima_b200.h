@@ -179,6 +179,12 @@ ANIMA_API int anima_rms_norm_channel_bf16(const anima_bf16 *x, const anima_bf16 
  * calls with one kernel and produces the same bits as that chain (the intermediate
  * bf16 rounding is kept). */
 
+/* out[b,c,s] = x[b,c,s] / sqrt(mean_c x[b,:,s]^2 + eps) on NCHW (no gamma; IEEE sqrt and
+ * divide as the reference). Replaces pixel_norm_bf16, kernels.h:156-158 (vae_kernels.cu:15-52).
+ * out may alias x. */
+ANIMA_API int anima_pixel_norm_bf16(const anima_bf16 *x, anima_bf16 *out, int B, int C, int spatial, float eps,
+                         anima_stream_t stream);
+
 /* silu(rms_norm_channel(x)) in one pass: the chain rms_norm_channel_bf16 + silu_bf16 at
  * vae.cpp:148,184 (and :189, :457-458). */
 ANIMA_API int anima_rms_norm_channel_silu_bf16(const anima_bf16 *x, const anima_bf16 *gamma,

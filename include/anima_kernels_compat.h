@@ -77,6 +77,9 @@ void gemma_rms_norm_bf16(const __nv_bfloat16 *x, const __nv_bfloat16 *weight, __
 // kernels.h:177-180
 void rms_norm_channel_bf16(const __nv_bfloat16 *x, const __nv_bfloat16 *gamma, __nv_bfloat16 *out,
                            int B, int C, int spatial, float eps = 1e-6f, cudaStream_t stream = 0);
+// kernels.h:156-158
+void pixel_norm_bf16(const __nv_bfloat16 *x, __nv_bfloat16 *out, int B, int C, int spatial, float eps = 1e-6f,
+                     cudaStream_t stream = 0);
 // kernels.h:189-192
 void channel_scale_shift_bf16(const __nv_bfloat16 *x, const __nv_bfloat16 *scale, const __nv_bfloat16 *shift,
                               __nv_bfloat16 *out, int B, int C, int spatial, cudaStream_t stream = 0);

@@ -412,6 +412,26 @@ void oracle_embedding_lookup(const uint16_t *table, const int32_t *ids, uint16_t
 
 /* ------------------------------------------------------------- VAE channel norm */
 
+/* vae_kernels.cu:15-39, launched per batch item at :41-52 (nvcc contracts sum_sq += v*v) */
+void oracle_pixel_norm(const uint16_t *x, uint16_t *out, int B, int C, int spatial, float eps) {
+    for (int b = 0; b < B; ++b) {
+        const uint16_t *xb = x + (int64_t)b * C * spatial;
+        uint16_t *ob = out + (int64_t)b * C * spatial;
+        for (int s = 0; s < spatial; ++s) {
+            float q = 0.0f;
+            for (int c = 0; c < C; ++c) {
+                float v = B2F(xb[(int64_t)c * spatial + s]);
+                q = fmaf(v, v, q);
+            }
+            float inv = 1.0f / sqrtf(q / (float)C + eps);
+            for (int c = 0; c < C; ++c) {
+                int64_t i = (int64_t)c * spatial + s;
+                ob[i] = F2B(B2F(xb[i]) * inv);
+            }
+        }
+    }
+}
+
 /* vae_kernels.cu:60-81, launched per batch item at :83-98 */
 void oracle_rms_norm_channel(const uint16_t *x, const uint16_t *gamma, uint16_t *out, int B,
                              int C, int spatial, float eps) {

@@ -104,6 +104,9 @@ void oracle_rope_standard(uint16_t *x, const float *cos_t, const float *sin_t,
 void oracle_embedding_lookup(const uint16_t *table, const int32_t *ids, uint16_t *out, int T,
                              int D, int vocab);
 
+/* vae_kernels.cu:15-52 -- NCHW pixel norm: x / sqrt(mean_c x^2 + eps), no gamma. */
+void oracle_pixel_norm(const uint16_t *x, uint16_t *out, int B, int C, int spatial, float eps);
+
 /* vae_kernels.cu:60-98 -- NCHW channel RMSNorm times gamma[c]; sequential sum over c. */
 void oracle_rms_norm_channel(const uint16_t *x, const uint16_t *gamma, uint16_t *out, int B,
                              int C, int spatial, float eps);

@@ -46,6 +46,7 @@ _SIGS = {
     "oracle_rope_standard": (P, P, P, I32, I32, I32, I32, I32),
     "oracle_embedding_lookup": (P, P, P, I32, I32, I32),
     "oracle_rms_norm_channel": (P, P, P, I32, I32, I32, F32),
+    "oracle_pixel_norm": (P, P, I32, I32, I32, F32),
     "oracle_timestep_sinusoid": (F32, I32, P),
     "oracle_cosmos_rope_tables": (I32, I32, I32, I32, P, P),
     "oracle_standard_rope_tables": (I32, I32, F32, P, P),
@@ -242,6 +243,12 @@ def embedding_lookup(table, ids, T, D, vocab):
 def rms_norm_channel(x, gamma, B, C, spatial, eps=1e-6):
     out = np.zeros((B, C, spatial), np.uint16)
     lib.oracle_rms_norm_channel(_p(x), _p(gamma), _p(out), B, C, spatial, eps)
+    return out
+
+
+def pixel_norm(x, B, C, spatial, eps=1e-6):
+    out = np.zeros((B, C, spatial), np.uint16)
+    lib.oracle_pixel_norm(_p(np.ascontiguousarray(x)), _p(out), B, C, spatial, eps)
     return out
 
 

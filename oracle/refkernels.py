@@ -59,6 +59,7 @@ LAUNCHERS = {
                             (P, P, P, I32, I32, F32, P)),  # :151-153
     "rms_norm_channel_bf16": ("_Z21rms_norm_channel_bf16PK13__nv_bfloat16S1_PS_iiifP11CUstream_st",
                               (P, P, P, I32, I32, I32, F32, P)),  # :177-180
+    "pixel_norm_bf16": ("_Z15pixel_norm_bf16PK13__nv_bfloat16PS_iiifP11CUstream_st", (P, P, I32, I32, I32, F32, P)),  # :156-158
     "channel_scale_shift_bf16": ("_Z24channel_scale_shift_bf16PK13__nv_bfloat16S1_S1_PS_iiiP11CUstream_st",
                                  (P, P, P, P, I32, I32, I32, P)),  # :189-192
     "head_transpose_bf16": ("_Z19head_transpose_bf16PK13__nv_bfloat16PS_iiiP11CUstream_st",

@@ -282,6 +282,14 @@ def main():
     put("conv_bias_residual_add", x=x, bias=b, residual=res, out=host(hr))
     put("conv_bias_rms_norm_channel_silu", x=x, bias=b, gamma=g, out=host(hn))
 
+    # ---- pixel norm (vae_kernels.cu:15-52); own seed
+    rng6 = np.random.default_rng(20265)
+    px = O.randn_bf16(rng6, (2, 24, 40))
+    po = torch.zeros((2, 24, 40), dtype=torch.int16, device="cuda")
+    R.pixel_norm_bf16(dev(px).data_ptr(), po.data_ptr(), 2, 24, 40, 1e-6, s)
+    torch.cuda.synchronize()
+    put("pixel_norm", x=px, out=host(po))
+
     # ---- attention glue (transpose.cu, gemma_ops.cu, softmax.cu); own seed
     rng5 = np.random.default_rng(20264)
     H, T, HD = 4, 6, 16

@@ -179,6 +179,13 @@ def test_conv_epilogue():
           "conv_bias_rms_norm_channel_silu")
 
 
+def test_pixel_norm():
+    """vae_kernels.cu:15-52 on the reference's output, within one ulp like the channel norm."""
+    z = load("pixel_norm")
+    B, C, sp = z["x"].shape
+    close(O.pixel_norm(z["x"], B, C, sp), z["out"], "pixel_norm")
+
+
 def test_attention_glue():
     """transpose.cu, gemma_ops.cu:99-127 and softmax.cu on the reference's outputs: the
     permutations and the mask exactly, the softmaxes within one ulp (libm expf)."""

@@ -527,6 +527,26 @@ def test_rms_norm_channel(anima, ref, rng, B, C, H, W):
         assert_one_ulp(host(out), O.rms_norm_channel(x, g, B, C, sp), "rms_norm_channel vs oracle")
 
 
+@pytest.mark.parametrize("B,C,H,W", [(1, 512, 32, 32), (1, 96, 10, 10), (2, 100, 5, 8), (1, 64, 160, 160),
+                                     (2, 128, 64, 64)])
+def test_pixel_norm(anima, ref, rng, B, C, H, W):
+    """vae_kernels.cu:15-52 through each channel-norm kernel: cluster (few tiles), tile (many),
+    per-pixel (spatial % 8 != 0)."""
+    sp = H * W
+    x = O.randn_bf16(rng, (B, C, sp))
+    dx = dev(x)
+    out, out_ref = empty_bf16((B, C, sp)), empty_bf16((B, C, sp))
+    anima.pixel_norm(dx, out, B, C, sp, 1e-6)
+    ref.pixel_norm_bf16(dx.data_ptr(), out_ref.data_ptr(), B, C, sp, 1e-6, stream_ptr())
+    xi = dev(x)
+    anima.pixel_norm(xi, xi, B, C, sp, 1e-6)  # in place
+    torch.cuda.synchronize()
+    assert_bit_exact(host(out), host(out_ref), "pixel_norm vs reference")
+    assert_bit_exact(host(xi), host(out_ref), "pixel_norm in place")
+    if x.size <= ORACLE_MAX_ELEMS:
+        assert_one_ulp(host(out), O.pixel_norm(x, B, C, sp), "pixel_norm vs oracle")
+
+
 @pytest.mark.parametrize("B,C,H,W", [(1, 512, 32, 32), (1, 96, 10, 10), (2, 100, 5, 8), (1, 256, 64, 64),
                                      (1, 64, 160, 160)])
 def test_rms_norm_channel_silu_matches_reference_chain(anima, ref, rng, B, C, H, W):

@@ -2,7 +2,7 @@
 its mangled name in libanima_b200.so's compatibility shim and in the reference's own build,
 on identical buffers, must write identical bytes. This is the path the reference's callers
 take after linking against the library, so it checks the shim's argument forwarding for all
-34 launchers, not only the C ABI behind it.
+35 launchers, not only the C ABI behind it.
 """
 import numpy as np
 import pytest
@@ -68,6 +68,7 @@ def _cases(rng):
     oc = np.zeros((Bc, C, sp), np.uint16)
     c["rms_norm_channel_bf16"] = (dict(x=xc, g=_bf(rng, C, 1.0, 0.02), o=oc),
                                   lambda p: (p["x"], p["g"], p["o"], Bc, C, sp, 1e-6), ["o"])
+    c["pixel_norm_bf16"] = (dict(x=xc, o=oc), lambda p: (p["x"], p["o"], Bc, C, sp, 1e-6), ["o"])
     c["channel_scale_shift_bf16"] = (dict(x=xc, sc=_bf(rng, C, 1.0, 0.3), sh=_bf(rng, C, std=0.5), o=oc),
                                      lambda p: (p["x"], p["sc"], p["sh"], p["o"], Bc, C, sp), ["o"])
     # latent I/O
