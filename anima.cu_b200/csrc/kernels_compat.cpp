@@ -136,6 +136,19 @@ void channel_scale_shift_bf16(const __nv_bfloat16 *x, const __nv_bfloat16 *scale
     record(anima_channel_scale_shift_bf16(in(x), in(scale), in(shift), io(out), B, C, spatial, stream));
 }
 
+void f32_to_bf16(const float *x, __nv_bfloat16 *out, int64_t N, cudaStream_t stream) {
+    record(anima_f32_to_bf16(x, io(out), N, stream));
+}
+
+void bf16_to_f32(const __nv_bfloat16 *x, float *out, int64_t N, cudaStream_t stream) {
+    record(anima_bf16_to_f32(in(x), out, N, stream));
+}
+
+void nearest_upsample_2x_bf16(const __nv_bfloat16 *src, __nv_bfloat16 *dst, int B, int C, int H, int W,
+                              cudaStream_t stream) {
+    record(anima_nearest_upsample_2x_bf16(in(src), io(dst), B, C, H, W, stream));
+}
+
 void causal_mask_bf16(__nv_bfloat16 *scores, int num_heads, int T, cudaStream_t stream) {
     record(anima_causal_mask_bf16(io(scores), num_heads, T, stream));
 }

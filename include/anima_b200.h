@@ -258,6 +258,18 @@ ANIMA_API int anima_channel_scale_shift_bf16(const anima_bf16 *x, const anima_bf
                                   const anima_bf16 *shift, anima_bf16 *out, int B, int C, int spatial,
                                   anima_stream_t stream);
 
+/* dtype conversions over floor(N/2) element pairs (an odd last element is left untouched,
+ * as the reference does): replace f32_to_bf16 and bf16_to_f32, kernels.h:96-97
+ * (elementwise.cu:311-352; transformer.cpp:543,622, pipeline.cpp:399-609). */
+ANIMA_API int anima_f32_to_bf16(const float *x, anima_bf16 *out, int64_t N, anima_stream_t stream);
+ANIMA_API int anima_bf16_to_f32(const anima_bf16 *x, float *out, int64_t N, anima_stream_t stream);
+
+/* [B, C, H, W] -> [B, C, 2H, 2W], each input element repeated 2x2. Replaces
+ * nearest_upsample_2x_bf16, kernels.h:172-174 (vae_kernels.cu:98-133; vae.cpp:339). in and
+ * out may not overlap. */
+ANIMA_API int anima_nearest_upsample_2x_bf16(const anima_bf16 *in, anima_bf16 *out, int B, int C, int H, int W,
+                                  anima_stream_t stream);
+
 /* Attention glue of the Qwen3 encoder and the LLM adapter (qwen3.cpp:164-226,
  * llm_adapter.cpp:169-222). Head layout changes: [T, H*HD] <-> [H, T, HD]
  * (head_transpose_bf16 / head_untranspose_bf16, transpose.cu:13-66) and

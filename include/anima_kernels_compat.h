@@ -80,6 +80,9 @@ void rms_norm_channel_bf16(const __nv_bfloat16 *x, const __nv_bfloat16 *gamma, _
 // kernels.h:156-158
 void pixel_norm_bf16(const __nv_bfloat16 *x, __nv_bfloat16 *out, int B, int C, int spatial, float eps = 1e-6f,
                      cudaStream_t stream = 0);
+// kernels.h:172-174
+void nearest_upsample_2x_bf16(const __nv_bfloat16 *in, __nv_bfloat16 *out, int B, int C, int H, int W,
+                              cudaStream_t stream = 0);
 // kernels.h:189-192
 void channel_scale_shift_bf16(const __nv_bfloat16 *x, const __nv_bfloat16 *scale, const __nv_bfloat16 *shift,
                               __nv_bfloat16 *out, int B, int C, int spatial, cudaStream_t stream = 0);
@@ -88,6 +91,9 @@ void patchify_3d_bf16(const __nv_bfloat16 *src, __nv_bfloat16 *dst, int B, int C
                       int pH, int pW, cudaStream_t stream = 0);
 void unpatchify_3d_bf16(const __nv_bfloat16 *src, __nv_bfloat16 *dst, int B, int C, int T, int H, int W, int pT,
                         int pH, int pW, cudaStream_t stream = 0);
+// kernels.h:96-97
+void f32_to_bf16(const float *x, __nv_bfloat16 *out, int64_t N, cudaStream_t stream = 0);
+void bf16_to_f32(const __nv_bfloat16 *x, float *out, int64_t N, cudaStream_t stream = 0);
 // kernels.h:104-117
 void causal_mask_bf16(__nv_bfloat16 *scores, int num_heads, int T, cudaStream_t stream = 0);
 void softmax_bf16(const __nv_bfloat16 *x, __nv_bfloat16 *out, int N, int D, cudaStream_t stream = 0);

@@ -246,6 +246,12 @@ def rms_norm_channel(x, gamma, B, C, spatial, eps=1e-6):
     return out
 
 
+def nearest_upsample_2x(x, B, C, H, W):
+    """vae_kernels.cu:98-133: out[b, c, h2, w2] = x[b, c, h2 // 2, w2 // 2]."""
+    x = np.asarray(x, np.uint16).reshape(B, C, H, W)
+    return np.repeat(np.repeat(x, 2, axis=2), 2, axis=3)
+
+
 def pixel_norm(x, B, C, spatial, eps=1e-6):
     out = np.zeros((B, C, spatial), np.uint16)
     lib.oracle_pixel_norm(_p(np.ascontiguousarray(x)), _p(out), B, C, spatial, eps)

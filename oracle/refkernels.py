@@ -35,6 +35,8 @@ LAUNCHERS = {
     "silu_bias_bf16": ("_Z14silu_bias_bf16PK13__nv_bfloat16S1_PS_liP11CUstream_st", (P, P, P, I64, I32, P)),  # :40-42
     "rope_cosmos_strided_bf16": ("_Z24rope_cosmos_strided_bf16P13__nv_bfloat16PKS_S2_iiiiP11CUstream_st",
                                  (P, P, P, I32, I32, I32, I32, P)),  # :51-53
+    "f32_to_bf16": ("_Z11f32_to_bf16PKfP13__nv_bfloat16lP11CUstream_st", (P, P, I64, P)),  # :96
+    "bf16_to_f32": ("_Z11bf16_to_f32PK13__nv_bfloat16PflP11CUstream_st", (P, P, I64, P)),  # :97
     "causal_mask_bf16": ("_Z16causal_mask_bf16P13__nv_bfloat16iiP11CUstream_st", (P, I32, I32, P)),  # :104-106
     "softmax_bf16": ("_Z12softmax_bf16PK13__nv_bfloat16PS_iiP11CUstream_st", (P, P, I32, I32, P)),  # :109-111
     "softmax_f32_to_bf16": ("_Z19softmax_f32_to_bf16PKfP13__nv_bfloat16iiP11CUstream_st",
@@ -59,6 +61,8 @@ LAUNCHERS = {
                             (P, P, P, I32, I32, F32, P)),  # :151-153
     "rms_norm_channel_bf16": ("_Z21rms_norm_channel_bf16PK13__nv_bfloat16S1_PS_iiifP11CUstream_st",
                               (P, P, P, I32, I32, I32, F32, P)),  # :177-180
+    "nearest_upsample_2x_bf16": ("_Z24nearest_upsample_2x_bf16PK13__nv_bfloat16PS_iiiiP11CUstream_st",
+                                 (P, P, I32, I32, I32, I32, P)),  # :172-174
     "pixel_norm_bf16": ("_Z15pixel_norm_bf16PK13__nv_bfloat16PS_iiifP11CUstream_st", (P, P, I32, I32, I32, F32, P)),  # :156-158
     "channel_scale_shift_bf16": ("_Z24channel_scale_shift_bf16PK13__nv_bfloat16S1_S1_PS_iiiP11CUstream_st",
                                  (P, P, P, P, I32, I32, I32, P)),  # :189-192

@@ -92,9 +92,8 @@ CALLERS = ("transformer", "qwen3", "llm_adapter", "vae")
 def test_reference_callers_resolve_every_launcher(archives):
     """The reference's own callers (transformer.cpp, qwen3.cpp, llm_adapter.cpp, vae.cpp,
     compiled unchanged into oracle/_ref/callers by `make -C oracle callers`): every
-    kernels.h launcher they leave undefined must be defined by libanima_b200.so (the
-    replaced launchers) or by the localized reference archive (the launchers this library
-    does not replace), and each replaced one must bind to the library."""
+    kernels.h launcher they leave undefined must be one this library replaces, defined by
+    libanima_b200.so and hidden in the localized reference archive, so each binds to it."""
     import anima_b200
 
     objs = {c: os.path.join(ROOT, "oracle", "_ref", "callers", c + ".o") for c in CALLERS}
@@ -114,7 +113,9 @@ def test_reference_callers_resolve_every_launcher(archives):
         assert launchers, f"{name}.cpp calls no reference launcher?"
         unresolved = [s for s in launchers if s not in lib and s not in g_local]
         assert not unresolved, f"{name}.cpp: unresolved launchers {unresolved}"
-        for s in launchers & replaced:
+        kept = sorted(launchers - replaced)
+        assert not kept, f"{name}.cpp: launchers left to the reference: {kept}"
+        for s in launchers:
             assert s in lib and s not in g_local, f"{name}.cpp: {s} would not bind to the B200 library"
-        bound += len(launchers & replaced)
-    assert bound >= 30  # the four callers reach 35 replaced launchers (some shared)
+        bound += len(launchers)
+    assert bound == 38  # 13 + 11 + 8 + 6 launcher references across the four callers

@@ -848,3 +848,47 @@ def test_row_norms_random_shapes(anima, ref, rng, N, D):
     torch.cuda.synchronize()
     for name, got, want in pairs:
         assert_bit_exact(host(got), host(want), f"{name} [{N}, {D}] vs reference")
+
+
+# ---------------------------------------------------------------- conversions, VAE upsample
+@pytest.mark.parametrize("N", [1 << 20, 1001, 2, 1])
+def test_f32_bf16_conversions(anima, ref, rng, N):
+    """elementwise.cu:311-352 over floor(N/2) pairs (an odd last element stays as it was), with
+    zeros, subnormals, Inf and NaN among the inputs."""
+    x = (rng.standard_normal(N) * 100).astype(np.float32)
+    special = np.array([0.0, -0.0, 1e-40, -1e-45, np.inf, -np.inf, np.nan, 3.0e38], np.float32)
+    x[: min(N, special.size)] = special[: min(N, special.size)]
+    dx = torch.from_numpy(x).cuda()
+    b, b_ref = torch.full((N,), 7, dtype=torch.int16, device="cuda"), torch.full((N,), 7, dtype=torch.int16, device="cuda")
+    anima.f32_to_bf16(dx, b, N)
+    ref.f32_to_bf16(dx.data_ptr(), b_ref.data_ptr(), N, stream_ptr())
+    f, f_ref = torch.full((N,), 5.0, device="cuda"), torch.full((N,), 5.0, device="cuda")
+    anima.bf16_to_f32(b_ref, f, N)
+    ref.bf16_to_f32(b_ref.data_ptr(), f_ref.data_ptr(), N, stream_ptr())
+    torch.cuda.synchronize()
+    assert host(b).tobytes() == host(b_ref).tobytes(), "f32_to_bf16 vs reference"
+    assert f.cpu().numpy().tobytes() == f_ref.cpu().numpy().tobytes(), "bf16_to_f32 vs reference"
+
+
+def test_f32_to_bf16_unaligned(anima, rng):
+    """A 4-byte-offset fp32 input (scalar path) against the oracle; the reference's float2 loads
+    would be misaligned there, so it is not run."""
+    N = 4098
+    x = (rng.standard_normal(N + 1) * 10).astype(np.float32)
+    dx = torch.from_numpy(x).cuda()
+    out = torch.zeros(N, dtype=torch.int16, device="cuda")
+    anima.f32_to_bf16(dx[1:], out, N)
+    torch.cuda.synchronize()
+    assert_bit_exact(host(out), O.f32_to_bf16(x[1:]), "f32_to_bf16 (unaligned) vs oracle")
+
+
+@pytest.mark.parametrize("B,C,H,W", [(1, 512, 64, 64), (2, 3, 5, 7), (1, 4, 5, 8), (1, 1, 1, 1)])
+def test_nearest_upsample_2x(anima, ref, rng, B, C, H, W):
+    x = O.randn_bf16(rng, (B, C, H, W))
+    dx = dev(x)
+    out, out_ref = empty_bf16((B, C, 2 * H, 2 * W)), empty_bf16((B, C, 2 * H, 2 * W))
+    anima.nearest_upsample_2x(dx, out, B, C, H, W)
+    ref.nearest_upsample_2x_bf16(dx.data_ptr(), out_ref.data_ptr(), B, C, H, W, stream_ptr())
+    torch.cuda.synchronize()
+    assert_bit_exact(host(out), host(out_ref), "nearest_upsample_2x vs reference")
+    assert_bit_exact(host(out), O.nearest_upsample_2x(x, B, C, H, W), "nearest_upsample_2x vs oracle")

@@ -2,7 +2,7 @@
 its mangled name in libanima_b200.so's compatibility shim and in the reference's own build,
 on identical buffers, must write identical bytes. This is the path the reference's callers
 take after linking against the library, so it checks the shim's argument forwarding for all
-35 launchers, not only the C ABI behind it.
+38 launchers, not only the C ABI behind it.
 """
 import numpy as np
 import pytest
@@ -92,6 +92,12 @@ def _cases(rng):
     c["cfg_er_sde_full_step_bf16"] = (dict(x=smp, a=pos, b=neg, den=z, od=od, dd=z, odd=odd, r=rnd),
                                       lambda p: (p["x"], p["a"], p["b"], p["den"], p["od"], p["dd"], p["odd"], p["r"])
                                       + coeffs + (ns,), ["x", "den", "dd"])
+    # conversions and the VAE upsample
+    c["f32_to_bf16"] = (dict(a=rng.standard_normal(1001).astype(np.float32), o=np.zeros(1001, np.uint16)),
+                        lambda p: (p["a"], p["o"], 1001), ["o"])
+    c["bf16_to_f32"] = (dict(a=_bf(rng, 1001), o=np.zeros(1001, np.float32)), lambda p: (p["a"], p["o"], 1001), ["o"])
+    c["nearest_upsample_2x_bf16"] = (dict(a=_bf(rng, (2, 3, 5, 8)), o=np.zeros((2, 3, 10, 16), np.uint16)),
+                                     lambda p: (p["a"], p["o"], 2, 3, 5, 8), ["o"])
     # attention glue
     Ha, Ta, HDa = 4, 6, 16
     src = _bf(rng, (Ta, Ha * HDa))
