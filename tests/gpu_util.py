@@ -47,3 +47,26 @@ def assert_bit_exact(got, want, what=""):
 def assert_one_ulp(got, want, what=""):
     ex, mx, w1 = compare(got, want)
     assert w1 == 1.0, f"{what}: {1 - w1:.3e} of elements beyond 1 bf16 ulp (exact {ex:.6f}, max {mx} ulp)"
+
+
+def assert_bit_exact_or_reference_race(got, ref_out, oracle_fn, what=""):
+    """Bit-exact against a kernel of the reference's layer_norm.cu, allowing for that file's
+    one race. Its CTA reduction helper (layer_norm.cu:7-19) returns shared[0] with no barrier
+    after the read, and its kernels call it twice in a row (the sum, then the sum of squares):
+    warp 0 can write its next partial into shared[0] before a slower warp has read the first
+    total, and that warp then normalises its elements with a wrong mean (rarely; gross errors
+    on a few dozen elements). A mismatch is accepted only where it is that: on few elements,
+    with our value within one ulp of the race-free CPU restatement (oracle_fn()) and the
+    reference's value not."""
+    got = np.asarray(got).reshape(-1)
+    ref_out = np.asarray(ref_out).reshape(-1)
+    diff = np.nonzero(got != ref_out)[0]
+    if diff.size == 0:
+        return
+    assert diff.size <= max(512, got.size // 1000), f"{what}: {diff.size} elements differ from the reference"
+    want = np.asarray(oracle_fn()).reshape(-1)
+    ours_ok = O.within_one_ulp(got[diff], want[diff])
+    theirs_ok = O.within_one_ulp(ref_out[diff], want[diff])
+    assert ours_ok.all() and not theirs_ok.any(), (
+        f"{what}: {diff.size} elements differ from the reference, and not as its reduction race would make them "
+        f"({int(ours_ok.sum())} of ours and {int(theirs_ok.sum())} of the reference's follow the CPU restatement)")

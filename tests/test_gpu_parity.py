@@ -13,7 +13,8 @@ import pytest
 import torch
 
 import oracle as O
-from gpu_util import assert_bit_exact, assert_one_ulp, dev, empty_bf16, host, stream_ptr
+from gpu_util import (assert_bit_exact, assert_bit_exact_or_reference_race, assert_one_ulp, dev, empty_bf16, host,
+                      stream_ptr)
 
 pytestmark = pytest.mark.gpu
 
@@ -63,8 +64,9 @@ def test_layer_norm(anima, ref, rng, N, D):
     xi = dev(x)
     anima.layer_norm(xi, xi, N, D, 1e-6)  # in place (transformer.cpp:563)
     torch.cuda.synchronize()
-    assert_bit_exact(host(out), host(out_ref), "layer_norm vs reference")
-    assert_bit_exact(host(xi), host(out_ref), "layer_norm in place")
+    lazy = lambda: O.layer_norm(x, N, D)  # noqa: E731
+    assert_bit_exact_or_reference_race(host(out), host(out_ref), lazy, "layer_norm vs reference")
+    assert_bit_exact_or_reference_race(host(xi), host(out_ref), lazy, "layer_norm in place")
     if N * D <= ORACLE_MAX_ELEMS:
         assert_one_ulp(host(out), O.layer_norm(x, N, D), "layer_norm vs oracle")
 
@@ -79,7 +81,8 @@ def test_adaln_layernorm(anima, ref, rng, N, D):
     ref.adaln_layernorm_bf16(dx.data_ptr(), dsc.data_ptr(), dsh.data_ptr(), out_ref.data_ptr(), N, D, 1e-6,
                              stream_ptr())
     torch.cuda.synchronize()
-    assert_bit_exact(host(out), host(out_ref), "adaln_layernorm vs reference")
+    assert_bit_exact_or_reference_race(host(out), host(out_ref), lambda: O.adaln_layernorm(x, sc, sh, N, D),
+                                       "adaln_layernorm vs reference")
     if N * D <= ORACLE_MAX_ELEMS:
         assert_one_ulp(host(out), O.adaln_layernorm(x, sc, sh, N, D), "adaln_layernorm vs oracle")
 
@@ -96,7 +99,8 @@ def test_residual_gate_adaln(anima, ref, rng, N, D):
                                  out_ref.data_ptr(), N, D, 1e-6, stream_ptr())
     torch.cuda.synchronize()
     assert_bit_exact(host(h), host(h_ref), "residual_gate_adaln hidden vs reference")
-    assert_bit_exact(host(out), host(out_ref), "residual_gate_adaln normed vs reference")
+    assert_bit_exact_or_reference_race(host(out), host(out_ref), lambda: O.residual_gate_adaln(x, y, g, sc, sh, N, D)[1],
+                                       "residual_gate_adaln normed vs reference")
     if N * D <= ORACLE_MAX_ELEMS:
         oh, on = O.residual_gate_adaln(x, y, g, sc, sh, N, D)
         assert_bit_exact(host(h), oh, "residual_gate_adaln hidden vs oracle")
@@ -136,7 +140,8 @@ def test_adaln_layernorm_temb_matches_reference_chain(anima, ref, rng, N, D, off
     ref.adaln_layernorm_bf16(dx.data_ptr(), m.data_ptr() + 2 * D, m.data_ptr(), out_ref.data_ptr(), N, D, 1e-6,
                              stream_ptr())
     torch.cuda.synchronize()
-    assert_bit_exact(host(out), host(out_ref), "adaln_layernorm_temb normed vs reference chain")
+    assert_bit_exact_or_reference_race(host(out), host(out_ref), lambda: O.adaln_layernorm_temb(x, mod, temb, N, D)[0],
+                                       "adaln_layernorm_temb normed vs reference chain")
     assert_bit_exact(host(gate), host(m)[2 * D:], "adaln_layernorm_temb gate vs reference chain")
     assert np.array_equal(host(dm), mod_before), "mod must be left unchanged"
     if N * D <= ORACLE_MAX_ELEMS:
@@ -163,7 +168,9 @@ def test_residual_gate_adaln_temb_matches_reference_chain(anima, ref, rng, N, D,
     gate_ref.copy_(m[2 * D:])
     torch.cuda.synchronize()
     assert_bit_exact(host(h), host(h_ref), "residual_gate_adaln_temb hidden vs reference chain")
-    assert_bit_exact(host(normed), host(normed_ref), "residual_gate_adaln_temb normed vs reference chain")
+    assert_bit_exact_or_reference_race(
+        host(normed), host(normed_ref), lambda: O.residual_gate_adaln_temb(x, y, g_prev, mod, temb, N, D)[1],
+        "residual_gate_adaln_temb normed vs reference chain")
     assert_bit_exact(host(gate), host(gate_ref), "residual_gate_adaln_temb gate vs reference chain")
     if N * D <= ORACLE_MAX_ELEMS:
         oh, on, og = O.residual_gate_adaln_temb(x, y, g_prev, mod, temb, N, D)
@@ -222,9 +229,10 @@ def test_row_norm_unaligned_subbuffer(anima, ref, rng):
                                      1e-6, stream_ptr())
         torch.cuda.synchronize()
         got = host(out)[e:e + N * D]
-        if off % 4 == 0:
-            assert_bit_exact(got, host(out_ref)[e:e + N * D], f"adaln at +{off} B vs reference")
         want = O.adaln_layernorm(np.ascontiguousarray(base[e:e + N * D]), scv, shv, N, D)
+        if off % 4 == 0:
+            assert_bit_exact_or_reference_race(got, host(out_ref)[e:e + N * D], lambda: want,
+                                               f"adaln at +{off} B vs reference")
         assert_one_ulp(got, want, f"adaln at +{off} B vs oracle")
 
 
@@ -573,7 +581,8 @@ def test_layer_norm_modulate_matches_reference_chain(anima, ref, rng, N, D):
     ref.layer_norm_bf16(r.data_ptr(), r.data_ptr(), N, D, 1e-6, stream_ptr())
     ref.scale_shift_bcast_bf16(r.data_ptr(), dsc.data_ptr(), dsh.data_ptr(), r.data_ptr(), N, D, stream_ptr())
     torch.cuda.synchronize()
-    assert_bit_exact(host(out), host(r), "layer_norm_modulate vs layer_norm + scale_shift_bcast")
+    assert_bit_exact_or_reference_race(host(out), host(r), lambda: O.layer_norm_modulate(x, sc, sh, N, D),
+                                       "layer_norm_modulate vs layer_norm + scale_shift_bcast")
 
 
 # ---------------------------------------------------------------- timestep embedding
@@ -830,24 +839,28 @@ def test_row_norms_random_shapes(anima, ref, rng, N, D):
     o, r_ = empty_bf16((N, D)), empty_bf16((N, D))
     anima.rms_norm(dx, dw, o, N, D, 1e-6)
     ref.rms_norm_bf16(dx.data_ptr(), dw.data_ptr(), r_.data_ptr(), N, D, 1e-6, S)
-    pairs.append(("rms_norm", o, r_))
+    pairs.append(("rms_norm", o, r_, None))
     o, r_ = empty_bf16((N, D)), empty_bf16((N, D))
     anima.layer_norm(dx, o, N, D, 1e-6)
     ref.layer_norm_bf16(dx.data_ptr(), r_.data_ptr(), N, D, 1e-6, S)
-    pairs.append(("layer_norm", o, r_))
+    pairs.append(("layer_norm", o, r_, lambda: O.layer_norm(x, N, D)))
     o, r_ = empty_bf16((N, D)), empty_bf16((N, D))
     anima.adaln_layernorm(dx, dsc, dsh, o, N, D, 1e-6)
     ref.adaln_layernorm_bf16(dx.data_ptr(), dsc.data_ptr(), dsh.data_ptr(), r_.data_ptr(), N, D, 1e-6, S)
-    pairs.append(("adaln_layernorm", o, r_))
+    pairs.append(("adaln_layernorm", o, r_, lambda: O.adaln_layernorm(x, sc, sh, N, D)))
     h, hr = dev(x), dev(x)
     o, r_ = empty_bf16((N, D)), empty_bf16((N, D))
     anima.residual_gate_adaln(h, dy, dg, dsc, dsh, o, N, D, 1e-6)
     ref.residual_gate_adaln_bf16(hr.data_ptr(), dy.data_ptr(), dg.data_ptr(), dsc.data_ptr(), dsh.data_ptr(),
                                  r_.data_ptr(), N, D, 1e-6, S)
-    pairs += [("residual_gate_adaln hidden", h, hr), ("residual_gate_adaln normed", o, r_)]
+    pairs += [("residual_gate_adaln hidden", h, hr, None),
+              ("residual_gate_adaln normed", o, r_, lambda: O.residual_gate_adaln(x, y, g, sc, sh, N, D)[1])]
     torch.cuda.synchronize()
-    for name, got, want in pairs:
-        assert_bit_exact(host(got), host(want), f"{name} [{N}, {D}] vs reference")
+    for name, got, want, oracle_fn in pairs:  # layer_norm.cu's kernels: see assert_bit_exact_or_reference_race
+        if oracle_fn is None:
+            assert_bit_exact(host(got), host(want), f"{name} [{N}, {D}] vs reference")
+        else:
+            assert_bit_exact_or_reference_race(host(got), host(want), oracle_fn, f"{name} [{N}, {D}] vs reference")
 
 
 # ---------------------------------------------------------------- conversions, VAE upsample

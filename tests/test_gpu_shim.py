@@ -133,6 +133,11 @@ def _run(lib, name, bufs, build, outs):
     return {k: dev[k].cpu().numpy().tobytes() for k in outs}
 
 
+# layer_norm.cu's kernels can race in the reference's own reduction helper (see
+# gpu_util.assert_bit_exact_or_reference_race); a mismatch there gets one fresh reference run.
+RACY = {"layer_norm_bf16", "adaln_layernorm_bf16", "residual_gate_adaln_bf16"}
+
+
 def test_every_launcher_through_the_shim_matches_the_reference(anima, ref, rng):
     import anima_b200
     import refkernels
@@ -145,6 +150,8 @@ def test_every_launcher_through_the_shim_matches_the_reference(anima, ref, rng):
     for name, (bufs, build, outs) in cases.items():
         got = _run(shim, name, bufs, build, outs)
         want = _run(ref, name, bufs, build, outs)
+        if name in RACY and any(got[k] != want[k] for k in outs):
+            want = _run(ref, name, bufs, build, outs)
         if anima_b200.lib.anima_compat_last_error() != 0:
             bad.append(f"{name}: the shim recorded an error")
         bad += [f"{name}: {k} differs" for k in outs if got[k] != want[k]]
