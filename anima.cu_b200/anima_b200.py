@@ -42,6 +42,7 @@ SIGNATURES = {
     "anima_unpatchify_3d_bf16": (P, P) + (I32,) * 8 + (P,),
     "anima_channel_scale_shift_bf16": (P, P, P, P, I32, I32, I32, P),
     "anima_pixel_norm_bf16": (P, P, I32, I32, I32, F32, P),
+    "anima_scale_bf16": (P, P, F32, I64, P),
     "anima_f32_to_bf16": (P, P, I64, P),
     "anima_bf16_to_f32": (P, P, I64, P),
     "anima_nearest_upsample_2x_bf16": (P, P, I32, I32, I32, I32, P),
@@ -325,6 +326,10 @@ def conv_bias_residual_add(x, bias, residual, out, B, C, spatial, stream=None):
 def conv_bias_rms_norm_channel_silu(x, bias, gamma, out, B, C, spatial, eps=1e-6, stream=None):
     call("anima_conv_bias_rms_norm_channel_silu_bf16", _ptr(x), _ptr(bias), _ptr(gamma), _ptr(out), B, C, spatial,
          eps, _stream(stream))
+
+
+def scale(x, out, s, N, stream=None):
+    call("anima_scale_bf16", _ptr(x), _ptr(out), s, N, _stream(stream))
 
 
 def f32_to_bf16(x, out, N, stream=None):

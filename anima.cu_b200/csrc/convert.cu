@@ -1,11 +1,13 @@
-// convert.cu -- dtype conversions and the VAE's nearest 2x upsample (sm_100a):
+// convert.cu -- dtype conversions, scaling by a scalar and the VAE's nearest 2x upsample (sm_100a):
 //
 //   f32_to_bf16   out = bf16(x) (RNE) over floor(N/2) pairs     elementwise.cu:311-331
 //   bf16_to_f32   out = float(x) over floor(N/2) pairs           elementwise.cu:333-352
+//   scale_bf16    out = bf16(x * s) over floor(N/2) pairs        elementwise.cu:97-122
 //   nearest_upsample_2x_bf16  [B, C, H, W] -> [B, C, 2H, 2W]     vae_kernels.cu:98-133
 //
-// All three are exact by construction. The conversions leave an odd last element untouched,
-// as the reference's pair loops do. Each thread moves 8 elements per step with 16-byte
+// The conversions and the upsample are exact by construction; the scaling is one fp32 multiply
+// and a rounding, as the reference's. The pair loops leave an odd last element untouched, as
+// the reference's do. Each thread moves 8 elements per step with 16-byte
 // accesses on the bf16 side (and 2 x 16 bytes on the fp32 side) when the pointers allow,
 // over one resident wave; the upsample writes each output row's 16-byte chunks from 8-byte
 // loads of the input row, one launch for all batch items (the reference launches per item).
@@ -64,6 +66,28 @@ int convert(const void *src, void *dst, int64_t N, cudaStream_t stream) {
     return launch_status();
 }
 
+// ------------------------------------------------------------------ scale
+__global__ void __launch_bounds__(kCvBlock) scale_kernel(const anima_bf16 *x, anima_bf16 *out, float s, int64_t n,
+                                                        bool vec) {
+    pdl_wait();
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (vec) {
+        for (; i < n / 8; i += stride) {
+            float f[8];
+            unpack8(ld_stream(x + 8 * i), f);
+#pragma unroll
+            for (int e = 0; e < 8; ++e) f[e] = f[e] * s;  // elementwise.cu:109-110
+            st_vec(out + 8 * i, pack8(f));
+        }
+        i = n / 8 * 8 + ((int64_t)blockIdx.x * blockDim.x + threadIdx.x);
+    }
+    for (; i < n; i += stride)
+        reinterpret_cast<__nv_bfloat16 *>(out)[i] =
+            __float2bfloat16_rn(__bfloat162float(reinterpret_cast<const __nv_bfloat16 *>(x)[i]) * s);
+    pdl_launch();
+}
+
 // ------------------------------------------------------------- nearest upsample
 struct UpArgs {
     const anima_bf16 *in;
@@ -115,6 +139,22 @@ extern "C" int anima_f32_to_bf16(const float *x, anima_bf16 *out, int64_t N, ani
 
 extern "C" int anima_bf16_to_f32(const anima_bf16 *x, float *out, int64_t N, anima_stream_t stream) {
     return convert<false>(x, out, N, stream);
+}
+
+extern "C" int anima_scale_bf16(const anima_bf16 *x, anima_bf16 *out, float scale, int64_t N,
+                                anima_stream_t stream) {
+    if (N < 0) return ANIMA_ERR_BAD_SHAPE;
+    const int64_t n = N / 2 * 2;
+    if (n == 0) return ANIMA_OK;
+    if (!x || !out) return ANIMA_ERR_NULL_POINTER;
+    if (!aligned_to(x, 2) || !aligned_to(out, 2)) return ANIMA_ERR_MISALIGNED;
+    if (partial_overlap(x, n * 2, out, n * 2)) return ANIMA_ERR_OVERLAP;
+    const bool vec = aligned16(x) && aligned16(out);
+    int err = ANIMA_OK;
+    const unsigned grid = wave_grid((const void *)scale_kernel, kCvBlock, 0, vec ? n / 8 + 1 : n, &err);
+    if (err) return err;
+    launch(scale_kernel, grid, kCvBlock, 0, stream, x, out, scale, n, vec);
+    return launch_status();
 }
 
 extern "C" int anima_nearest_upsample_2x_bf16(const anima_bf16 *in, anima_bf16 *out, int B, int C, int H, int W,

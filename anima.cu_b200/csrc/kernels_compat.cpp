@@ -136,6 +136,10 @@ void channel_scale_shift_bf16(const __nv_bfloat16 *x, const __nv_bfloat16 *scale
     record(anima_channel_scale_shift_bf16(in(x), in(scale), in(shift), io(out), B, C, spatial, stream));
 }
 
+void scale_bf16(const __nv_bfloat16 *x, __nv_bfloat16 *out, float scale, int64_t N, cudaStream_t stream) {
+    record(anima_scale_bf16(in(x), io(out), scale, N, stream));
+}
+
 void f32_to_bf16(const float *x, __nv_bfloat16 *out, int64_t N, cudaStream_t stream) {
     record(anima_f32_to_bf16(x, io(out), N, stream));
 }

@@ -264,6 +264,10 @@ ANIMA_API int anima_channel_scale_shift_bf16(const anima_bf16 *x, const anima_bf
 ANIMA_API int anima_f32_to_bf16(const float *x, anima_bf16 *out, int64_t N, anima_stream_t stream);
 ANIMA_API int anima_bf16_to_f32(const anima_bf16 *x, float *out, int64_t N, anima_stream_t stream);
 
+/* out = bf16(x * scale) over floor(N/2) element pairs. Replaces scale_bf16, kernels.h:75-76
+ * (elementwise.cu:97-122; the initial noise, pipeline.cpp:519). out may alias x. */
+ANIMA_API int anima_scale_bf16(const anima_bf16 *x, anima_bf16 *out, float scale, int64_t N, anima_stream_t stream);
+
 /* [B, C, H, W] -> [B, C, 2H, 2W], each input element repeated 2x2. Replaces
  * nearest_upsample_2x_bf16, kernels.h:172-174 (vae_kernels.cu:98-133; vae.cpp:339). in and
  * out may not overlap. */

@@ -91,6 +91,8 @@ void patchify_3d_bf16(const __nv_bfloat16 *src, __nv_bfloat16 *dst, int B, int C
                       int pH, int pW, cudaStream_t stream = 0);
 void unpatchify_3d_bf16(const __nv_bfloat16 *src, __nv_bfloat16 *dst, int B, int C, int T, int H, int W, int pT,
                         int pH, int pW, cudaStream_t stream = 0);
+// kernels.h:75-76
+void scale_bf16(const __nv_bfloat16 *x, __nv_bfloat16 *out, float scale, int64_t N, cudaStream_t stream = 0);
 // kernels.h:96-97
 void f32_to_bf16(const float *x, __nv_bfloat16 *out, int64_t N, cudaStream_t stream = 0);
 void bf16_to_f32(const __nv_bfloat16 *x, float *out, int64_t N, cudaStream_t stream = 0);

@@ -35,6 +35,7 @@ LAUNCHERS = {
     "silu_bias_bf16": ("_Z14silu_bias_bf16PK13__nv_bfloat16S1_PS_liP11CUstream_st", (P, P, P, I64, I32, P)),  # :40-42
     "rope_cosmos_strided_bf16": ("_Z24rope_cosmos_strided_bf16P13__nv_bfloat16PKS_S2_iiiiP11CUstream_st",
                                  (P, P, P, I32, I32, I32, I32, P)),  # :51-53
+    "scale_bf16": ("_Z10scale_bf16PK13__nv_bfloat16PS_flP11CUstream_st", (P, P, F32, I64, P)),  # :75-76
     "f32_to_bf16": ("_Z11f32_to_bf16PKfP13__nv_bfloat16lP11CUstream_st", (P, P, I64, P)),  # :96
     "bf16_to_f32": ("_Z11bf16_to_f32PK13__nv_bfloat16PflP11CUstream_st", (P, P, I64, P)),  # :97
     "causal_mask_bf16": ("_Z16causal_mask_bf16P13__nv_bfloat16iiP11CUstream_st", (P, I32, I32, P)),  # :104-106

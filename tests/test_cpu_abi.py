@@ -113,6 +113,7 @@ X, Y, Z = 0x10000, 0x20000, 0x30000  # never dereferenced: every call below fail
     (("anima_rms_norm_channel_silu_bf16", X, None, Z, 1, 4, 16, 1e-6, None), -1),
     (("anima_pixel_norm_bf16", X, X + 2, 1, 4, 16, 1e-6, None), -5),
     (("anima_f32_to_bf16", X + 2, Y, 16, None), -3),
+    (("anima_scale_bf16", X, X + 2, 0.5, 16, None), -5),
     (("anima_bf16_to_f32", X, X + 8, 16, None), -5),
     (("anima_nearest_upsample_2x_bf16", X, X + 32, 1, 2, 4, 4, None), -5),
     (("anima_nearest_upsample_2x_bf16", X, None, 1, 2, 4, 4, None), -1),

@@ -905,3 +905,18 @@ def test_nearest_upsample_2x(anima, ref, rng, B, C, H, W):
     torch.cuda.synchronize()
     assert_bit_exact(host(out), host(out_ref), "nearest_upsample_2x vs reference")
     assert_bit_exact(host(out), O.nearest_upsample_2x(x, B, C, H, W), "nearest_upsample_2x vs oracle")
+
+
+@pytest.mark.parametrize("N", [1 << 20, 4097, 9, 2])
+def test_scale(anima, ref, rng, N):
+    """elementwise.cu:97-122 (pipeline.cpp:519: the initial noise times sigma_0)."""
+    x = O.randn_bf16(rng, N, std=2.0)
+    dx = dev(x)
+    out, out_ref = dev(np.full(N, 3, np.uint16)), dev(np.full(N, 3, np.uint16))
+    anima.scale(dx, out, 14.614642, N)
+    ref.scale_bf16(dx.data_ptr(), out_ref.data_ptr(), 14.614642, N, stream_ptr())
+    xi = dev(x)
+    anima.scale(xi, xi, 14.614642, N)  # in place, as pipeline.cpp:519
+    torch.cuda.synchronize()
+    assert_bit_exact(host(out), host(out_ref), "scale vs reference")
+    assert_bit_exact(host(xi)[: N // 2 * 2], host(out_ref)[: N // 2 * 2], "scale in place")

@@ -2,7 +2,7 @@
 its mangled name in libanima_b200.so's compatibility shim and in the reference's own build,
 on identical buffers, must write identical bytes. This is the path the reference's callers
 take after linking against the library, so it checks the shim's argument forwarding for all
-38 launchers, not only the C ABI behind it.
+39 launchers, not only the C ABI behind it.
 """
 import numpy as np
 import pytest
@@ -93,6 +93,8 @@ def _cases(rng):
                                       lambda p: (p["x"], p["a"], p["b"], p["den"], p["od"], p["dd"], p["odd"], p["r"])
                                       + coeffs + (ns,), ["x", "den", "dd"])
     # conversions and the VAE upsample
+    c["scale_bf16"] = (dict(a=_bf(rng, 1001), o=np.zeros(1001, np.uint16)), lambda p: (p["a"], p["o"], 0.7311, 1001),
+                       ["o"])
     c["f32_to_bf16"] = (dict(a=rng.standard_normal(1001).astype(np.float32), o=np.zeros(1001, np.uint16)),
                         lambda p: (p["a"], p["o"], 1001), ["o"])
     c["bf16_to_f32"] = (dict(a=_bf(rng, 1001), o=np.zeros(1001, np.float32)), lambda p: (p["a"], p["o"], 1001), ["o"])
