@@ -614,7 +614,7 @@ def headline_kernels(ops, device, peak, reps=192):
     return res
 
 
-def other_ops(ops, device, peak, reps=96):
+def other_ops(ops, device, peak, reps=96, only=None, steps=3, warmup=3):
     """The in-scope ops outside the cfg2 chain, at BASELINE's other configs, each through
     the arm's own entry points: cfg3 (Qwen3-0.6B layer ops at seq 512), cfg4 (the VAE
     decoder's channel RMSNorm + SiLU at its four shapes), and the final LayerNorm +
@@ -623,7 +623,11 @@ def other_ops(ops, device, peak, reps=96):
     times the fused call and the reference arm the reference's call chain it replaces;
     the anima arm also times its own drop-in chain. Each case cycles enough buffer sets
     to exceed L2 where its tensors are large (small cfg3 tensors stay L2-resident, as in
-    the model) and is timed as a CUDA graph replay. Returns name -> us per call, GB/s."""
+    the model) and is timed as a CUDA graph replay. Returns name -> us per call, GB/s.
+
+    only: the name of one case (profiling aid, for ncu captures): allocate only what that
+    case needs where the tensors are large (the cfg4 shapes), run `warmup` then `steps`
+    eager calls of it, print their timing and return None."""
     import torch
 
     import tables
@@ -725,6 +729,8 @@ def other_ops(ops, device, peak, reps=96):
 
     # ---- cfg4: VAE channel RMSNorm + SiLU, NCHW
     for (C, Hs) in ((512, 128), (512, 256), (256, 512), (128, 1024)):
+        if only is not None and not (only.startswith("cfg4_") and only.endswith(f"_{C}x{Hs}x{Hs}")):
+            continue
         sp = Hs * Hs
         sets = max(2, min(8, -(-512 * 2**20 // (4 * C * sp))))
         xs = [bf((C, sp)) for _ in range(sets)]
@@ -780,6 +786,25 @@ def other_ops(ops, device, peak, reps=96):
                       lambda i: (ops.call("rms_norm", P(xl[i]), P(wh), P(xl[i]), R * H, HD, eps, S()),
                                  ops.call("rope_cosmos_strided", P(xl[i]), P(ct_d), P(st_d), 2, 4096, H, HD,
                                           S()))))
+
+    if only is not None:
+        match = [c for c in cases if c[0] == only]
+        if not match:
+            raise SystemExit(f"--only {only}: no such case (cases: {', '.join(c[0] for c in cases)})")
+        name, nbytes, launches, sets, fn = match[0]
+        for i in range(warmup):
+            fn(i % sets)
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for i in range(steps):
+            fn(i % sets)
+        b.record()
+        torch.cuda.synchronize()
+        us = a.elapsed_time(b) * 1e3 / steps
+        print(json.dumps({"op": name, "impl": ops.kind, "calls": steps, "launches_per_call": launches,
+                          "us_per_call": round(us, 2), "gbs": round(nbytes / (us * 1e-6) / 1e9, 1)}))
+        return None
 
     res = {}
     for name, nbytes, launches, sets, fn in cases:
@@ -912,7 +937,8 @@ def main():
                     help="cfg2 (default): 8192 rows per GPU, weak scaling. cfg5: BASELINE's throughput sweep, "
                          "8 image pairs at 1536x1536 (18432 rows each) split 8/N pairs per GPU, strong scaling")
     ap.add_argument("--only", default=None,
-                    help="profiling aid: run only this op type of the chain (eager), print its timing, exit")
+                    help="profiling aid: run only this op type of the chain, or this case of the other "
+                         "configs (e.g. cfg4_rms_norm_channel_silu_512x256x256), eagerly; print its timing, exit")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -950,7 +976,9 @@ def main():
     total_bytes, per_block, lpb = chain_bytes()
 
     if args.only is not None:
-        return profile_one_op(args, chain, lpb[args.only] * CFG["blocks"], per_block[args.only] / lpb[args.only])
+        if args.only in lpb:
+            return profile_one_op(args, chain, lpb[args.only] * CFG["blocks"], per_block[args.only] / lpb[args.only])
+        return other_ops(ops, device, peak, only=args.only, steps=args.steps, warmup=args.warmup)
 
     # warm-up (also initialises every kernel and the library's device caches)
     for _ in range(args.warmup):
