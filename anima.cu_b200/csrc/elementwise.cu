@@ -23,6 +23,7 @@
 #include "activation.cuh"
 
 #include <atomic>
+#include <mutex>
 #include <type_traits>
 
 namespace anima {
@@ -322,6 +323,7 @@ __global__ void __launch_bounds__(kTabBlock, 1) table_act_kernel(EwArgs a, const
 constexpr int kTabDevices = 64;
 std::atomic<uintptr_t> g_table_addr[kTabDevices];  // device address of g_act_table (set before a ready bit)
 std::atomic<unsigned> g_table_ready[kTabDevices];  // bit t set = table t filled on that device
+std::mutex g_table_fill_mu[kTabDevices];           // one first fill per device and table at a time
 
 // The device's table `t`, filled if it is not yet and the stream is not being captured
 // (filling launches on `stream` and waits for it, once per device). Null: use the
@@ -342,6 +344,12 @@ const uint16_t *act_table(int t, cudaStream_t stream, int *err) {
         cudaGetLastError();
         return nullptr;
     }
+    // Threads making a first call on this device at the same time: one fills, the others
+    // wait here and then find the ready bit set (no second fill, no fill over a table that
+    // another thread's kernel is already reading).
+    std::lock_guard<std::mutex> lock(g_table_fill_mu[dev]);
+    if (g_table_ready[dev].load(std::memory_order_acquire) & (1u << t))
+        return reinterpret_cast<const uint16_t *>(g_table_addr[dev].load(std::memory_order_acquire)) + t * kTabEntries;
     void *p = nullptr;
     if (cudaGetSymbolAddress(&p, g_act_table) != cudaSuccess) {
         cudaGetLastError();
@@ -356,8 +364,6 @@ const uint16_t *act_table(int t, cudaStream_t stream, int *err) {
         *err = (int)e;
         return nullptr;
     }
-    // Concurrent first calls fill the same bits; a reader only starts after its own caller
-    // saw this bit, i.e. after a completed fill.
     g_table_ready[dev].fetch_or(1u << t, std::memory_order_acq_rel);
     return table;
 }

@@ -76,6 +76,8 @@ extern "C" int anima_embedding_lookup_bf16(const anima_bf16 *table, const int32_
         return ANIMA_ERR_MISALIGNED;
     if (partial_overlap(out, (int64_t)T * D * 2, ids, (int64_t)T * 4) || (const void *)out == ids)
         return ANIMA_ERR_OVERLAP;
+    // Rows written while other warps still read the table would race.
+    if (vocab > 0 && overlaps(out, (int64_t)T * D * 2, table, (int64_t)vocab * D * 2)) return ANIMA_ERR_OVERLAP;
     GatherArgs a{table, ids, out, T, D, vocab, bad_id_count};
     const int64_t per_block = kGatherBlock / 32;
     const unsigned grid = (unsigned)((T + per_block - 1) / per_block);

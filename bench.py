@@ -44,6 +44,8 @@ METRIC = "fused-kernel HBM GB/s (% of B200 peak) at 4096×2048 bf16; DiT-step ms
 CFG = dict(batch=2, pe=(1, 64, 64), hidden=2048, heads=16, head_dim=128, mlp=8192, text=512, blocks=28,
            ts_dim=2048, eps=1e-6)
 NSETS = 4  # rotating activation buffer sets: ~1.4 GB touched per step, >> 126 MB L2
+# 512x512 image -> 64x64 latent -> 32x32 patches = 1024 tokens, batch 1
+CFG1 = dict(batch=1, pe=(1, 32, 32))
 
 
 def chain_bytes(c=CFG):
@@ -104,7 +106,7 @@ class AnimaOps:
     def residual_gate_bcast(self, x, y, g, o, M, D, s):
         self._ck("bcast", self.L.anima_residual_gate_bcast_bf16(x, y, g, o, M, D, s))
 
-    def timestep(self, t, w, sin_out, normed, dim, eps, s, host_buf=None):
+    def timestep(self, t, w, sin_out, normed, dim, eps, s, host_buf=None, sin_tensor=None):
         self._ck("timestep", self.L.anima_timestep_embedding_bf16(t, w, sin_out, normed, dim, eps, s))
 
     def call(self, name, *args):
@@ -178,10 +180,10 @@ class RefOps:
     def residual_gate_bcast(self, x, y, g, o, M, D, s):
         self.R.residual_gate_bcast_bf16(x, y, g, o, M, D, s)
 
-    def timestep(self, t, w, sin_out, normed, dim, eps, s, host_buf=None):
+    def timestep(self, t, w, sin_out, normed, dim, eps, s, host_buf=None, sin_tensor=None):
         # transformer.cpp:182-200: host sinusoid, bf16 upload, then rms_norm_bf16 on one row
         host_buf.numpy()[:] = self.O.timestep_sinusoid(t, dim).view(np.int16)
-        self._sin_tensor.copy_(host_buf, non_blocking=False)  # synchronous, like the reference's cudaMemcpy
+        sin_tensor.copy_(host_buf, non_blocking=False)  # synchronous, like the reference's cudaMemcpy
         self.R.rms_norm_bf16(sin_out, w, normed, 1, dim, eps, s)
 
     def call(self, name, *args):
@@ -222,13 +224,13 @@ class RefOps:
 
 # ---------------------------------------------------------------- device state
 class Chain:
-    def __init__(self, ops, device, seed=1234):
+    def __init__(self, ops, device, seed=1234, cfg=None):
         import torch
 
         import tables
 
         self.ops, self.dev = ops, device
-        c = CFG
+        c = self.cfg = dict(cfg if cfg is not None else CFG)
         self.B, self.S = c["batch"], c["pe"][0] * c["pe"][1] * c["pe"][2]
         self.R, self.D, self.H, self.HD = self.B * self.S, c["hidden"], c["heads"], c["head_dim"]
         self.M, self.T, self.NB, self.eps = c["mlp"], c["text"], c["blocks"], c["eps"]
@@ -257,17 +259,17 @@ class Chain:
         self.ts_sin = torch.empty((c["ts_dim"],), dtype=torch.bfloat16, device=device)
         self.ts_out = torch.empty((c["ts_dim"],), dtype=torch.bfloat16, device=device)
         self.ts_host = torch.empty((c["ts_dim"],), dtype=torch.int16).pin_memory()
-        if isinstance(ops, RefOps):
-            ops._sin_tensor = self.ts_sin.view(torch.int16)
         self.ts_rng = np.random.default_rng(seed)
         self.launches_per_block = 14
         self.gates = [torch.empty((D,), dtype=torch.bfloat16, device=device) for _ in range(2)]
         self.launches_fused = 7 * self.NB + (self.NB - 1) + 2  # + the first adaLN and the last residual gate
 
     def timestep(self, stream):
+        import torch
+
         t = float(np.float32(self.ts_rng.uniform()) * np.float32(1000.0))
-        self.ops.timestep(t, self.ts_w.data_ptr(), self.ts_sin.data_ptr(), self.ts_out.data_ptr(), CFG["ts_dim"],
-                          self.eps, stream, host_buf=self.ts_host)
+        self.ops.timestep(t, self.ts_w.data_ptr(), self.ts_sin.data_ptr(), self.ts_out.data_ptr(), self.cfg["ts_dim"],
+                          self.eps, stream, host_buf=self.ts_host, sin_tensor=self.ts_sin.view(torch.int16))
 
     def block(self, i, stream, only=None):
         """One DiT block's chain; `only` restricts it to one op type (for per-op timing)."""
@@ -477,7 +479,7 @@ def e2e_pipelined(chain, graph, steps, h_in, m_in, h_out):
     import torch
 
     R, D = chain.R, chain.D
-    last = chain.sets[(CFG["blocks"] - 1) % NSETS]["hidden"]
+    last = chain.sets[(chain.NB - 1) % NSETS]["hidden"]
     compute, copy = torch.cuda.Stream(), torch.cuda.Stream()
     in_stage = [torch.empty((R, D), dtype=torch.bfloat16, device=chain.dev) for _ in range(2)]
     out_stage = [torch.empty((R, D), dtype=torch.bfloat16, device=chain.dev) for _ in range(2)]
@@ -560,34 +562,55 @@ def per_op_times(chain, ops, reps):
     return out
 
 
-def headline_kernels(ops, device, peak, reps=192):
-    """Each row kernel at the headline [4096, 2048] (GELU at [4096, 8192]), cycling 8
-    buffer sets (> 4x L2) so every launch reads from HBM. Returns op -> GB/s, frac, us."""
+def headline_kernels(ops, device, peak, reps=384):
+    """Every in-scope row / elementwise kernel at the headline shape, 4096 tokens x 2048
+    (GELU and SiLU at the FFN width, [4096, 8192]; QK RMSNorm on the same tensor as
+    [4096*16, 128] head rows; Cosmos RoPE on [4096, 16*128] with the (1, 64, 64) grid's
+    tables), each launch cycling 8 buffer sets (> 2x L2) so every launch reads from HBM.
+    Each case is a CUDA graph of 48 back-to-back launches of that kernel alone, replayed;
+    us = graph time / launches. Returns name -> {us, gbs, frac}."""
     import torch
 
-    N, D, M = 4096, 2048, 8192
+    import tables
+
+    N, D, M, H, HD = 4096, 2048, 8192, 16, 128
     sets = 8
     x = [torch.randn((N, D), device=device).to(torch.bfloat16) for _ in range(sets)]
     y = [torch.randn((N, D), device=device).to(torch.bfloat16) for _ in range(sets)]
     o = [torch.empty((N, D), dtype=torch.bfloat16, device=device) for _ in range(sets)]
     f = [torch.randn((N, M), device=device).to(torch.bfloat16) for _ in range(4)]
     v = (torch.randn((3 * D,), device=device) * 0.1).to(torch.bfloat16)
+    w = (torch.randn((D,), device=device) * 0.02 + 1.0).to(torch.bfloat16)
     sc, sh, g = v.data_ptr(), v.data_ptr() + 2 * D, v.data_ptr() + 4 * D
+    ct, st = tables.cosmos_rope_tables(1, 64, 64, HD)
+    ct_d = torch.from_numpy(ct.view(np.int16)).to(device)
+    st_d = torch.from_numpy(st.view(np.int16)).to(device)
     eps = 1e-6
+    P = lambda t: t.data_ptr()  # noqa: E731
 
     def S():
         return torch.cuda.current_stream().cuda_stream  # the capture stream inside capture()
 
+    # (§8 row, algorithmic bytes per launch, launch(i)); bytes as in SURVEY §8(a)
     cases = {
-        "adaln_layernorm": (4 * N * D + 4 * D, lambda i: ops.adaln_layernorm(x[i].data_ptr(), sc, sh, o[i].data_ptr(), N, D, eps, S())),
-        "residual_gate_adaln": (8 * N * D + 6 * D, lambda i: ops.residual_gate_adaln(
-            x[i].data_ptr(), y[i].data_ptr(), g, sc, sh, o[i].data_ptr(), N, D, eps, S())),
-        "residual_gate_bcast": (6 * N * D + 2 * D, lambda i: ops.residual_gate_bcast(
-            x[i].data_ptr(), y[i].data_ptr(), g, x[i].data_ptr(), N, D, S())),
-        "rms_norm_qk128": (4 * N * D + 256, lambda i: ops.rms_norm(x[i].data_ptr(), v.data_ptr(), o[i].data_ptr(),
-                                                                   N * 16, 128, eps, S())),
-        "gelu_tanh_4096x8192": (4 * N * M, lambda i: ops.gelu_tanh(f[i % 2].data_ptr(), f[2 + i % 2].data_ptr(), N * M,
-                                                                   S())),
+        "a1_adaln_layernorm": (4 * N * D + 4 * D,
+                               lambda i: ops.adaln_layernorm(P(x[i]), sc, sh, P(o[i]), N, D, eps, S())),
+        "a2_residual_gate_adaln": (8 * N * D + 6 * D, lambda i: ops.residual_gate_adaln(
+            P(x[i]), P(y[i]), g, sc, sh, P(o[i]), N, D, eps, S())),
+        "a3_residual_gate_bcast": (6 * N * D + 2 * D, lambda i: ops.residual_gate_bcast(
+            P(x[i]), P(y[i]), g, P(x[i]), N, D, S())),
+        "a4_layer_norm": (4 * N * D, lambda i: ops.call("layer_norm", P(x[i]), P(o[i]), N, D, eps, S())),
+        "a5_scale_shift_bcast": (4 * N * D + 4 * D, lambda i: ops.call(
+            "scale_shift_bcast", P(x[i]), sc, sh, P(o[i]), N, D, S())),
+        "a6_rms_norm_2048": (4 * N * D + 2 * D, lambda i: ops.rms_norm(P(x[i]), P(w), P(o[i]), N, D, eps, S())),
+        "a6_rms_norm_qk128": (4 * N * D + 2 * HD, lambda i: ops.rms_norm(P(x[i]), P(w), P(o[i]), N * H, HD, eps,
+                                                                         S())),
+        "a7_rope_cosmos_strided": (4 * N * D + 2 * N * (HD // 2) * 2, lambda i: ops.rope_cosmos_strided(
+            P(x[i]), P(ct_d), P(st_d), 1, N, H, HD, S())),
+        "a8_gelu_tanh_4096x8192": (4 * N * M, lambda i: ops.gelu_tanh(P(f[i % 2]), P(f[2 + i % 2]), N * M, S())),
+        "a9_silu_4096x8192": (4 * N * M, lambda i: ops.call("silu", P(f[i % 2]), P(f[2 + i % 2]), N * M, S())),
+        "a10_add": (6 * N * D, lambda i: ops.add(P(x[i]), P(y[i]), P(o[i]), N * D, S())),
+        "a10_mul": (6 * N * D, lambda i: ops.call("mul", P(x[i]), P(y[i]), P(o[i]), N * D, S())),
     }
     res = {}
     per_graph = 6 * sets  # launches per captured graph, cycling the buffer sets
@@ -608,7 +631,7 @@ def headline_kernels(ops, device, peak, reps=192):
         del graph
         us = a.elapsed_time(b) * 1e3 / (n_rep * per_graph)
         gbs = nbytes / (us * 1e-6) / 1e9
-        res[name] = {"gbs": round(gbs, 1), "frac": round(gbs / peak, 3), "us": round(us, 2), "bytes": nbytes}
+        res[name] = {"us": round(us, 2), "gbs": round(gbs, 1), "frac": round(gbs / peak, 3)}
     del x, y, o, f
     torch.cuda.empty_cache()
     return res
@@ -832,74 +855,86 @@ def other_ops(ops, device, peak, reps=96, only=None, steps=3, warmup=3):
 
 
 def cpu_baseline_sample(blocks=2, rows=8192, threads=1):
-    """The CPU restatement (oracle/) over `blocks` blocks of the same chain at cfg2 shapes,
-    on `threads` host threads: every op's rows (GELU's elements) are split into `threads`
-    contiguous ranges, one oracle call per range (ctypes releases the GIL, so the C code
-    runs in parallel). Returns (GB/s, description)."""
-    from concurrent.futures import ThreadPoolExecutor
-
+    """The plain C host loop of the chain's ops (oracle/hostloop.c: fp32 math on bf16
+    storage, gcc -O3 -march=native -fopenmp, built on this host) over `blocks` blocks of the
+    cfg2 chain at full size on `threads` OpenMP threads. Returns (GB/s, description)."""
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import hostloop
     import oracle as O
 
+    L = hostloop.load()
+    L.hostloop_set_threads(threads)
     rng = np.random.default_rng(5)
     c = CFG
     B, S = c["batch"], c["pe"][0] * c["pe"][1] * c["pe"][2]
     R = rows
     D, H, HD, M, T = c["hidden"], c["heads"], c["head_dim"], c["mlp"], c["text"]
-    hidden, sub = O.randn_bf16(rng, (R, D)), O.randn_bf16(rng, (R, D))
+    hidden, sub, normed = O.randn_bf16(rng, (R, D)), O.randn_bf16(rng, (R, D)), np.empty((R, D), np.uint16)
     q, k, qc = (O.randn_bf16(rng, (R * H, HD)) for _ in range(3))
     kc = O.randn_bf16(rng, (B * T * H, HD))
-    ff = O.randn_bf16(rng, R * M)
-    mod = O.randn_bf16(rng, (3, 3 * D), std=0.1)
+    ff, ff_out = O.randn_bf16(rng, R * M), np.empty(R * M, np.uint16)
+    mod_raw = O.randn_bf16(rng, (3, 3 * D), std=0.1)
+    mod = np.empty_like(mod_raw)
     temb = O.randn_bf16(rng, 3 * D, std=0.1)
     w = O.randn_bf16(rng, HD, mean=1.0, std=0.02)
     ct, st = O.cosmos_rope_tables(*c["pe"], HD)
-    pool = ThreadPoolExecutor(threads)
-
-    def split(n, align=1):
-        step = -(-n // (threads * align)) * align
-        return [(i, min(n, i + step)) for i in range(0, n, step)]
-
-    def rows_op(fn, n, *arrays):
-        """fn(lo, hi) -> result rows [lo, hi); results concatenated in order."""
-        parts = list(pool.map(lambda r: fn(*r), split(n)))
-        return parts[0] if len(parts) == 1 else np.concatenate(parts)
-
-    def rope(x):  # rows of [R*H, HD] grouped by token; table row = token % S
-        def part(lo, hi):
-            t0, t1 = lo // H, hi // H
-            out = []
-            while t0 < t1:
-                s0 = t0 % S
-                n = min(t1 - t0, S - s0)
-                out.append(O.rope_cosmos_strided(x[t0 * H:(t0 + n) * H], ct[s0:s0 + n], st[s0:s0 + n], 1, n, H, HD))
-                t0 += n
-            return np.concatenate(out) if len(out) > 1 else out[0]
-        parts = list(pool.map(lambda r: part(*r), split(x.shape[0], H)))
-        return parts[0] if len(parts) == 1 else np.concatenate(parts)
-
+    A = lambda a: a.ctypes.data  # noqa: E731
+    eps = np.float32(1e-6)
     t0 = time.perf_counter()
     for _ in range(blocks):
-        m = [O.add(mod[j], temb) for j in range(3)]  # each [shift | scale | gate]
-        shift, scale, gate = ([mj[:D], mj[D:2 * D], mj[2 * D:]] for mj in m)
-        rows_op(lambda lo, hi: O.adaln_layernorm(hidden[lo:hi], scale[0], shift[0], hi - lo, D), R)
-        q = rows_op(lambda lo, hi: O.rms_norm(q[lo:hi], w, hi - lo, HD), R * H)
-        k = rows_op(lambda lo, hi: O.rms_norm(k[lo:hi], w, hi - lo, HD), R * H)
-        q, k = rope(q), rope(k)
-        hidden = rows_op(lambda lo, hi: O.residual_gate_adaln(hidden[lo:hi], sub[lo:hi], gate[0], scale[1],
-                                                              shift[1], hi - lo, D)[0], R)
-        qc = rows_op(lambda lo, hi: O.rms_norm(qc[lo:hi], w, hi - lo, HD), R * H)
-        kc = rows_op(lambda lo, hi: O.rms_norm(kc[lo:hi], w, hi - lo, HD), B * T * H)
-        hidden = rows_op(lambda lo, hi: O.residual_gate_adaln(hidden[lo:hi], sub[lo:hi], gate[1], scale[2],
-                                                              shift[2], hi - lo, D)[0], R)
-        ff = rows_op(lambda lo, hi: O.gelu_tanh(ff[lo:hi]), R * M)
-        hidden = rows_op(lambda lo, hi: O.residual_gate_bcast(hidden[lo:hi], sub[lo:hi], gate[2], hi - lo, D), R)
+        for j in range(3):
+            L.hostloop_add(A(mod_raw[j]), A(temb), A(mod[j]), 3 * D)
+        sh = [A(mod[j]) for j in range(3)]
+        sc = [A(mod[j]) + 2 * D for j in range(3)]
+        gt = [A(mod[j]) + 4 * D for j in range(3)]
+        L.hostloop_adaln_layernorm(A(hidden), sc[0], sh[0], A(normed), R, D, eps)
+        L.hostloop_rms_norm(A(q), A(w), A(q), R * H, HD, eps)
+        L.hostloop_rms_norm(A(k), A(w), A(k), R * H, HD, eps)
+        L.hostloop_rope_cosmos(A(q), A(ct), A(st), B, S, H, HD)
+        L.hostloop_rope_cosmos(A(k), A(ct), A(st), B, S, H, HD)
+        L.hostloop_residual_gate_adaln(A(hidden), A(sub), gt[0], sc[1], sh[1], A(normed), R, D, eps)
+        L.hostloop_rms_norm(A(qc), A(w), A(qc), R * H, HD, eps)
+        L.hostloop_rms_norm(A(kc), A(w), A(kc), B * T * H, HD, eps)
+        L.hostloop_residual_gate_adaln(A(hidden), A(sub), gt[1], sc[2], sh[2], A(normed), R, D, eps)
+        L.hostloop_gelu_tanh(A(ff), A(ff_out), R * M)
+        L.hostloop_residual_gate_bcast(A(hidden), A(sub), gt[2], A(hidden), R, D)
     dt = time.perf_counter() - t0
-    pool.shutdown()
     _, per_block, _ = chain_bytes()
     nbytes = blocks * sum(per_block.values()) * R / (B * S)
-    return nbytes / dt / 1e9, (f"{blocks} of the 28 blocks of the cfg2 chain at {R} rows on {threads} "
+    return nbytes / dt / 1e9, (f"{blocks} of the 28 blocks of the cfg2 chain at {R} rows on {threads} OpenMP "
                                f"thread{'s' if threads > 1 else ''} ({dt:.1f} s)")
+
+
+def cfg1_step(ops, device, steps, peak):
+    """BASELINE config 1 (512x512 image, 1024 tokens, batch 1): the same 28-block chain at 1024
+    rows, timed as CUDA graph replays and as eager launches. The per-block figure is the
+    single-block chain BASELINE names. Its activations (~58 MB per buffer set) sit near the L2
+    size, so the 4 rotating sets keep most reads in HBM; launches dominate at this size."""
+    import torch
+
+    c = dict(CFG, **CFG1)
+    chain = Chain(ops, device, cfg=c)
+    total, per_block, lpb = chain_bytes(c)
+    s = torch.cuda.current_stream()
+    for _ in range(3):
+        chain.timestep(s.cuda_stream)
+        chain.blocks(s.cuda_stream)
+    torch.cuda.synchronize()
+    graph = capture(lambda st: chain.blocks(st))
+    graph.replay()
+    torch.cuda.synchronize()
+    k = max(3, min(steps, 50))
+    g_ms = time_steps(chain, k, s, graph) / k
+    del graph
+    e_ms = time_steps(chain, max(3, min(steps, 20)), s, None) / max(3, min(steps, 20))
+    gbs = total / (g_ms * 1e-3) / 1e9
+    out = {"workload": "cfg1: 512x512 image -> 1024 tokens, batch 1, 28-block DiT elementwise chain",
+           "rows": chain.R, "bytes_per_step": total, "launches_per_step": c["blocks"] * chain.launches_per_block + 1,
+           "ms_per_step": round(g_ms, 4), "ms_per_block": round(g_ms / c["blocks"], 4), "gbs": round(gbs, 1),
+           "frac": round(gbs / peak, 3), "eager_ms_per_step": round(e_ms, 4)}
+    del chain
+    torch.cuda.empty_cache()
+    return out
 
 
 def profile_one_op(args, chain, launches_per_step, bytes_per_launch):
@@ -933,8 +968,9 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-headline", action="store_true")
     ap.add_argument("--no-other-ops", action="store_true", help="skip the cfg3/cfg4/fused-entry measurements")
-    ap.add_argument("--workload", choices=["cfg2", "cfg5"], default="cfg2",
-                    help="cfg2 (default): 8192 rows per GPU, weak scaling. cfg5: BASELINE's throughput sweep, "
+    ap.add_argument("--workload", choices=["cfg1", "cfg2", "cfg5"], default="cfg2",
+                    help="cfg2 (default): 8192 rows per GPU, weak scaling. cfg1: BASELINE's 512x512 image, "
+                         "1024 tokens, batch 1 (weak scaling). cfg5: BASELINE's throughput sweep, "
                          "8 image pairs at 1536x1536 (18432 rows each) split 8/N pairs per GPU, strong scaling")
     ap.add_argument("--only", default=None,
                     help="profiling aid: run only this op type of the chain, or this case of the other "
@@ -945,15 +981,14 @@ def main():
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
-    if args.impl == "reference" and rank != 0:
-        return  # the reference is single-GPU code: rank 0 alone runs it
-
     import torch
 
     torch.cuda.set_device(local_rank)
     device = torch.device("cuda", local_rank)
     dist = None
-    if world > 1 and args.impl == "anima":
+    # Both arms run one replica per rank: the reference's launchers are stateless and act on the
+    # calling rank's own device, so at N GPUs its line reports the same N-replica aggregate.
+    if world > 1:
         import datetime
 
         import torch.distributed as dist
@@ -968,6 +1003,9 @@ def main():
             raise SystemExit("cfg5 shares 8 image pairs over the GPUs: use 1, 2, 4 or 8")
         CFG.update(pe=(1, 96, 96), batch=2 * (8 // n_gpus))
         args.no_headline = args.no_other_ops = args.no_cpu_baseline = True
+    elif args.workload == "cfg1":
+        CFG.update(CFG1)
+        args.no_headline = args.no_other_ops = True
 
     ops = AnimaOps() if args.impl == "anima" else RefOps()
     chain = Chain(ops, device)
@@ -1014,8 +1052,24 @@ def main():
     ms_per_step = ms / args.steps
     value = aggregate_gbs(n_gpus, total_bytes, args.steps, ms)
 
+    # the same steps launched eagerly (no graph): the reference launches this way on stream 0
+    # (transformer.cpp:476); here both arms go through the same Python launcher loop
+    eager = None
+    if graph is not None:
+        e_steps = max(3, min(args.steps, 20))
+        eager_ms = reduce_max(time_steps(chain, e_steps, stream, None), dist, device) / e_steps
+        eager = {"ms_per_step": round(eager_ms, 4),
+                 "value": round(aggregate_gbs(n_gpus, total_bytes, 1, eager_ms), 1), "unit": "GB/s",
+                 "steps": e_steps,
+                 "note": "eager launches from the Python harness, one ctypes call per launch (host-bound)"}
+
+    # BASELINE config 1 beside the default workload: the 28-block chain at 1024 tokens, batch 1
+    cfg1 = None
+    if args.workload == "cfg2" and rank == 0 and not args.no_other_ops:
+        cfg1 = cfg1_step(ops, device, args.steps, peak)
+
     # per-op device times (graph replay of each op type alone) -> roofline
-    ops_t = per_op_times(chain, {k: v * CFG["blocks"] for k, v in lpb.items()}, max(3, min(args.steps, 20)))
+    ops_t = per_op_times(chain, {k: v * CFG["blocks"] for k, v in lpb.items()}, 50)
     kernels = {}
     for name, mean_ms in ops_t.items():
         per_launch = per_block[name] / lpb[name]
@@ -1082,7 +1136,7 @@ def main():
     if not args.no_cpu_baseline and rank == 0:
         n_cores = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else (os.cpu_count() or 1)
         v1, sample1 = cpu_baseline_sample(blocks=2, threads=1)
-        vn, samplen = cpu_baseline_sample(blocks=4 if n_cores >= 8 else 2, threads=n_cores)
+        vn, samplen = cpu_baseline_sample(blocks=8 if n_cores >= 8 else 2, threads=n_cores)
         cpu_model = None
         try:
             with open("/proc/cpuinfo") as f:
@@ -1092,8 +1146,8 @@ def main():
         cpu = {"value": round(vn, 3), "unit": "GB/s", "cores": n_cores, "kind": "port", "sample": samplen,
                "cpu_model": cpu_model, "host_threads": os.cpu_count(),
                "single_thread": {"value": round(v1, 3), "cores": 1, "sample": sample1},
-               "note": "CPU restatement of the reference kernels (oracle/oracle.c, -O2), rows split over the "
-                       "host's threads; the reference itself has no CPU implementation of these ops"}
+               "note": "plain C host loop of the chain's ops (oracle/hostloop.c, gcc -O3 -march=native -fopenmp, "
+                       "built on this host); the reference itself has no CPU implementation of these ops"}
 
     used_graph = graph is not None
     del graph  # release the captured graph before the process group goes away
@@ -1132,10 +1186,13 @@ def main():
         "chain_frac_of_peak": round(value / n_gpus / peak, 3),
         "cpu_baseline": cpu,
         "clocks": clk,
-        "kernels": kernels,
-        "headline_4096x2048": headline,
-        "other_ops": other,
+        # compact per-case figures ({us, frac}); the full record is in the DESIGN tables
+        "other_ops": ({k: {"us": v["us"], "frac": v["frac"]} for k, v in other.items()} if other else None),
+        "kernels": {k: {"us": v["us"], "frac": v["frac"], "share": v["share"], "launches": v["launches_per_step"]}
+                    for k, v in kernels.items()},
         "fused_step": fused,
+        "eager_step": eager,
+        "cfg1": cfg1,
     }
     if args.impl == "reference":
         line["impl"] = "reference"
@@ -1150,8 +1207,11 @@ def main():
                                 "sample": f"{args.steps} full {args.workload} steps: the reference's kernels.h launchers driven "
                                           "from one host thread, kernels on the B200",
                                 "note": "the reference implements this path only as CUDA kernels"}
+    # last, so that it survives in any tail of the output: every in-scope kernel at the
+    # headline [4096, 2048] shape, the metric BASELINE.json names
+    line["headline_4096x2048"] = headline
     if rank == 0:
-        print(json.dumps(line), flush=True)
+        print(json.dumps(line, separators=(",", ":")), flush=True)
     if dist is not None:
         dist.barrier()
         dist.destroy_process_group()

@@ -160,7 +160,9 @@ ANIMA_API int anima_rope_standard_bf16(anima_bf16 *x, const float *cos_table, co
 
 /* out[t,:] = table[ids[t],:], bit-exact. ids outside [0, vocab) produce a zero row and,
  * when bad_id_count is non-NULL, increment *bad_id_count (a device int the caller
- * zeroes). vocab <= 0 disables the check (the reference's behaviour).
+ * zeroes). vocab <= 0 disables the check (the reference's behaviour). `out` must not
+ * overlap `table` or `ids` (rejected with ANIMA_ERR_OVERLAP; with vocab <= 0 the table's
+ * extent is unknown and the caller guarantees it).
  * Replaces embedding_lookup_bf16, kernels.h:142-144 (gemma_ops.cu:47-53), which takes
  * no vocabulary size. */
 ANIMA_API int anima_embedding_lookup_bf16(const anima_bf16 *table, const int32_t *ids, anima_bf16 *out,
@@ -371,7 +373,9 @@ ANIMA_API int anima_residual_gate_adaln_temb_bf16(anima_bf16 *hidden, const anim
  * (cos of t*f_i in [0, dim/2), sin in [dim/2, dim), f_i = exp(-ln(1e4) i / (dim/2)))
  * as bf16 to sinusoid_out[dim], and, when normed_out is non-NULL, its RMSNorm times
  * norm_weight (nullable) to normed_out[dim]. The reference builds the sinusoid on the
- * host and uploads it (transformer.cpp:182-197) before rms_norm_bf16 (:200). dim even. */
+ * host and uploads it (transformer.cpp:182-197) before rms_norm_bf16 (:200). dim even.
+ * Not bit-exact with that host loop: exp/cos/sin are correctly rounded here, glibc's fp32
+ * functions are not everywhere, so rare elements differ by one bf16 ulp. */
 ANIMA_API int anima_timestep_embedding_bf16(float timestep, const anima_bf16 *norm_weight,
                                   anima_bf16 *sinusoid_out, anima_bf16 *normed_out, int dim,
                                   float eps, anima_stream_t stream);

@@ -109,6 +109,7 @@ X, Y, Z = 0x10000, 0x20000, 0x30000  # never dereferenced: every call below fail
     (("anima_rope_standard_bf16", X, Y, Z, 4, 0, 8, None), -2),
     (("anima_embedding_lookup_bf16", X, Y + 1, Z, 4, 8, 10, None, None), -3),
     (("anima_embedding_lookup_bf16", None, Y, Z, 4, 8, 10, None, None), -1),
+    (("anima_embedding_lookup_bf16", X, Y, X + 0x40, 4, 8, 10, None, None), -5),  # out inside the table
     (("anima_rms_norm_channel_bf16", X, Y, Z, 1, 0, 16, 1e-6, None), -2),
     (("anima_rms_norm_channel_silu_bf16", X, None, Z, 1, 4, 16, 1e-6, None), -1),
     (("anima_pixel_norm_bf16", X, X + 2, 1, 4, 16, 1e-6, None), -5),

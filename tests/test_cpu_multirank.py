@@ -1,6 +1,6 @@
 """Multi-rank plumbing of bench.py on the CPU: two gloo ranks (127.0.0.1) exercise the
 max-over-ranks reduction and the whole-job aggregate that the GPU run uses over NCCL,
-and the reference arm's rule that only rank 0 runs (the reference is single-GPU code)."""
+and the rule that both arms run one replica per rank."""
 import os
 import socket
 import sys
@@ -51,15 +51,38 @@ def test_two_rank_max_and_aggregate():
         assert v == pytest.approx(2 * 10**9 * 10 / 0.150 / 1e9)
 
 
-def test_reference_arm_runs_on_rank_zero_only(monkeypatch):
+def test_reference_arm_runs_on_every_rank(monkeypatch):
+    """Both arms run one replica per rank (the reference's launchers act on the calling
+    rank's own device), so rank 1 of the reference arm goes on to set up its GPU instead of
+    returning early; here that set-up is intercepted before any CUDA call."""
     sys.path.insert(0, ROOT)
+    import torch
+
     import bench
+
+    class Reached(Exception):
+        pass
+
+    def fake_set_device(i):
+        raise Reached(i)
 
     monkeypatch.setenv("RANK", "1")
     monkeypatch.setenv("WORLD_SIZE", "2")
     monkeypatch.setenv("LOCAL_RANK", "1")
     monkeypatch.setattr(sys, "argv", ["bench.py", "--impl", "reference", "--gpus", "2"])
-    assert bench.main() is None  # returns before touching a GPU
+    monkeypatch.setattr(torch.cuda, "set_device", fake_set_device)
+    with pytest.raises(Reached) as e:
+        bench.main()
+    assert e.value.args == (1,)
+
+
+def test_cfg1_byte_count_per_block():
+    """BASELINE config 1 (512x512 image, 1024 tokens, batch 1): 134.5 MB per block."""
+    sys.path.insert(0, ROOT)
+    import bench
+
+    total, _, _ = bench.chain_bytes(dict(bench.CFG, **bench.CFG1))
+    assert abs(total / 28 / 1e6 - 134.5) < 1.0
 
 
 def test_chain_byte_count_per_block():
