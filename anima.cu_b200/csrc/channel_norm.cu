@@ -8,17 +8,19 @@
 // gives each pixel a thread that walks the channels with 2-byte strided loads, twice
 // (once for the sum, once for the output), launched once per batch item.
 //
-// Here one 256-thread CTA owns a tile of 64 consecutive pixels x all C channels of one
-// image. The tile is staged into shared memory with 16-byte cp.async copies (each channel
-// contributes one contiguous 128-byte segment), then 64 threads walk the channels of their
-// pixel in order -- the reference's own summation order, so the statistics and outputs
-// match it bit for bit -- with the next 8 channels' shared-memory loads issued before the
-// current 8 fmas, and finally all threads scale the tile out of shared memory with 16-byte
-// stores (the fused SiLU through the decided fast path of activation.cuh). x crosses HBM
-// once and out once. Shared memory per CTA is C*128 bytes (64 KB at C = 512). A sweep of
-// tile widths (32, 64 pixels) and CTA sizes (32 to 256 threads) at the VAE decoder's four
-// shapes put this one first or within 5 % of first everywhere: fewer threads starve the
-// SiLU epilogue, narrower tiles halve the 128-byte channel segments.
+// Here one CTA owns a tile of P consecutive pixels x all C channels of one image (P = 64 for
+// C <= 256, 32 for C = 512, 16 beyond, so that a tile stays <= 64 KB; the CTA has P*C/64
+// threads, clamped to 64..256, i.e. eight 16-byte chunks of the tile per thread). The tile is
+// staged into shared memory with 16-byte cp.async copies (each channel contributes one
+// contiguous 2P-byte segment). Then P/2 lanes walk the channels, two adjacent pixels per lane
+// with one 32-bit shared load and one packed fp32x2 fma per channel, in channel order -- the
+// reference's own summation order per pixel, so statistics and outputs match it bit for bit.
+// Finally every thread scales its eight chunks out of shared memory (its pixels' rms held in
+// registers, gamma staged in shared memory as fp32) with 16-byte stores, the fused SiLU
+// through the decided fast path of activation.cuh. x crosses HBM once and out once. Measured
+// against the previous layout (64 threads walking one pixel each with 2-byte loads, 256
+// threads per CTA at every C): the norm alone 85.9 against 93.5 us at [128, 1024^2] (0.96 of
+// the measured peak), fused with SiLU 124 against 141 us.
 //
 // When the tiles are few, channel_norm_cluster (below) spreads each over a cluster of CTAs.
 //
@@ -37,9 +39,17 @@
 namespace anima {
 namespace {
 
-constexpr int kCnPix = 64;                  // pixels per tile
-constexpr int kCnBlock = 256;
+constexpr int kCnPix = 64;                  // pixels per tile of the cluster kernel
+constexpr int kCnBlock = 256;               // threads per CTA of the cluster kernel (and the tile kernel's maximum)
 constexpr int kCnMaxSmem = 200 * 1024;      // tile bytes we allow per CTA
+
+// Tile width of the tile kernel for C channels: <= 64 KB of bf16 per tile, 16..64 pixels.
+inline int cn_tile_pix(int C) { return C <= 256 ? 64 : C <= 512 ? 32 : 16; }
+// Its CTA size: eight 16-byte chunks of the tile per thread, 64..256 threads.
+inline int cn_tile_threads(int C, int P) {
+    const int64_t t = (int64_t)P * C / 64;
+    return t < 64 ? 64 : t > kCnBlock ? kCnBlock : ((int)t + 31) / 32 * 32;
+}
 
 __device__ __forceinline__ float ldb(const anima_bf16 *p) {
     return __bfloat162float(*reinterpret_cast<const __nv_bfloat16 *>(p));
@@ -141,51 +151,114 @@ __device__ __forceinline__ Vec8 norm_chunk(const anima_bf16 *chunk, const float 
     return o;
 }
 
-template <bool kSilu, bool kBias, bool kPixel>
+// The tile kernel (see the header): P pixels x C channels per CTA, blockDim.x threads.
+// Shared memory: gamma as fp32 [C], the per-pixel rms [P], then the tile [C][P] (+ the
+// conv-bias pairs [C] for kBias).
+template <int P, bool kSilu, bool kBias, bool kPixel>
 __global__ void __launch_bounds__(kCnBlock) channel_norm_tile(CnArgs a) {
     pdl_wait();
-    constexpr int kVecs = kCnPix / 8;  // 16-byte chunks per channel row of the tile
-    extern __shared__ __align__(16) anima_bf16 tile[];  // [C][kCnPix]
-    __shared__ __align__(16) float rms_s[kCnPix];
+    constexpr int kVecs = P / 8;  // 16-byte chunks per channel row of the tile
+    extern __shared__ __align__(16) unsigned char cn_smem[];
+    float *gam = reinterpret_cast<float *>(cn_smem);            // [C]
+    float *rms_s = gam + ((a.C + 3) & ~3);                      // [P]
+    anima_bf16 *tile = reinterpret_cast<anima_bf16 *>(rms_s + P);  // [C][P]
+    const int nthr = blockDim.x;
     const int b = blockIdx.x / a.tiles_per_image;
-    const int s_tile = (blockIdx.x - b * a.tiles_per_image) * kCnPix;
-    const int live_vecs = min(kCnPix, a.spatial - s_tile) / 8;  // spatial % 8 == 0
+    const int s_tile = (blockIdx.x - b * a.tiles_per_image) * P;
+    const int live_vecs = min(P, a.spatial - s_tile) / 8;  // spatial % 8 == 0
     const int64_t img = (int64_t)b * a.C * a.spatial;
     const int nchunks = a.C * kVecs;
 
-    // Stage: chunk q = (channel q / kVecs, pixel vector q % kVecs).
-    for (int q = threadIdx.x; q < nchunks; q += kCnBlock) {
+    // Stage: chunk q = (channel q / kVecs, pixel vector q % kVecs) lands at tile + 8q.
+    const anima_bf16 *src = a.x + img + s_tile;
+    for (int q = threadIdx.x; q < nchunks; q += nthr) {
         const int c = q / kVecs, v = q % kVecs;
-        if (v < live_vecs)
-            cp_async16(tile + c * kCnPix + v * 8, a.x + img + (int64_t)c * a.spatial + s_tile + v * 8);
+        if (v < live_vecs) cp_async16(tile + q * 8, src + (int64_t)c * a.spatial + v * 8);
     }
-    uint32_t *bias_s = reinterpret_cast<uint32_t *>(tile + a.C * kCnPix);  // [C] (b, b) pairs (kBias)
+    uint32_t *bias_s = reinterpret_cast<uint32_t *>(tile + a.C * P);  // [C] (b, b) pairs (kBias)
     if constexpr (kBias) {  // loads in flight with the tile's copies
-        for (int c = threadIdx.x; c < a.C; c += kCnBlock) bias_s[c] = bias_pair(a.bias + c);
+        for (int c = threadIdx.x; c < a.C; c += nthr) bias_s[c] = bias_pair(a.bias + c);
+    }
+    if constexpr (!kPixel) {
+        for (int c = threadIdx.x; c < a.C; c += nthr) gam[c] = ldb(a.gamma + c);
     }
     cp_async_wait_all();
     __syncthreads();
     if constexpr (kBias) {
-        for (int q = threadIdx.x; q < nchunks; q += kCnBlock) {
+        for (int q = threadIdx.x; q < nchunks; q += nthr) {
             const int c = q / kVecs, v = q % kVecs;
-            if (v < live_vecs) add_bias8(tile + c * kCnPix + v * 8, bias_s[c]);
+            if (v < live_vecs) add_bias8(tile + q * 8, bias_s[c]);
         }
         __syncthreads();
     }
 
-    if (threadIdx.x < kCnPix) rms_s[threadIdx.x] = pixel_rms<kPixel>(tile, threadIdx.x, live_vecs, a.C, a.eps);
+    // vae_kernels.cu:68-74: each pixel's sum of squares over the channels in order; lane t
+    // walks pixels 2t and 2t+1 with one packed fma per channel (each lane of FFMA2 rounds like
+    // the scalar fma), the next 8 channels' loads issued before the current 8 fmas.
+    if (threadIdx.x < P / 2) {
+        const uint32_t *col = reinterpret_cast<const uint32_t *>(tile) + threadIdx.x;
+        float2 q2 = make_float2(0.0f, 0.0f);
+        const int full = a.C & ~7;
+        uint32_t cur[8];
+        if (full > 0) {
+#pragma unroll
+            for (int j = 0; j < 8; ++j) cur[j] = col[j * (P / 2)];
+        }
+        for (int c = 0; c < full; c += 8) {
+            uint32_t nxt[8];
+            const bool more = c + 8 < full;
+            if (more) {
+#pragma unroll
+                for (int j = 0; j < 8; ++j) nxt[j] = col[(c + 8 + j) * (P / 2)];
+            }
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                const float2 f = make_float2(bf_lo(cur[j]), bf_hi(cur[j]));
+                q2 = __ffma2_rn(f, f, q2);
+            }
+            if (more) {
+#pragma unroll
+                for (int j = 0; j < 8; ++j) cur[j] = nxt[j];
+            }
+        }
+        for (int c = full; c < a.C; ++c) {
+            const uint32_t w = col[c * (P / 2)];
+            const float2 f = make_float2(bf_lo(w), bf_hi(w));
+            q2 = __ffma2_rn(f, f, q2);
+        }
+        // pixels beyond the tile's live width hold no data: their values are never used
+        reinterpret_cast<float2 *>(rms_s)[threadIdx.x] =
+            make_float2(norm_scale<kPixel>(q2.x, a.C, a.eps), norm_scale<kPixel>(q2.y, a.C, a.eps));
+    }
     __syncthreads();
     pdl_launch();
 
     // vae_kernels.cu:75-80: out = (x * rms) * gamma[c], from shared memory; SiLU (silu.cu)
-    // of the stored bf16 value when fused.
-    for (int q = threadIdx.x; q < nchunks; q += kCnBlock) {
-        const int c = q / kVecs, v = q % kVecs;
-        if (v >= live_vecs) continue;
+    // of the stored bf16 value when fused. Thread t owns pixel vector v = t % kVecs of
+    // channels t / kVecs, t / kVecs + nthr / kVecs, ...
+    const int v = threadIdx.x % kVecs;
+    if (v >= live_vecs) return;
+    float r[8];
+    {
+        const float4 r0 = reinterpret_cast<const float4 *>(rms_s)[2 * v];
+        const float4 r1 = reinterpret_cast<const float4 *>(rms_s)[2 * v + 1];
+        r[0] = r0.x; r[1] = r0.y; r[2] = r0.z; r[3] = r0.w;
+        r[4] = r1.x; r[5] = r1.y; r[6] = r1.z; r[7] = r1.w;
+    }
+    anima_bf16 *dst = a.out + img + s_tile + v * 8;
+    for (int c = threadIdx.x / kVecs; c < a.C; c += nthr / kVecs) {
+        const Vec8 xv = *reinterpret_cast<const Vec8 *>(tile + c * P + v * 8);
         // the pixel norm has no gamma: a factor of exactly 1 leaves x * rms as it is
-        Vec8 o = norm_chunk(tile + c * kCnPix + v * 8, rms_s, v, kPixel ? 1.0f : ldb(a.gamma + c));
+        const float gm = kPixel ? 1.0f : gam[c];
+        Vec8 o;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const float2 t2 = __fmul2_rn(make_float2(bf_lo(xv.w[j]), bf_hi(xv.w[j])), make_float2(r[2 * j], r[2 * j + 1]));
+            const float2 u = __fmul2_rn(t2, make_float2(gm, gm));
+            o.w[j] = pack_bf2(u.x, u.y);
+        }
         if constexpr (kSilu) o = fast_chunk<SiluF>(o);
-        st_vec(a.out + img + (int64_t)c * a.spatial + s_tile + v * 8, o);
+        st_vec(dst + (int64_t)c * a.spatial, o);
     }
 }
 
@@ -328,25 +401,41 @@ int channel_norm(const anima_bf16 *x, const anima_bf16 *gamma, anima_bf16 *out, 
     if (partial_overlap(x, n * 2, out, n * 2) || (!kPixel && partial_overlap(gamma, (int64_t)C * 2, out, n * 2)) ||
         (kBias && overlaps(bias, (int64_t)C * 2, out, n * 2)))
         return ANIMA_ERR_OVERLAP;
-    CnArgs a{x, gamma, out, bias, C, spatial, eps, (spatial + kCnPix - 1) / kCnPix};
+    const int P = cn_tile_pix(C);
+    CnArgs a{x, gamma, out, bias, C, spatial, eps, (spatial + P - 1) / P};
     const int64_t tiles = (int64_t)B * a.tiles_per_image;
-    const int64_t per_ch = kCnPix * 2 + (kBias ? 4 : 0);  // shared bytes per channel: tile row (+ bias)
-    const int64_t smem = (int64_t)C * per_ch;
+    // tile kernel shared bytes: gamma (fp32) + rms + tile rows (+ bias pairs)
+    const int64_t smem = (int64_t)((C + 3) & ~3) * 4 + (int64_t)P * 4 + (int64_t)C * (P * 2 + (kBias ? 4 : 0));
+    const int64_t per_ch = kCnPix * 2 + (kBias ? 4 : 0);  // cluster kernel: shared bytes per channel
     const int Cq = (C + kCnCluster - 1) / kCnCluster;
+    const int64_t cl_tiles = (int64_t)B * ((spatial + kCnPix - 1) / kCnPix);
     int err = ANIMA_OK;
-    // Few tiles (at most two per SM): spread each over a cluster. Many tiles keep every SM busy
-    // already, and the cluster's hand-offs would then only serialise each tile (measured).
-    if (spatial % 8 == 0 && aligned16(x) && aligned16(out) && C >= 64 && (int64_t)Cq * per_ch <= kCnMaxSmem &&
-        tiles <= 2 * (int64_t)sm_count()) {
+    // Few tiles (at most two per SM): the fused SiLU forms spread each over a cluster (their
+    // epilogue needs the threads). Many tiles keep every SM busy already, and the cluster's
+    // hand-offs would then only serialise each tile (measured); the norm alone runs the tile
+    // kernel at every size (13.0 against 14.7 us on the cluster at [512, 128^2]).
+    if (kSilu && spatial % 8 == 0 && aligned16(x) && aligned16(out) && C >= 64 &&
+        (int64_t)Cq * per_ch <= kCnMaxSmem && cl_tiles <= 2 * (int64_t)sm_count()) {
+        a.tiles_per_image = (spatial + kCnPix - 1) / kCnPix;
         auto kern = channel_norm_cluster<kSilu, kBias, kPixel>;
         if (int e = allow_dynamic_smem((const void *)kern, kCnMaxSmem, kPixel ? 13 : kBias ? 7 : kSilu ? 5 : 4)) return e;
-        launch_cluster(kern, kCnCluster, (unsigned)(tiles * kCnCluster), kCnBlock, (size_t)(Cq * per_ch), stream, a,
-                       Cq);
-    } else if (spatial % 8 == 0 && aligned16(x) && aligned16(out) && smem <= kCnMaxSmem &&
-        tiles < 2147483647) {
-        auto kern = channel_norm_tile<kSilu, kBias, kPixel>;
-        if (int e = allow_dynamic_smem((const void *)kern, kCnMaxSmem, kPixel ? 12 : kBias ? 6 : kSilu ? 1 : 0)) return e;
-        launch(kern, (unsigned)tiles, kCnBlock, (size_t)smem, stream, a);
+        launch_cluster(kern, kCnCluster, (unsigned)(cl_tiles * kCnCluster), kCnBlock, (size_t)(Cq * per_ch), stream,
+                       a, Cq);
+    } else if (spatial % 8 == 0 && aligned16(x) && aligned16(out) && smem <= kCnMaxSmem && tiles < 2147483647) {
+        const int nthr = cn_tile_threads(C, P);
+        const int form = kPixel ? 3 : kBias ? 2 : kSilu ? 1 : 0;  // one smem slot per kernel instance
+        const int slot = P == 64 ? (kPixel ? 12 : kBias ? 6 : kSilu ? 1 : 0) : (P == 32 ? 16 : 20) + form;
+        switch (P) {
+#define ANIMA_CN_TILE(Pv)                                                                                  \
+    case Pv: {                                                                                             \
+        auto kern = channel_norm_tile<Pv, kSilu, kBias, kPixel>;                                           \
+        if (int e = allow_dynamic_smem((const void *)kern, kCnMaxSmem, slot)) return e;                    \
+        launch(kern, (unsigned)tiles, nthr, (size_t)smem, stream, a);                                      \
+        break;                                                                                             \
+    }
+            ANIMA_CN_TILE(64) ANIMA_CN_TILE(32) ANIMA_CN_TILE(16)
+#undef ANIMA_CN_TILE
+        }
     } else {
         const int64_t pixels = (int64_t)B * spatial;
         const unsigned blocks = wave_grid((const void *)channel_norm_serial<kSilu, kBias, kPixel>, 256, 0, pixels, &err);

@@ -363,7 +363,7 @@ class ClockSampler:
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+                 "-lms", "20"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except OSError:
             self.proc = None
 
@@ -562,13 +562,16 @@ def per_op_times(chain, ops, reps):
     return out
 
 
-def headline_kernels(ops, device, peak, reps=384):
+def headline_kernels(ops, device, peak, reps=384, only=None, steps=3, warmup=3):
     """Every in-scope row / elementwise kernel at the headline shape, 4096 tokens x 2048
     (GELU and SiLU at the FFN width, [4096, 8192]; QK RMSNorm on the same tensor as
     [4096*16, 128] head rows; Cosmos RoPE on [4096, 16*128] with the (1, 64, 64) grid's
     tables), each launch cycling 8 buffer sets (> 2x L2) so every launch reads from HBM.
     Each case is a CUDA graph of 48 back-to-back launches of that kernel alone, replayed;
-    us = graph time / launches. Returns name -> {us, gbs, frac}."""
+    us = graph time / launches. Returns name -> {us, gbs, frac}.
+
+    only: the name of one case (profiling aid, for ncu captures): run `warmup` then `steps`
+    eager launches of it, print their timing and return None."""
     import torch
 
     import tables
@@ -612,6 +615,23 @@ def headline_kernels(ops, device, peak, reps=384):
         "a10_add": (6 * N * D, lambda i: ops.add(P(x[i]), P(y[i]), P(o[i]), N * D, S())),
         "a10_mul": (6 * N * D, lambda i: ops.call("mul", P(x[i]), P(y[i]), P(o[i]), N * D, S())),
     }
+    if only is not None:
+        if only not in cases:
+            raise SystemExit(f"--only {only}: no such case (cases: {', '.join(cases)})")
+        nbytes, fn = cases[only]
+        for i in range(warmup):
+            fn(i % sets)
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for i in range(steps):
+            fn(i % sets)
+        b.record()
+        torch.cuda.synchronize()
+        us = a.elapsed_time(b) * 1e3 / steps
+        print(json.dumps({"op": only, "impl": ops.kind, "calls": steps, "us_per_call": round(us, 2),
+                          "gbs": round(nbytes / (us * 1e-6) / 1e9, 1)}))
+        return None
     res = {}
     per_graph = 6 * sets  # launches per captured graph, cycling the buffer sets
     for name, (nbytes, fn) in cases.items():
@@ -809,6 +829,23 @@ def other_ops(ops, device, peak, reps=96, only=None, steps=3, warmup=3):
                       lambda i: (ops.call("rms_norm", P(xl[i]), P(wh), P(xl[i]), R * H, HD, eps, S()),
                                  ops.call("rope_cosmos_strided", P(xl[i]), P(ct_d), P(st_d), 2, 4096, H, HD,
                                           S()))))
+    # the adaLN-Zero temb folds (one launch each for add + norm + gate copy) and the GPU
+    # timestep embedding; the reference arm times its own chains for these in the DiT step
+    if ops.kind == "anima":
+        yl = [bf((R, D)) for _ in range(4)]
+        mods = bf((3 * D,), std=0.1)
+        tembv = bf((3 * D,), std=0.1)
+        gts = [torch.empty((D,), dtype=torch.bfloat16, device=device) for _ in range(2)]
+        cases.append(("cfg2_adaln_layernorm_temb_8192x2048", 4 * R * D + 12 * D, 1, 4,
+                      lambda i: ops.adaln_layernorm_temb(P(xl[i]), P(mods), P(tembv), P(gts[i % 2]), P(ol[i]), R, D,
+                                                         eps, S())))
+        cases.append(("cfg2_residual_gate_adaln_temb_8192x2048", 8 * R * D + 14 * D, 1, 4,
+                      lambda i: ops.residual_gate_adaln_temb(P(xl[i]), P(yl[i]), P(gts[i % 2]), P(mods), P(tembv),
+                                                             P(gts[(i + 1) % 2]), P(ol[i]), R, D, eps, S())))
+        tsw = bf((2048,), mean=1.0, std=0.02)
+        tss = [torch.empty((2048,), dtype=torch.bfloat16, device=device) for _ in range(2)]
+        cases.append(("cfg2_timestep_embedding_2048", 2 * 2048 + 6 * 2048, 1, 2,
+                      lambda i: ops.timestep(617.25 + i, P(tsw), P(tss[0]), P(tss[1]), 2048, eps, S())))
 
     if only is not None:
         match = [c for c in cases if c[0] == only]
@@ -1008,15 +1045,17 @@ def main():
         args.no_headline = args.no_other_ops = True
 
     ops = AnimaOps() if args.impl == "anima" else RefOps()
-    chain = Chain(ops, device)
-    stream = torch.cuda.current_stream()
     peak, peak_kind = peaks()
     total_bytes, per_block, lpb = chain_bytes()
+    if args.only is not None and args.only not in lpb:  # one case of the other measurements
+        if args.only.startswith("a") and args.only[1:2].isdigit():
+            return headline_kernels(ops, device, peak, only=args.only, steps=args.steps, warmup=args.warmup)
+        return other_ops(ops, device, peak, only=args.only, steps=args.steps, warmup=args.warmup)
+    chain = Chain(ops, device)
+    stream = torch.cuda.current_stream()
 
     if args.only is not None:
-        if args.only in lpb:
-            return profile_one_op(args, chain, lpb[args.only] * CFG["blocks"], per_block[args.only] / lpb[args.only])
-        return other_ops(ops, device, peak, only=args.only, steps=args.steps, warmup=args.warmup)
+        return profile_one_op(args, chain, lpb[args.only] * CFG["blocks"], per_block[args.only] / lpb[args.only])
 
     # warm-up (also initialises every kernel and the library's device caches)
     for _ in range(args.warmup):
