@@ -10,7 +10,7 @@ namespace anima {
 namespace {
 constexpr int kMaxDevices = 64;
 std::atomic<int> g_sm_count[kMaxDevices];          // 0 = not queried yet
-std::atomic<unsigned> g_smem_slots[kMaxDevices];   // bit i set = slot i configured
+std::atomic<uint64_t> g_smem_slots[kMaxDevices];   // bit i set = slot i configured
 }  // namespace
 
 int sm_count() {
@@ -33,7 +33,7 @@ int sm_count() {
 int allow_dynamic_smem(const void *kernel, int bytes, int slot) {
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess) return ANIMA_ERR_NO_DEVICE;
-    const unsigned bit = 1u << slot;
+    const uint64_t bit = 1ull << slot;
     if (dev < kMaxDevices && (g_smem_slots[dev].load(std::memory_order_acquire) & bit)) return ANIMA_OK;
     cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
     if (e != cudaSuccess) return (int)e;

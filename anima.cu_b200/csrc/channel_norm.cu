@@ -45,10 +45,10 @@ constexpr int kCnMaxSmem = 200 * 1024;      // tile bytes we allow per CTA
 
 // Tile width of the tile kernel for C channels: <= 64 KB of bf16 per tile, 16..64 pixels.
 inline int cn_tile_pix(int C) { return C <= 256 ? 64 : C <= 512 ? 32 : 16; }
-// Its CTA size: eight 16-byte chunks of the tile per thread, 64..256 threads.
+// Its CTA size: about eight 16-byte chunks of the tile per thread, 64, 128 or 256 threads.
 inline int cn_tile_threads(int C, int P) {
     const int64_t t = (int64_t)P * C / 64;
-    return t < 64 ? 64 : t > kCnBlock ? kCnBlock : ((int)t + 31) / 32 * 32;
+    return t <= 64 ? 64 : t <= 128 ? 128 : 256;
 }
 
 __device__ __forceinline__ float ldb(const anima_bf16 *p) {
@@ -151,18 +151,20 @@ __device__ __forceinline__ Vec8 norm_chunk(const anima_bf16 *chunk, const float 
     return o;
 }
 
-// The tile kernel (see the header): P pixels x C channels per CTA, blockDim.x threads.
+// The tile kernel (see the header): P pixels x C channels per CTA, T threads (a compile-time
+// constant, so that the epilogue's channel loop has a fixed stride: measured faster than the
+// same kernel with the CTA size read at run time).
 // Shared memory: gamma as fp32 [C], the per-pixel rms [P], then the tile [C][P] (+ the
 // conv-bias pairs [C] for kBias).
-template <int P, bool kSilu, bool kBias, bool kPixel>
-__global__ void __launch_bounds__(kCnBlock) channel_norm_tile(CnArgs a) {
+template <int P, int T, bool kSilu, bool kBias, bool kPixel>
+__global__ void __launch_bounds__(T) channel_norm_tile(CnArgs a) {
     pdl_wait();
     constexpr int kVecs = P / 8;  // 16-byte chunks per channel row of the tile
     extern __shared__ __align__(16) unsigned char cn_smem[];
     float *gam = reinterpret_cast<float *>(cn_smem);            // [C]
     float *rms_s = gam + ((a.C + 3) & ~3);                      // [P]
     anima_bf16 *tile = reinterpret_cast<anima_bf16 *>(rms_s + P);  // [C][P]
-    const int nthr = blockDim.x;
+    constexpr int nthr = T;
     const int b = blockIdx.x / a.tiles_per_image;
     const int s_tile = (blockIdx.x - b * a.tiles_per_image) * P;
     const int live_vecs = min(P, a.spatial - s_tile) / 8;  // spatial % 8 == 0
@@ -423,19 +425,22 @@ int channel_norm(const anima_bf16 *x, const anima_bf16 *gamma, anima_bf16 *out, 
                        a, Cq);
     } else if (spatial % 8 == 0 && aligned16(x) && aligned16(out) && smem <= kCnMaxSmem && tiles < 2147483647) {
         const int nthr = cn_tile_threads(C, P);
-        const int form = kPixel ? 3 : kBias ? 2 : kSilu ? 1 : 0;  // one smem slot per kernel instance
-        const int slot = P == 64 ? (kPixel ? 12 : kBias ? 6 : kSilu ? 1 : 0) : (P == 32 ? 16 : 20) + form;
-        switch (P) {
-#define ANIMA_CN_TILE(Pv)                                                                                  \
-    case Pv: {                                                                                             \
-        auto kern = channel_norm_tile<Pv, kSilu, kBias, kPixel>;                                           \
+        // one shared-memory slot per kernel instance: 16 + 4 * (P, T) shape + form
+        const int form = kPixel ? 3 : kBias ? 2 : kSilu ? 1 : 0;
+        const int shape = P == 64 ? (nthr == 64 ? 0 : nthr == 128 ? 1 : 2) : P == 32 ? 3 : 4;
+        const int slot = 16 + 4 * shape + form;
+#define ANIMA_CN_TILE(Pv, Tv)                                                                              \
+    {                                                                                                      \
+        auto kern = channel_norm_tile<Pv, Tv, kSilu, kBias, kPixel>;                                       \
         if (int e = allow_dynamic_smem((const void *)kern, kCnMaxSmem, slot)) return e;                    \
-        launch(kern, (unsigned)tiles, nthr, (size_t)smem, stream, a);                                      \
-        break;                                                                                             \
+        launch(kern, (unsigned)tiles, Tv, (size_t)smem, stream, a);                                        \
     }
-            ANIMA_CN_TILE(64) ANIMA_CN_TILE(32) ANIMA_CN_TILE(16)
+        if (P == 64 && nthr == 64) ANIMA_CN_TILE(64, 64)
+        else if (P == 64 && nthr == 128) ANIMA_CN_TILE(64, 128)
+        else if (P == 64) ANIMA_CN_TILE(64, 256)
+        else if (P == 32) ANIMA_CN_TILE(32, 256)
+        else ANIMA_CN_TILE(16, 256)
 #undef ANIMA_CN_TILE
-        }
     } else {
         const int64_t pixels = (int64_t)B * spatial;
         const unsigned blocks = wave_grid((const void *)channel_norm_serial<kSilu, kBias, kPixel>, 256, 0, pixels, &err);

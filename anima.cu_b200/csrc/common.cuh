@@ -228,7 +228,7 @@ __device__ __forceinline__ void pdl_launch() { asm volatile("griddepcontrol.laun
 int sm_count();
 
 // Raises a kernel's dynamic shared-memory limit to `bytes` on the current device, once
-// per (device, slot); `slot` names the kernel (0..31). Returns ANIMA_OK or a cudaError_t.
+// per (device, slot); `slot` names the kernel (0..63). Returns ANIMA_OK or a cudaError_t.
 int allow_dynamic_smem(const void *kernel, int bytes, int slot);
 
 // Resident CTAs per SM of `kernel` launched with `block` threads and `smem` bytes of

@@ -531,111 +531,6 @@ __global__ void __launch_bounds__(SegShape<Op::NIN>::kThreads, SegShape<Op::NIN>
     cp_async_wait<0>();
 }
 
-// ------------------------------------------- residual gate + adaLN: one warp per row
-// hidden <- x + y*gate, normed <- LN(hidden)*(1+scale)+shift for D = 256K (K = 4: 1024,
-// K = 8: 2048). Lane l loads chunks l + 32k of both rows with direct 16-byte loads (all 2K
-// issued at once, coalesced), forms h in fp32, keeps bf16(h) for the outputs and replays the
-// reference's row tree on the unrounded h with the transposed butterfly
-// (ref_pair_tree_sum<32, K>). No shared-memory ring: short-lived 4-warp CTAs, one row per
-// warp, so CTAs retire progressively and the next launch's CTAs take their place early.
-// Before waiting on the previous kernel, each warp asks L2 for its two rows
-// (cp.async.bulk.prefetch -- a hint that cannot change what the loads after the wait
-// return) and the CTA triggers the dependent launch: the DRAM reads of this launch start
-// while the previous launch drains. Measured against the segment kernel: 13.3 against 13.7
-// us at 4096 rows, 23.3 against 23.7 at 8192, 47.8 against 51.5 at 18432 (bit-exact).
-constexpr int kRgBlock = 128;
-
-__device__ __forceinline__ void prefetch_l2(const void *p, unsigned bytes) {
-    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
-}
-
-template <int K, bool kTemb>
-__global__ void __launch_bounds__(kRgBlock) resgate_row_warp(ResGateAdaLNOp<kTemb> op, int64_t N, int D) {
-    const int lane = threadIdx.x & 31;
-    const int64_t row = (int64_t)blockIdx.x * (kRgBlock / 32) + (threadIdx.x >> 5);
-    const bool live = row < N;
-    anima_bf16 *hr = op.hidden + row * (int64_t)D;
-    const anima_bf16 *yr = op.sub_out + row * (int64_t)D;
-    if (live && lane < 2) prefetch_l2(lane == 0 ? (const void *)hr : (const void *)yr, (unsigned)D * 2u);
-    pdl_launch();
-    pdl_wait();
-    if constexpr (kTemb) fold_gate(op.fold, D);
-    Vec8 xv[K], yv[K];
-#pragma unroll
-    for (int k = 0; k < K; ++k) {
-        xv[k] = live ? ld_stream(hr + (lane + 32 * k) * 8) : Vec8{{0u, 0u, 0u, 0u}};
-        yv[k] = live ? ld_stream(yr + (lane + 32 * k) * 8) : Vec8{{0u, 0u, 0u, 0u}};
-    }
-    // h = x + y*gate in fp32 (the bf16 product is exact, so the fma rounds like the
-    // reference's); pair p = (h[2p], h[2p+1]): sum h0 + h1, squares fma(h0, h0, h1*h1)
-    float s[K][4], q[K][4];
-    Vec8 hb[K];
-#pragma unroll
-    for (int k = 0; k < K; ++k) {
-        float g[8], fx[8], fy[8], h[8];
-        unpack8(ld_cached(op.gate + (lane + 32 * k) * 8), g);
-        unpack8(xv[k], fx);
-        unpack8(yv[k], fy);
-#pragma unroll
-        for (int e = 0; e < 8; e += 2) {
-            const float2 hv = __ffma2_rn(f2(fy[e], fy[e + 1]), f2(g[e], g[e + 1]), f2(fx[e], fx[e + 1]));
-            h[e] = hv.x;
-            h[e + 1] = hv.y;
-        }
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            s[k][j] = h[2 * j] + h[2 * j + 1];
-            q[k][j] = resid_sq_pair(h[2 * j], h[2 * j + 1]);
-        }
-        hb[k] = pack8(h);
-    }
-    const float sum = ref_pair_tree_sum<32, K>(s, lane, kFull);
-    const float sq = ref_pair_tree_sum<32, K>(q, lane, kFull);
-    const float mean = __fdiv_rn(sum, (float)D);
-    const float inv = rsqrtf(ln_var(sq, mean, D) + op.eps);
-    if (!live) return;
-    anima_bf16 *o = op.normed + row * (int64_t)D;
-#pragma unroll
-    for (int k = 0; k < K; ++k) {
-        const int c = lane + 32 * k;
-        float f[8], sc[8], sh[8];
-        unpack8(hb[k], f);
-        unpack8(ld_cached(op.scale + c * 8), sc);
-        unpack8(ld_cached(op.shift + c * 8), sh);
-        if constexpr (kTemb) {  // the modulation vector plus temb, rounded as add_bf16 stores it
-            float ts[8], th[8];
-            unpack8(ld_cached(op.fold.tsc + c * 8), ts);
-            unpack8(ld_cached(op.fold.tsh + c * 8), th);
-#pragma unroll
-            for (int e = 0; e < 8; ++e) {
-                sc[e] = bf16_add(sc[e], ts[e]);
-                sh[e] = bf16_add(sh[e], th[e]);
-            }
-        }
-#pragma unroll
-        for (int e = 0; e < 8; e += 2) {
-            const float2 m = __fadd2_rn(f2(sc[e], sc[e + 1]), f2(1.0f, 1.0f));
-            const float2 n = __fmul2_rn(__fadd2_rn(f2(f[e], f[e + 1]), f2(-mean, -mean)), f2(inv, inv));
-            const float2 r = __ffma2_rn(n, m, f2(sh[e], sh[e + 1]));
-            f[e] = r.x;
-            f[e + 1] = r.y;
-        }
-        st_vec(hr + c * 8, hb[k]);
-        st_vec(o + c * 8, pack8(f));
-    }
-}
-
-// The warp-per-row residual gate for D in {1024, 2048} with every pointer 16-byte aligned.
-template <bool kTemb>
-bool dispatch_resgate_warp(const ResGateAdaLNOp<kTemb> &op, int64_t N, int D, cudaStream_t s, int &status) {
-    const unsigned grid = (unsigned)((N + kRgBlock / 32 - 1) / (kRgBlock / 32));
-    if (D == 2048) launch(resgate_row_warp<8, kTemb>, grid, kRgBlock, 0, s, op, N, D);
-    else if (D == 1024) launch(resgate_row_warp<4, kTemb>, grid, kRgBlock, 0, s, op, N, D);
-    else return false;
-    status = launch_status();
-    return true;
-}
-
 // ------------------------------------------------ small-row RMSNorm (D <= 256)
 // Per-head QK-norm rows (D = 128, 64) are a few hundred bytes, too short for the unit
 // pipeline above to pay off. Here every 8-lane team loads its row with direct 16-byte
@@ -951,8 +846,7 @@ extern "C" int anima_residual_gate_adaln_bf16(anima_bf16 *hidden, const anima_bf
     int st;
     if (aligned16(hidden) && aligned16(sub_out) && aligned16(gate) && aligned16(scale) && aligned16(shift) &&
         aligned16(normed) &&
-        (dispatch_resgate_warp(ResGateAdaLNOp<>{hidden, sub_out, gate, scale, shift, normed, eps}, N, D, stream, st) ||
-         dispatch_seg(ResGateAdaLNOp<>{hidden, sub_out, gate, scale, shift, normed, eps}, N, D, stream, st)))
+        dispatch_seg(ResGateAdaLNOp<>{hidden, sub_out, gate, scale, shift, normed, eps}, N, D, stream, st))
         return st;
     GenArgs a{hidden, hidden, sub_out, gate, scale, shift, nullptr, normed, D, eps};
     launch(row_generic<GenKind::ResGate>, generic_grid(N), ref_row_threads(D), 0, stream, a, N);
@@ -985,9 +879,7 @@ extern "C" int anima_residual_gate_adaln_temb_bf16(anima_bf16 *hidden, const ani
     int st;
     if (aligned16(hidden) && aligned16(sub_out) && aligned16(gate_in) && aligned16(mod) && aligned16(temb) &&
         aligned16(normed) && D % 8 == 0 &&
-        (dispatch_resgate_warp(ResGateAdaLNOp<true>{hidden, sub_out, gate_in, mod + D, mod, normed, eps, fold}, N, D,
-                               stream, st) ||
-         dispatch_seg(ResGateAdaLNOp<true>{hidden, sub_out, gate_in, mod + D, mod, normed, eps, fold}, N, D, stream, st)))
+        dispatch_seg(ResGateAdaLNOp<true>{hidden, sub_out, gate_in, mod + D, mod, normed, eps, fold}, N, D, stream, st))
         return st;
     GenArgs a{hidden, hidden, sub_out, gate_in, mod + D, mod, nullptr, normed, D, eps, fold};
     launch(row_generic<GenKind::ResGate>, generic_grid(N), ref_row_threads(D), 0, stream, a, N);
