@@ -43,11 +43,15 @@ constexpr int kCnPix = 64;                  // pixels per tile of the cluster ke
 constexpr int kCnBlock = 256;               // threads per CTA of the cluster kernel (and the tile kernel's maximum)
 constexpr int kCnMaxSmem = 200 * 1024;      // tile bytes we allow per CTA
 
-// Tile width of the tile kernel for C channels: <= 64 KB of bf16 per tile, 16..64 pixels.
-inline int cn_tile_pix(int C) { return C <= 256 ? 64 : C <= 512 ? 32 : 16; }
-// Its CTA size: about eight 16-byte chunks of the tile per thread, 64, 128 or 256 threads.
-inline int cn_tile_threads(int C, int P) {
-    const int64_t t = (int64_t)P * C / 64;
+// Tile width of the tile kernel for C channels, 16..64 pixels, and its CTA size (64, 128 or
+// 256 threads), from a sweep at the VAE decoder's shapes. With the SiLU epilogue: tiles of
+// <= 32 KB and about eight 16-byte chunks per thread (the epilogue wants many tiles in
+// flight); the norm alone: tiles of <= 64 KB and about four chunks per thread.
+inline int cn_tile_pix(int C, bool silu) {
+    return silu ? (C <= 256 ? 64 : C <= 512 ? 32 : 16) : (C <= 512 ? 64 : C <= 1024 ? 32 : 16);
+}
+inline int cn_tile_threads(int C, int P, bool silu) {
+    const int64_t t = (int64_t)P * C / (silu ? 64 : 32);
     return t <= 64 ? 64 : t <= 128 ? 128 : 256;
 }
 
@@ -403,7 +407,7 @@ int channel_norm(const anima_bf16 *x, const anima_bf16 *gamma, anima_bf16 *out, 
     if (partial_overlap(x, n * 2, out, n * 2) || (!kPixel && partial_overlap(gamma, (int64_t)C * 2, out, n * 2)) ||
         (kBias && overlaps(bias, (int64_t)C * 2, out, n * 2)))
         return ANIMA_ERR_OVERLAP;
-    const int P = cn_tile_pix(C);
+    const int P = cn_tile_pix(C, kSilu);
     CnArgs a{x, gamma, out, bias, C, spatial, eps, (spatial + P - 1) / P};
     const int64_t tiles = (int64_t)B * a.tiles_per_image;
     // tile kernel shared bytes: gamma (fp32) + rms + tile rows (+ bias pairs)
@@ -424,10 +428,10 @@ int channel_norm(const anima_bf16 *x, const anima_bf16 *gamma, anima_bf16 *out, 
         launch_cluster(kern, kCnCluster, (unsigned)(cl_tiles * kCnCluster), kCnBlock, (size_t)(Cq * per_ch), stream,
                        a, Cq);
     } else if (spatial % 8 == 0 && aligned16(x) && aligned16(out) && smem <= kCnMaxSmem && tiles < 2147483647) {
-        const int nthr = cn_tile_threads(C, P);
+        const int nthr = cn_tile_threads(C, P, kSilu);
         // one shared-memory slot per kernel instance: 16 + 4 * (P, T) shape + form
         const int form = kPixel ? 3 : kBias ? 2 : kSilu ? 1 : 0;
-        const int shape = P == 64 ? (nthr == 64 ? 0 : nthr == 128 ? 1 : 2) : P == 32 ? 3 : 4;
+        const int shape = P == 64 ? (nthr == 64 ? 0 : nthr == 128 ? 1 : 2) : P == 32 ? (nthr == 256 ? 3 : 5) : 4;
         const int slot = 16 + 4 * shape + form;
 #define ANIMA_CN_TILE(Pv, Tv)                                                                              \
     {                                                                                                      \
@@ -438,7 +442,8 @@ int channel_norm(const anima_bf16 *x, const anima_bf16 *gamma, anima_bf16 *out, 
         if (P == 64 && nthr == 64) ANIMA_CN_TILE(64, 64)
         else if (P == 64 && nthr == 128) ANIMA_CN_TILE(64, 128)
         else if (P == 64) ANIMA_CN_TILE(64, 256)
-        else if (P == 32) ANIMA_CN_TILE(32, 256)
+        else if (P == 32 && nthr == 256) ANIMA_CN_TILE(32, 256)
+        else if (P == 32) ANIMA_CN_TILE(32, 128)
         else ANIMA_CN_TILE(16, 256)
 #undef ANIMA_CN_TILE
     } else {
