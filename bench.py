@@ -964,11 +964,20 @@ def cfg1_step(ops, device, steps, peak):
     g_ms = time_steps(chain, k, s, graph) / k
     del graph
     e_ms = time_steps(chain, max(3, min(steps, 20)), s, None) / max(3, min(steps, 20))
+    f_ms = None
+    if ops.kind == "anima":  # the same step through the opt-in fused entry points
+        fgraph = capture(lambda st: chain.blocks_fused(st))
+        fgraph.replay()
+        torch.cuda.synchronize()
+        f_ms = time_steps(chain, k, s, fgraph) / k
+        del fgraph
     gbs = total / (g_ms * 1e-3) / 1e9
     out = {"workload": "cfg1: 512x512 image -> 1024 tokens, batch 1, 28-block DiT elementwise chain",
            "rows": chain.R, "bytes_per_step": total, "launches_per_step": c["blocks"] * chain.launches_per_block + 1,
            "ms_per_step": round(g_ms, 4), "ms_per_block": round(g_ms / c["blocks"], 4), "gbs": round(gbs, 1),
-           "frac": round(gbs / peak, 3), "eager_ms_per_step": round(e_ms, 4)}
+           "frac": round(gbs / peak, 3), "eager_ms_per_step": round(e_ms, 4),
+           "fused_ms_per_step": round(f_ms, 4) if f_ms is not None else None,
+           "fused_launches_per_step": chain.launches_fused + 1 if f_ms is not None else None}
     del chain
     torch.cuda.empty_cache()
     return out
