@@ -182,7 +182,8 @@ struct SoftmaxArgs {
 
 // Loads the 32 columns [c0, c0 + 32) of `row` into v (masked columns take the mask value;
 // columns at or beyond D are marked absent in `present`, a bit per column).
-template <bool kCausal>
+// kFull: every team lane's 32 columns exist (D == 32 x lanes per row, 16-byte rows).
+template <bool kCausal, bool kFull = false>
 __device__ __forceinline__ uint32_t load_seg(const SoftmaxArgs &a, const anima_bf16 *xr, int c0, int qi,
                                              float (&v)[32]) {
     uint32_t present = 0;
@@ -190,7 +191,7 @@ __device__ __forceinline__ uint32_t load_seg(const SoftmaxArgs &a, const anima_b
 #pragma unroll
     for (int g = 0; g < 4; ++g) {
         const int cc = c0 + 8 * g;
-        if (a.vec && cc + 8 <= a.D) {
+        if (kFull || (a.vec && cc + 8 <= a.D)) {
             if (kCausal && cc > qi) {
 #pragma unroll
                 for (int e = 0; e < 8; ++e) v[8 * g + e] = mv;
@@ -227,7 +228,10 @@ __device__ __forceinline__ float warp_tree32(float (&t)[32]) {
     return t[0];
 }
 
-template <bool kCausal, bool kCache>
+// kFull (with kCache): rows of exactly 32 columns per team lane, so no lane has absent
+// columns and the per-column presence tests drop out (measured 31 instructions per element
+// with them at [16 x 512, 512]).
+template <bool kCausal, bool kCache, bool kFull = false>
 __global__ void __launch_bounds__(kAttBlock) softmax_rows_kernel(SoftmaxArgs a) {
     pdl_wait();
     const int lane = threadIdx.x & 31;
@@ -247,17 +251,29 @@ __global__ void __launch_bounds__(kAttBlock) softmax_rows_kernel(SoftmaxArgs a) 
         uint32_t present = 0;
         float mx = -1e30f;
         for (int m = 0; m < spans; ++m) {
-            present = live ? load_seg<kCausal>(a, xr, 1024 * m + 32 * w, qi, v) : 0u;
+            if constexpr (kFull) {  // a row past the end reads row 0 and stores nothing
+                load_seg<kCausal, true>(a, xr, 32 * w, qi, v);
 #pragma unroll
-            for (int k = 0; k < 32; ++k)
-                if (present >> k & 1) mx = fmaxf(mx, v[k]);
+                for (int k = 0; k < 32; ++k) mx = fmaxf(mx, v[k]);
+            } else {
+                present = live ? load_seg<kCausal>(a, xr, 1024 * m + 32 * w, qi, v) : 0u;
+#pragma unroll
+                for (int k = 0; k < 32; ++k)
+                    if (present >> k & 1) mx = fmaxf(mx, v[k]);
+            }
         }
         for (int o = RL >> 1; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o, RL));
 
         // softmax.cu:37-54: per reference thread, the sum of its columns' exponentials in
         // column order; then the warp tree in registers and the tree over warps across the team.
         float p[32];
-        if constexpr (kCache) {
+        if constexpr (kFull) {
+#pragma unroll
+            for (int k = 0; k < 32; ++k) {
+                v[k] = expf(v[k] - mx);
+                p[k] = v[k];  // 0.0f + e == e
+            }
+        } else if constexpr (kCache) {
 #pragma unroll
             for (int k = 0; k < 32; ++k) {
                 v[k] = (present >> k & 1) ? expf(v[k] - mx) : 0.0f;
@@ -293,7 +309,7 @@ __global__ void __launch_bounds__(kAttBlock) softmax_rows_kernel(SoftmaxArgs a) 
                 float f[8];
 #pragma unroll
                 for (int e = 0; e < 8; ++e) f[e] = v[8 * g + e] * inv;
-                if (a.vec && cc + 8 <= a.D) {
+                if (kFull || (a.vec && cc + 8 <= a.D)) {
                     st_vec(yr + cc, pack8(f));
                 } else {
 #pragma unroll
@@ -319,15 +335,20 @@ int softmax_bf16(const anima_bf16 *x, anima_bf16 *out, int64_t rows, int D, int 
     SoftmaxArgs a{x, out, rows, D, T, rl_log, D % 8 == 0 && aligned16(x) && aligned16(out)};
     const int64_t warps = (rows + (32 >> rl_log) - 1) >> (5 - rl_log);
     const bool cache = D <= 1024;
-    const void *k = causal ? (cache ? (const void *)softmax_rows_kernel<true, true>
-                                    : (const void *)softmax_rows_kernel<true, false>)
-                           : (cache ? (const void *)softmax_rows_kernel<false, true>
-                                    : (const void *)softmax_rows_kernel<false, false>);
+    const bool full = cache && a.vec && D == (32 << rl_log);
+    const void *k = causal ? (full ? (const void *)softmax_rows_kernel<true, true, true>
+                                   : cache ? (const void *)softmax_rows_kernel<true, true>
+                                           : (const void *)softmax_rows_kernel<true, false>)
+                           : (full ? (const void *)softmax_rows_kernel<false, true, true>
+                                   : cache ? (const void *)softmax_rows_kernel<false, true>
+                                           : (const void *)softmax_rows_kernel<false, false>);
     int err = ANIMA_OK;
     const unsigned grid = wave_grid(k, kAttBlock, 0, warps * 32, &err);
     if (err) return err;
-    if (causal && cache) launch(softmax_rows_kernel<true, true>, grid, kAttBlock, 0, stream, a);
+    if (causal && full) launch(softmax_rows_kernel<true, true, true>, grid, kAttBlock, 0, stream, a);
+    else if (causal && cache) launch(softmax_rows_kernel<true, true>, grid, kAttBlock, 0, stream, a);
     else if (causal) launch(softmax_rows_kernel<true, false>, grid, kAttBlock, 0, stream, a);
+    else if (full) launch(softmax_rows_kernel<false, true, true>, grid, kAttBlock, 0, stream, a);
     else if (cache) launch(softmax_rows_kernel<false, true>, grid, kAttBlock, 0, stream, a);
     else launch(softmax_rows_kernel<false, false>, grid, kAttBlock, 0, stream, a);
     return launch_status();
@@ -507,8 +528,17 @@ extern "C" int anima_softmax_f32_to_bf16(const float *x, anima_bf16 *out, int N,
     if (!aligned_to(x, 4) || !aligned_to(out, 2)) return ANIMA_ERR_MISALIGNED;
     if (overlaps(x, (int64_t)N * D * 4, out, (int64_t)N * D * 2)) return ANIMA_ERR_OVERLAP;
     if (N > 2147483647) return ANIMA_ERR_TOO_LARGE;
-    const int threads = D <= 1024 ? (D + 31) / 32 * 32 : 1024;  // softmax.cu:248-249
+    // The reference launches min(roundup32(D), 1024) threads per row (softmax.cu:248-249), so
+    // for D <= 4096 thread t holds float4 t and nothing else, and the threads past D/4 -- whole
+    // warps of them, 12 of 16 at D = 512 -- carry the empty pair (-1e30, 0), which every merge
+    // passes through unchanged: merging it into (m, s) leaves (m, s), and merging (m, s) into
+    // it yields (m, s). Launching only the warps that hold columns therefore gives the same
+    // bits (warp 0's padding supplies the same empty pairs for the missing warps) with a
+    // quarter of the threads and no idle warps at D = 512.
+    const int ref_threads = D <= 1024 ? (D + 31) / 32 * 32 : 1024;
+    const int used = (D / 4 + 31) / 32 * 32;
+    const int threads = D <= 4096 ? (used < 32 ? 32 : used) : ref_threads;
     const bool vec = D % 4 == 0 && aligned16(x) && aligned_to(out, 8);
-    launch(softmax_f32_bf16_kernel, (unsigned)N, threads < 32 ? 32 : threads, 0, stream, x, out, D, vec);
+    launch(softmax_f32_bf16_kernel, (unsigned)N, threads, 0, stream, x, out, D, vec);
     return launch_status();
 }
