@@ -171,6 +171,26 @@ __device__ __forceinline__ void bc8(const float *bc, int seg, int k, float (&f)[
     f[4] = b.x; f[5] = b.y; f[6] = b.z; f[7] = b.w;
 }
 
+// Broadcast vector b of an op, chunk k of segment `seg`, as 8 floats. kBf: the vectors are
+// staged as bf16 chunks in the rows' swizzled layout (b * D/8 chunks in), and `plus1` adds the
+// reference's 1.0f in fp32 here; otherwise they are fp32 in the bc_pos layout with it added.
+template <bool kBf>
+__device__ __forceinline__ void bvec8(const float *bc, int b, int D, int seg, int k, bool plus1, float (&f)[8]) {
+    if constexpr (kBf) {
+        unpack8(reinterpret_cast<const Vec8 *>(bc)[b * (D >> 3) + swz(8 * seg + k)], f);
+        if (plus1) {
+#pragma unroll
+            for (int e = 0; e < 8; e += 2) {
+                const float2 t = __fadd2_rn(make_float2(f[e], f[e + 1]), make_float2(1.0f, 1.0f));
+                f[e] = t.x;
+                f[e + 1] = t.y;
+            }
+        }
+    } else {
+        bc8(bc + b * D, seg, k, f);
+    }
+}
+
 // Packed fp32x2 arithmetic (sm_100 FFMA2/FADD2/FMUL2): two lanes of IEEE round-to-nearest
 // per instruction, so results equal the scalar ops bit for bit at half the issue cost.
 __device__ __forceinline__ float2 f2(float a, float b) { return make_float2(a, b); }
@@ -243,6 +263,7 @@ struct AdaLNOp {
     __device__ anima_bf16 *dst(int) const { return out; }
     TembFold fold = {};
     static constexpr bool kFold = kTemb;
+    static constexpr bool kBfBc = !kTemb;     // bf16 staging (the fold needs its sums rounded first)
     static constexpr unsigned kPlusOne = 1u;  // the reference's (1.0f + scale[d]), rounded to fp32
     __device__ const anima_bf16 *bvec(int i) const { return i == 0 ? scale : shift; }
     __device__ const anima_bf16 *btemb(int i) const { return i == 0 ? fold.tsc : fold.tsh; }
@@ -260,8 +281,8 @@ struct AdaLNOp {
         for (int k = 0; k < 8; ++k) {
             float f[8], sc[8], sh[8];
             unpack8(v[k], f);
-            bc8(bc, seg, k, sc);
-            bc8(bc + D, seg, k, sh);
+            bvec8<kBfBc>(bc, 0, D, seg, k, true, sc);
+            bvec8<kBfBc>(bc, 1, D, seg, k, false, sh);
             ln_modulate8<kRoundFirst>(f, mean, inv, sc, sh, f);
             slot[swz(8 * lane + k)] = pack8(f);
         }
@@ -279,6 +300,7 @@ struct ResGateAdaLNOp {  // layer_norm.cu:146-196
     __device__ anima_bf16 *dst(int o) const { return o == 0 ? hidden : normed; }
     TembFold fold = {};  // the gate is the previous set's, already summed
     static constexpr bool kFold = kTemb;
+    static constexpr bool kBfBc = !kTemb;
     static constexpr unsigned kPlusOne = 2u;
     __device__ const anima_bf16 *bvec(int i) const { return i == 0 ? gate : (i == 1 ? scale : shift); }
     __device__ const anima_bf16 *btemb(int i) const { return i == 0 ? nullptr : (i == 1 ? fold.tsc : fold.tsh); }
@@ -293,7 +315,7 @@ struct ResGateAdaLNOp {  // layer_norm.cu:146-196
 #pragma unroll
         for (int k = 0; k < 8; ++k) {
             float g[8], fx[8], fy[8];
-            bc8(bc, seg, k, g);
+            bvec8<kBfBc>(bc, 0, D, seg, k, false, g);
             unpack8(x[k], fx);
             unpack8(y[k], fy);
 #pragma unroll
@@ -320,8 +342,8 @@ struct ResGateAdaLNOp {  // layer_norm.cu:146-196
             const Vec8 hb = pack8(h[k]);
             float f[8], sc[8], sh[8];
             unpack8(hb, f);
-            bc8(bc + D, seg, k, sc);
-            bc8(bc + 2 * D, seg, k, sh);
+            bvec8<kBfBc>(bc, 1, D, seg, k, true, sc);
+            bvec8<kBfBc>(bc, 2, D, seg, k, false, sh);
             ln_modulate8<false>(f, mean, inv, sc, sh, f);
             slot[swz(8 * lane + k)] = hb;
             slot[kUnitChunks + swz(8 * lane + k)] = pack8(f);
@@ -339,6 +361,7 @@ struct RmsOp {  // rms_norm.cu:9-67
     __device__ anima_bf16 *dst(int) const { return out; }
     TembFold fold = {};
     static constexpr bool kFold = false;
+    static constexpr bool kBfBc = true;
     static constexpr unsigned kPlusOne = 0u;
     __device__ const anima_bf16 *bvec(int) const { return weight; }
     __device__ const anima_bf16 *btemb(int) const { return nullptr; }
@@ -355,7 +378,7 @@ struct RmsOp {  // rms_norm.cu:9-67
             unpack8(v[k], f);
             if constexpr (kWeight) {
                 float w[8];
-                bc8(bc, seg, k, w);
+                bvec8<kBfBc>(bc, 0, D, seg, k, false, w);
 #pragma unroll
                 for (int e = 0; e < 8; e += 2) {
                     const float2 o = __fmul2_rn(__fmul2_rn(f2(f[e], f[e + 1]), f2(r, r)), f2(w[e], w[e + 1]));
@@ -457,6 +480,14 @@ struct BcastStage {
     }
 };
 
+// Bytes per broadcast-vector element in shared memory: 2 for ops that stage them as bf16
+// (Op::kBfBc), 4 for the fp32 stage (the temb folds, whose sums are rounded on the way in).
+template <class Op>
+__host__ __device__ constexpr int bc_bytes() {
+    if constexpr (Op::NB > 0) return Op::kBfBc ? 2 : 4;
+    return 4;
+}
+
 template <int NW, class Op>
 __global__ void __launch_bounds__(SegShape<Op::NIN>::kThreads, SegShape<Op::NIN>::kMinCtas)
     row_seg(Op op, int64_t N, int D) {
@@ -468,7 +499,7 @@ __global__ void __launch_bounds__(SegShape<Op::NIN>::kThreads, SegShape<Op::NIN>
     constexpr int kRowChunks = NW * 8;
     extern __shared__ __align__(16) unsigned char seg_smem[];
     float *bc = reinterpret_cast<float *>(seg_smem);
-    Vec8 *ring = reinterpret_cast<Vec8 *>(seg_smem + (size_t)NB * D * 4) +
+    Vec8 *ring = reinterpret_cast<Vec8 *>(seg_smem + (size_t)NB * D * bc_bytes<Op>()) +
                  (size_t)(threadIdx.x >> 5) * NST * NIN * kUnitChunks;
     const int lane = threadIdx.x & 31;
     const int64_t units = (N + G - 1) / G;
@@ -494,7 +525,20 @@ __global__ void __launch_bounds__(SegShape<Op::NIN>::kThreads, SegShape<Op::NIN>
         }
         cp_async_commit();  // one group per unit, empty or not, keeps the counting uniform
     };
-    if constexpr (NB > 0) {
+    if constexpr (NB > 0 && bc_bytes<Op>() == 2) {
+        // the vectors as bf16 chunks, swizzled like a unit, in the same copy group as the first
+        // unit: no conversion pass, and half the shared-memory reads per row of an fp32 stage
+        const int nch = D >> 3;
+        Vec8 *bcv = reinterpret_cast<Vec8 *>(seg_smem);
+        for (int i = threadIdx.x; i < NB * nch; i += SegShape<NIN>::kThreads) {
+            const int b = i / nch, c = i - b * nch;
+            cp_async16(bcv + b * nch + swz(c), op.bvec(b) + 8 * c);
+        }
+#pragma unroll
+        for (int st = 0; st < NST; ++st) issue(first + st * nwarps, st);
+        cp_async_wait<NST - 1>();  // group 0 (the vectors and this warp's first unit) has landed ...
+        __syncthreads();           // ... for every thread
+    } else if constexpr (NB > 0) {
         BcastStage<Op> bcs;
         bcs.load(op, D);
 #pragma unroll
@@ -707,7 +751,7 @@ __global__ void gemma_rms_generic(const anima_bf16 *x, const anima_bf16 *w, anim
 
 template <class Op, int NW>
 int launch_seg(const Op &op, int64_t N, int D, cudaStream_t s) {
-    const int smem = Op::NB * D * 4 + SegShape<Op::NIN>::kRingBytes;
+    const int smem = Op::NB * D * bc_bytes<Op>() + SegShape<Op::NIN>::kRingBytes;
     auto kern = row_seg<NW, Op>;
     int err = ANIMA_OK;
     constexpr int kSegWarps = SegShape<Op::NIN>::kWarps, kSegThreads = SegShape<Op::NIN>::kThreads;
