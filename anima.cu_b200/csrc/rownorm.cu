@@ -81,18 +81,12 @@ __device__ __forceinline__ void fold_gate(const TembFold &t, int D) {
 // copies chunks l, l+32, ...), read back per segment, the outputs are written into the
 // same slot and stored to global memory coalesced again. Slots are XOR-swizzled at
 // 16-byte granularity inside each 128-byte group so that both patterns are free of bank
-// conflicts. Broadcast vectors (1+scale, shift, gate, weight) are converted to fp32 once
-// per CTA into shared memory (swizzled per segment the same way).
+// conflicts. Broadcast vectors (scale, shift, gate, weight) are staged once per CTA in shared
+// memory as bf16 chunks, swizzled the same way, and converted as they are read.
 
 constexpr int kUnitChunks = 256;  // 16-byte chunks per input per unit (4 KB)
 
 __device__ __forceinline__ int swz(int c) { return (c & ~7) | ((c & 7) ^ ((c >> 3) & 7)); }
-
-// fp32 broadcast vector layout: float4 j (0..15) of segment s lives at 16s + (j ^ (s&7)).
-__device__ __forceinline__ int bc_pos(int d) {
-    const int s = d >> 6, j = (d >> 2) & 15;
-    return ((s << 4) + (j ^ (s & 7))) * 4 + (d & 3);
-}
 
 // CTA size, ring depth and occupancy target: 4 warps with 2 slots each; one-input ops run 4
 // CTAs per SM (at most 128 registers per thread), two- and three-input ops 2.
@@ -164,30 +158,18 @@ __device__ __forceinline__ void load_seg(const Vec8 *buf, int lane, Vec8 (&v)[8]
     for (int k = 0; k < 8; ++k) v[k] = buf[swz(8 * lane + k)];
 }
 
-__device__ __forceinline__ void bc8(const float *bc, int seg, int k, float (&f)[8]) {
-    const float4 *q = reinterpret_cast<const float4 *>(bc) + (seg << 4);
-    const float4 a = q[(2 * k) ^ (seg & 7)], b = q[(2 * k + 1) ^ (seg & 7)];
-    f[0] = a.x; f[1] = a.y; f[2] = a.z; f[3] = a.w;
-    f[4] = b.x; f[5] = b.y; f[6] = b.z; f[7] = b.w;
-}
-
-// Broadcast vector b of an op, chunk k of segment `seg`, as 8 floats. kBf: the vectors are
-// staged as bf16 chunks in the rows' swizzled layout (b * D/8 chunks in), and `plus1` adds the
-// reference's 1.0f in fp32 here; otherwise they are fp32 in the bc_pos layout with it added.
-template <bool kBf>
+// Broadcast vector b of an op, chunk k of segment `seg`, as 8 floats: the vectors are staged
+// as bf16 chunks in the rows' swizzled layout (vector b starts D/8 chunks after vector b-1);
+// `plus1` adds the reference's 1.0f (its (1.0f + scale[d]) in fp32) here.
 __device__ __forceinline__ void bvec8(const float *bc, int b, int D, int seg, int k, bool plus1, float (&f)[8]) {
-    if constexpr (kBf) {
-        unpack8(reinterpret_cast<const Vec8 *>(bc)[b * (D >> 3) + swz(8 * seg + k)], f);
-        if (plus1) {
+    unpack8(reinterpret_cast<const Vec8 *>(bc)[b * (D >> 3) + swz(8 * seg + k)], f);
+    if (plus1) {
 #pragma unroll
-            for (int e = 0; e < 8; e += 2) {
-                const float2 t = __fadd2_rn(make_float2(f[e], f[e + 1]), make_float2(1.0f, 1.0f));
-                f[e] = t.x;
-                f[e + 1] = t.y;
-            }
+        for (int e = 0; e < 8; e += 2) {
+            const float2 t = __fadd2_rn(make_float2(f[e], f[e + 1]), make_float2(1.0f, 1.0f));
+            f[e] = t.x;
+            f[e + 1] = t.y;
         }
-    } else {
-        bc8(bc + b * D, seg, k, f);
     }
 }
 
@@ -216,7 +198,7 @@ __device__ __forceinline__ float bf(const anima_bf16 *p, int i) {
 }
 
 // ---- ops: NIN streamed inputs, NOUT outputs (written over input buffers 0..NOUT-1),
-// NB fp32 broadcast vectors.
+// NB broadcast vectors (bf16 in shared memory, read through bvec8).
 
 struct LayerNormOp {  // layer_norm.cu:26-59
     static constexpr int NIN = 1, NOUT = 1, NB = 0;
@@ -263,8 +245,6 @@ struct AdaLNOp {
     __device__ anima_bf16 *dst(int) const { return out; }
     TembFold fold = {};
     static constexpr bool kFold = kTemb;
-    static constexpr bool kBfBc = !kTemb;     // bf16 staging (the fold needs its sums rounded first)
-    static constexpr unsigned kPlusOne = 1u;  // the reference's (1.0f + scale[d]), rounded to fp32
     __device__ const anima_bf16 *bvec(int i) const { return i == 0 ? scale : shift; }
     __device__ const anima_bf16 *btemb(int i) const { return i == 0 ? fold.tsc : fold.tsh; }
     template <int NW>
@@ -281,8 +261,8 @@ struct AdaLNOp {
         for (int k = 0; k < 8; ++k) {
             float f[8], sc[8], sh[8];
             unpack8(v[k], f);
-            bvec8<kBfBc>(bc, 0, D, seg, k, true, sc);
-            bvec8<kBfBc>(bc, 1, D, seg, k, false, sh);
+            bvec8(bc, 0, D, seg, k, true, sc);
+            bvec8(bc, 1, D, seg, k, false, sh);
             ln_modulate8<kRoundFirst>(f, mean, inv, sc, sh, f);
             slot[swz(8 * lane + k)] = pack8(f);
         }
@@ -300,8 +280,6 @@ struct ResGateAdaLNOp {  // layer_norm.cu:146-196
     __device__ anima_bf16 *dst(int o) const { return o == 0 ? hidden : normed; }
     TembFold fold = {};  // the gate is the previous set's, already summed
     static constexpr bool kFold = kTemb;
-    static constexpr bool kBfBc = !kTemb;
-    static constexpr unsigned kPlusOne = 2u;
     __device__ const anima_bf16 *bvec(int i) const { return i == 0 ? gate : (i == 1 ? scale : shift); }
     __device__ const anima_bf16 *btemb(int i) const { return i == 0 ? nullptr : (i == 1 ? fold.tsc : fold.tsh); }
     template <int NW>
@@ -315,7 +293,7 @@ struct ResGateAdaLNOp {  // layer_norm.cu:146-196
 #pragma unroll
         for (int k = 0; k < 8; ++k) {
             float g[8], fx[8], fy[8];
-            bvec8<kBfBc>(bc, 0, D, seg, k, false, g);
+            bvec8(bc, 0, D, seg, k, false, g);
             unpack8(x[k], fx);
             unpack8(y[k], fy);
 #pragma unroll
@@ -342,8 +320,8 @@ struct ResGateAdaLNOp {  // layer_norm.cu:146-196
             const Vec8 hb = pack8(h[k]);
             float f[8], sc[8], sh[8];
             unpack8(hb, f);
-            bvec8<kBfBc>(bc, 1, D, seg, k, true, sc);
-            bvec8<kBfBc>(bc, 2, D, seg, k, false, sh);
+            bvec8(bc, 1, D, seg, k, true, sc);
+            bvec8(bc, 2, D, seg, k, false, sh);
             ln_modulate8<false>(f, mean, inv, sc, sh, f);
             slot[swz(8 * lane + k)] = hb;
             slot[kUnitChunks + swz(8 * lane + k)] = pack8(f);
@@ -361,8 +339,6 @@ struct RmsOp {  // rms_norm.cu:9-67
     __device__ anima_bf16 *dst(int) const { return out; }
     TembFold fold = {};
     static constexpr bool kFold = false;
-    static constexpr bool kBfBc = true;
-    static constexpr unsigned kPlusOne = 0u;
     __device__ const anima_bf16 *bvec(int) const { return weight; }
     __device__ const anima_bf16 *btemb(int) const { return nullptr; }
     template <int NW>
@@ -378,7 +354,7 @@ struct RmsOp {  // rms_norm.cu:9-67
             unpack8(v[k], f);
             if constexpr (kWeight) {
                 float w[8];
-                bvec8<kBfBc>(bc, 0, D, seg, k, false, w);
+                bvec8(bc, 0, D, seg, k, false, w);
 #pragma unroll
                 for (int e = 0; e < 8; e += 2) {
                     const float2 o = __fmul2_rn(__fmul2_rn(f2(f[e], f[e + 1]), f2(r, r)), f2(w[e], w[e + 1]));
@@ -421,11 +397,12 @@ struct AdaRmsOp {  // adaln.cu:11-58 (per-row scale/shift streamed alongside x)
     }
 };
 
-// The op's NB broadcast vectors -> fp32 in shared memory (bc_pos layout), 1.0f added to those
-// in Op::kPlusOne. Split in two so that the row prefetch can be issued in between: the
-// vectors' 16-byte loads go out first (they hit L2 and must not queue behind megabytes of
-// rows), then the rows, then the conversion. Vectors that are not 16-byte aligned are read
-// with scalar loads in the second half.
+// The temb-fold ops' broadcast vectors (modulation + temb, rounded to bf16 as add_bf16 stores
+// them) -> bf16 chunks in shared memory, in the rows' swizzled layout. Split in two so that the
+// row prefetch can be issued in between: the vectors' 16-byte loads go out first (they hit L2
+// and must not queue behind megabytes of rows), then the rows, then the sums. Vectors that are
+// not 16-byte aligned are read with scalar loads in the second half. (The other ops copy their
+// vectors with cp.async; see row_seg.)
 template <class Op>
 struct BcastStage {
     static constexpr int kThreads = SegShape<Op::NIN>::kThreads;
@@ -468,24 +445,23 @@ struct BcastStage {
 #pragma unroll
                     for (int e = 0; e < 8; ++e) f[e] = add ? bf16_add(bf(src, 8 * c + e), bf(add, 8 * c + e)) : bf(src, 8 * c + e);
                 }
-                if ((Op::kPlusOne >> b) & 1u) {
-#pragma unroll
-                    for (int e = 0; e < 8; ++e) f[e] = 1.0f + f[e];
-                }
-                float4 *q = reinterpret_cast<float4 *>(bc + b * D);
-                q[bc_pos(8 * c) >> 2] = make_float4(f[0], f[1], f[2], f[3]);
-                q[bc_pos(8 * c + 4) >> 2] = make_float4(f[4], f[5], f[6], f[7]);
+                // bf16 chunks in the rows' swizzled layout (the values are bf16 already, so the
+                // packing is exact); the reference's 1.0f is added where they are read
+                reinterpret_cast<Vec8 *>(bc)[b * nch + swz(c)] = pack8(f);
             }
         }
     }
 };
 
-// Bytes per broadcast-vector element in shared memory: 2 for ops that stage them as bf16
-// (Op::kBfBc), 4 for the fp32 stage (the temb folds, whose sums are rounded on the way in).
+// Bytes per broadcast-vector element in shared memory (bf16 staging).
 template <class Op>
-__host__ __device__ constexpr int bc_bytes() {
-    if constexpr (Op::NB > 0) return Op::kBfBc ? 2 : 4;
-    return 4;
+__host__ __device__ constexpr int bc_bytes() { return 2; }
+
+// Whether the op folds temb into its broadcast vectors (ops without vectors have no kFold).
+template <class Op>
+__host__ __device__ constexpr bool op_folds() {
+    if constexpr (Op::NB > 0) return Op::kFold;
+    return false;
 }
 
 template <int NW, class Op>
@@ -525,7 +501,7 @@ __global__ void __launch_bounds__(SegShape<Op::NIN>::kThreads, SegShape<Op::NIN>
         }
         cp_async_commit();  // one group per unit, empty or not, keeps the counting uniform
     };
-    if constexpr (NB > 0 && bc_bytes<Op>() == 2) {
+    if constexpr (NB > 0 && !op_folds<Op>()) {
         // the vectors as bf16 chunks, swizzled like a unit, in the same copy group as the first
         // unit: no conversion pass, and half the shared-memory reads per row of an fp32 stage
         const int nch = D >> 3;
