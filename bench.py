@@ -358,14 +358,32 @@ class ClockSampler:
     def __init__(self, gpu_index):
         self.gpu = gpu_index
         self.proc = None
+        self.lines = []
+        self.reader = None
 
-    def start(self):
+    def start(self, ready_timeout=10.0):
+        """Start sampling and wait (bounded) for the first sample, so that a slow nvidia-smi
+        start-up on a fresh box cannot leave a short timed region without samples."""
+        import threading
+
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
                  "-lms", "20"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except OSError:
             self.proc = None
+            return
+        self.lines = []
+
+        def read(stream, sink):
+            for line in stream:
+                sink.append(line)
+
+        self.reader = threading.Thread(target=read, args=(self.proc.stdout, self.lines), daemon=True)
+        self.reader.start()
+        deadline = time.time() + ready_timeout
+        while not self.lines and self.proc.poll() is None and time.time() < deadline:
+            time.sleep(0.02)
 
     def mark(self):
         """Wall-clock bounds of the timed region (samples outside it are dropped)."""
@@ -380,10 +398,13 @@ class ClockSampler:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"], "samples": 0}
         self.proc.terminate()
         try:
-            out, _ = self.proc.communicate(timeout=5)
+            self.proc.wait(timeout=5)
         except subprocess.TimeoutExpired:
             self.proc.kill()
-            out, _ = self.proc.communicate()
+            self.proc.wait()
+        if self.reader is not None:
+            self.reader.join(timeout=5)
+        out = "".join(self.lines)
         sm, mx, reasons, power = [], [], set(), []
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         for line in out.strip().splitlines():
@@ -1085,8 +1106,7 @@ def main():
     except Exception:
         smi_id = str(local_rank)
     clocks = ClockSampler(smi_id)
-    clocks.start()
-    time.sleep(0.3)  # let nvidia-smi start sampling
+    clocks.start()  # returns once nvidia-smi has produced its first sample
     if dist is not None:
         dist.barrier()
     torch.cuda.synchronize()
