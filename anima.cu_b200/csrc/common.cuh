@@ -50,6 +50,23 @@ __device__ __forceinline__ void st_vec(void *p, const Vec8 &v) {
 __device__ __forceinline__ float bf_lo(uint32_t w) { return __uint_as_float(w << 16); }
 __device__ __forceinline__ float bf_hi(uint32_t w) { return __uint_as_float(w & 0xffff0000u); }
 
+// x / D for a compile-time power of two D: the exact quotient equals x * 2^-k, so the
+// correctly rounded product is the correctly rounded quotient (IEEE round-to-nearest, also
+// for subnormal results), one multiply instead of the division sequence.
+template <int D>
+__device__ __forceinline__ float div_pow2(float x) {
+    static_assert(D > 0 && (D & (D - 1)) == 0, "D must be a power of two");
+    return __fmul_rn(x, 1.0f / (float)D);
+}
+
+// Pair sums of squares fmaf(b, b, a * a) (the reference's a*a + b*b as nvcc contracts it)
+// for the bf16 pairs in words w0 and w1, on packed fp32x2 ops: each lane rounds as the
+// scalar op does, at half the issue cost.
+__device__ __forceinline__ float2 sq_pair2(uint32_t w0, uint32_t w1) {
+    const float2 a = make_float2(bf_lo(w0), bf_lo(w1)), b = make_float2(bf_hi(w0), bf_hi(w1));
+    return __ffma2_rn(b, b, __fmul2_rn(a, a));
+}
+
 // Round two floats to a packed bf16 pair (RNE), like __floats2bfloat162_rn.
 __device__ __forceinline__ uint32_t pack_bf2(float lo, float hi) {
     __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);

@@ -114,6 +114,7 @@ __global__ void __launch_bounds__(kEwBlock) ew_kernel(EwArgs a, Op op) {
         const int64_t nch = a.n >> 3;
         done = nch << 3;
         const uint32_t dch = NB ? (uint32_t)(a.D >> 3) : 1u;
+        const uint32_t cstep = NB ? (uint32_t)kEwBlock % dch : 0u;  // < dch
         // one group of U * kEwBlock consecutive chunks per CTA, chunk u of a thread at
         // threadIdx.x + u * kEwBlock (coalesced); the grid normally covers every group once
         for (int64_t base = (int64_t)blockIdx.x * kEwBlock * U + threadIdx.x; base < nch;
@@ -127,6 +128,12 @@ __global__ void __launch_bounds__(kEwBlock) ew_kernel(EwArgs a, Op op) {
                     if constexpr (NS > 1) in[u][NS - 1] = ld_stream(a.s1 + i * 8);
                 }
             }
+            // column chunk of the thread's first chunk: one division per group (32-bit below
+            // 2^32 chunks), then advanced by kEwBlock with one compare-subtract per chunk. A
+            // 64-bit modulo per chunk had cost ~60 instructions of ~110 per chunk.
+            uint32_t c = 0;
+            if constexpr (NB > 0)
+                c = base < 4294967296ll ? (uint32_t)base % dch : (uint32_t)((uint64_t)base % dch);
 #pragma unroll
             for (int u = 0; u < U; ++u) {
                 const int64_t i = base + u * kEwBlock;
@@ -135,11 +142,10 @@ __global__ void __launch_bounds__(kEwBlock) ew_kernel(EwArgs a, Op op) {
                 unpack8(in[u][0], f0);
                 if constexpr (NS > 1) unpack8(in[u][NS - 1], f1);
                 if constexpr (NB > 0) {
-                    // column chunk of this chunk; chunk counts stay below 2^32 for any
-                    // tensor that fits in memory at 8 elements per chunk x 2 bytes
-                    const uint32_t c = (uint32_t)((uint64_t)i % dch);
                     unpack8(ld_cached(a.b0 + (int64_t)c * 8), g0);
                     if constexpr (NB > 1) unpack8(ld_cached(a.b1 + (int64_t)c * 8), g1);
+                    c += cstep;
+                    if (c >= dch) c -= dch;
                 }
                 float r[8];
 #pragma unroll

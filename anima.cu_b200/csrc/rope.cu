@@ -222,7 +222,7 @@ struct QkArgs {
 };
 
 // kNarrow (heads < 2^32): token and table row by 32-bit division. A compile-time choice: with
-// a run-time flag the unused 64-bit path cost 0.6 us per launch at [8192 x 16, 128].
+// a run-time flag the unused 64-bit path cost 0.7 us per launch at [8192 x 16, 128].
 template <bool kNarrow>
 __global__ void __launch_bounds__(kRopeBlock) qk_norm_rope_128(QkArgs a) {
     pdl_wait();
@@ -248,12 +248,13 @@ __global__ void __launch_bounds__(kRopeBlock) qk_norm_rope_128(QkArgs a) {
 #pragma unroll
     for (int k = 0; k < K; ++k)
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            const float lo = bf_lo(v[k].w[j]), hi = bf_hi(v[k].w[j]);
-            q[k][j] = __fmaf_rn(hi, hi, lo * lo);
+        for (int j = 0; j < 4; j += 2) {
+            const float2 t = sq_pair2(v[k].w[j], v[k].w[j + 1]);
+            q[k][j] = t.x;
+            q[k][j + 1] = t.y;
         }
     const float sq = ref_pair_tree_sum<LPR, K>(q, l, 0xffffffffu);
-    const float r = rsqrtf(__fdiv_rn(sq, (float)HD) + a.eps);
+    const float r = rsqrtf(div_pow2<HD>(sq) + a.eps);
     pdl_launch();
     if (!live) return;
     // rms_norm.cu:62-64 ((x*r)*w, stored as bf16) then rope.cu:101-107, on element pairs with
@@ -327,11 +328,12 @@ __global__ void __launch_bounds__(kRopeBlock) head_norm_rope_128(HeadArgs a) {
 #pragma unroll
     for (int k = 0; k < K; ++k)
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            const float lo = bf_lo(v[k].w[j]), hi = bf_hi(v[k].w[j]);
-            q[k][j] = fmaf(hi, hi, lo * lo);
+        for (int j = 0; j < 4; j += 2) {
+            const float2 t = sq_pair2(v[k].w[j], v[k].w[j + 1]);
+            q[k][j] = t.x;
+            q[k][j + 1] = t.y;
         }
-    const float r = rsqrtf(__fdiv_rn(ref_pair_tree_sum<LPR, K>(q, l, 0xffffffffu), (float)HD) + a.eps);
+    const float r = rsqrtf(div_pow2<HD>(ref_pair_tree_sum<LPR, K>(q, l, 0xffffffffu)) + a.eps);
     pdl_launch();
     if (!live) return;
     // rms_norm.cu:62-64: (x * r) * w, stored as bf16
