@@ -105,6 +105,8 @@ def _load() -> ctypes.CDLL:
     lib.anima_version.restype = c_char_p
     lib.anima_compat_last_error.argtypes = []
     lib.anima_compat_last_error.restype = c_int
+    lib.anima_wait_timeouts.argtypes = [ctypes.POINTER(ctypes.c_uint), c_int]
+    lib.anima_wait_timeouts.restype = c_int
     return lib
 
 
@@ -117,6 +119,16 @@ def version() -> str:
 
 def status_string(status: int) -> str:
     return lib.anima_status_string(status).decode()
+
+
+def wait_timeouts(reset: bool = False) -> int:
+    """Bounded device waits that ran out on the current device (anima_wait_timeouts); 0 in
+    normal operation. Synchronize the streams that ran the kernels first."""
+    n = ctypes.c_uint(0)
+    st = lib.anima_wait_timeouts(ctypes.byref(n), 1 if reset else 0)
+    if st != ANIMA_OK:
+        raise AnimaError("anima_wait_timeouts", st, status_string(st))
+    return int(n.value)
 
 
 def call(name: str, *args) -> None:

@@ -3,7 +3,10 @@
 #include <mutex>
 #include <vector>
 
+#include <cudaTypedefs.h>
+
 #include "common.cuh"
+#include "tma.cuh"
 
 namespace anima {
 
@@ -76,6 +79,37 @@ int resident_ctas(const void *kernel, int block, int smem, int *err) {
     std::lock_guard<std::mutex> lock(g_occ_mu);
     g_occ.push_back(OccEntry{dev, kernel, block, smem, n});
     return n;
+}
+
+namespace {
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no libcuda link), looked up
+// once per process.
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = []() -> PFN_cuTensorMapEncodeTiled_v12000 {
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) != cudaSuccess ||
+            q != cudaDriverEntryPointSuccess) {
+            cudaGetLastError();
+            return nullptr;
+        }
+        return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    }();
+    return fn;
+}
+}  // namespace
+
+bool encode_bf16_map_3d(CUtensorMap *map, const void *base, uint64_t d0, uint64_t d1, uint64_t d2, uint64_t s1,
+                        uint64_t s2, uint32_t b0, uint32_t b1) {
+    PFN_cuTensorMapEncodeTiled_v12000 encode = tensor_map_encoder();
+    if (!encode) return false;
+    const cuuint64_t dims[3] = {d0, d1, d2};
+    const cuuint64_t strides[2] = {s1, s2};
+    const cuuint32_t box[3] = {b0, b1, 1};
+    const cuuint32_t elem[3] = {1, 1, 1};
+    return encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void *>(base), dims, strides, box, elem,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
 unsigned wave_grid(const void *kernel, int block, int smem, int64_t work, int *err) {

@@ -23,6 +23,9 @@
 // the measured peak), fused with SiLU 124 against 141 us.
 //
 // When the tiles are few, channel_norm_cluster (below) spreads each over a cluster of CTAs.
+// Where it measured faster (the fused SiLU at C <= 512, the norm alone at C = 512),
+// channel_norm_tma stages the tile with TMA bulk tensor loads, one per 64 channels on its own
+// mbarrier, so the chain starts while the rest of the tile is still arriving.
 //
 // The conv-bias form (kBias) first adds the convolution's bias[c] to the staged tile in place,
 // rounded to bf16 as the reference's bias launch stores it (causal_conv3d.cu:187-195); the
@@ -33,6 +36,7 @@
 // arithmetic, one launch for all batch items.
 #include "common.cuh"
 #include "activation.cuh"
+#include "tma.cuh"
 
 #include <cooperative_groups.h>
 
@@ -268,6 +272,130 @@ __global__ void __launch_bounds__(T) channel_norm_tile(CnArgs a) {
     }
 }
 
+// The TMA tile kernel's shapes (pixels per tile, threads, channels per load group), chosen by
+// kernel experiments at the VAE decoder's shapes against the cp.async tile kernel: with the
+// SiLU epilogue it won at C = 128, 256 and 512 (105.3 against 110.6 us at [128, 1024^2],
+// 60.6 against 64.9 at [256, 512^2], 43.1 against 47.9 at [512, 256^2]); the norm alone only
+// at C = 512 (32.0 against 33.6 us at [512, 256^2]), elsewhere it tied. P = 0: not used.
+struct CnTmaShape {
+    int P, T, CG, id;
+};
+inline CnTmaShape cn_tma_shape(int C, bool silu) {
+    if (silu) {
+        if (C <= 128) return {64, 128, 64, 0};
+        if (C <= 256) return {64, 256, 64, 1};
+        if (C <= 512) return {32, 256, 64, 2};
+        return {0, 0, 64, 0};
+    }
+    if (C > 256 && C <= 512) return {64, 256, 64, 1};
+    return {0, 0, 64, 0};
+}
+
+// Waits of the TMA tile kernel that ran out (never expected; read by anima_wait_timeouts).
+__device__ unsigned int g_cn_wait_timeouts;
+
+// The tile kernel with the tile staged by the TMA unit: one 3-D bulk tensor load per group of
+// CG channels ([CG][P] boxes of the [B][C][spatial] tensor, this GPU's memory, no multicast),
+// each completing on its own mbarrier. The P/2 chain lanes start on the first group as soon as
+// it lands and wait for each next group only when they reach it, so the serial per-pixel chain
+// runs while the rest of the tile is still arriving, and no thread spends issue slots on
+// per-chunk copy addresses. Same chain order, epilogue and rounding as channel_norm_tile.
+// Shared memory: the tile [C][P] at a 1024-byte boundary, gamma fp32 [C], rms [P], barriers.
+template <int P, int T, bool kSilu, bool kPixel, int CG>
+__global__ void __launch_bounds__(T) channel_norm_tma(const __grid_constant__ CUtensorMap xmap, CnArgs a) {
+    constexpr int kVecs = P / 8;
+    extern __shared__ unsigned char cn_raw[];
+    unsigned char *base = reinterpret_cast<unsigned char *>((reinterpret_cast<uintptr_t>(cn_raw) + 1023) & ~uintptr_t(1023));
+    anima_bf16 *tile = reinterpret_cast<anima_bf16 *>(base);                   // [C][P]
+    float *gam = reinterpret_cast<float *>(base + (size_t)a.C * P * 2);        // [C]
+    float *rms_s = gam + ((a.C + 3) & ~3);                                      // [P]
+    uint64_t *bars = reinterpret_cast<uint64_t *>(rms_s + P);                  // [C / CG]
+    const int groups = a.C / CG;
+    const int b = blockIdx.x / a.tiles_per_image;
+    const int s_tile = (blockIdx.x - b * a.tiles_per_image) * P;
+    const int live_vecs = min(P, a.spatial - s_tile) / 8;  // spatial % 8 == 0
+    const int64_t img = (int64_t)b * a.C * a.spatial;
+    if (threadIdx.x == 0) {
+        for (int g = 0; g < groups; ++g) mbar_init(&bars[g], 1);
+        mbar_fence_init();
+    }
+    __syncthreads();
+    pdl_wait();
+    if (threadIdx.x == 0) {
+        for (int g = 0; g < groups; ++g) {
+            mbar_arrive_expect_tx(&bars[g], (uint32_t)(CG * P * 2));  // out-of-range pixels arrive as zeros
+            tma_load_3d(tile + (size_t)g * CG * P, &xmap, s_tile, g * CG, b, &bars[g]);
+        }
+    }
+    if constexpr (!kPixel) {
+        for (int c = threadIdx.x; c < a.C; c += T) gam[c] = ldb(a.gamma + c);
+    }
+    bool ok = true;
+    // vae_kernels.cu:68-74 as in channel_norm_tile: lane t walks pixels 2t, 2t+1 over the channels
+    // in order, one packed fma per channel, the next 8 channels' loads ahead within a group.
+    if (threadIdx.x < P / 2) {
+        const uint32_t *col = reinterpret_cast<const uint32_t *>(tile) + threadIdx.x;
+        float2 q2 = make_float2(0.0f, 0.0f);
+        for (int g = 0; g < groups; ++g) {
+            ok = mbar_wait(&bars[g], 0) && ok;
+            const int c0 = g * CG, c1 = c0 + CG;
+            uint32_t cur[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) cur[j] = col[(c0 + j) * (P / 2)];
+            for (int c = c0; c < c1; c += 8) {
+                uint32_t nxt[8];
+                const bool more = c + 8 < c1;
+                if (more) {
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) nxt[j] = col[(c + 8 + j) * (P / 2)];
+                }
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                    const float2 f = make_float2(bf_lo(cur[j]), bf_hi(cur[j]));
+                    q2 = __ffma2_rn(f, f, q2);
+                }
+                if (more) {
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) cur[j] = nxt[j];
+                }
+            }
+        }
+        reinterpret_cast<float2 *>(rms_s)[threadIdx.x] =
+            make_float2(norm_scale<kPixel>(q2.x, a.C, a.eps), norm_scale<kPixel>(q2.y, a.C, a.eps));
+    }
+    __syncthreads();
+    // every thread observes the completed groups before reading the tile (completed phases
+    // return at once)
+    for (int g = 0; g < groups; ++g) ok = mbar_wait(&bars[g], 0) && ok;
+    if (!ok) atomicAdd(&g_cn_wait_timeouts, 1u);
+    pdl_launch();
+    if (!ok) return;
+
+    const int v = threadIdx.x % kVecs;
+    if (v >= live_vecs) return;
+    float r[8];
+    {
+        const float4 r0 = reinterpret_cast<const float4 *>(rms_s)[2 * v];
+        const float4 r1 = reinterpret_cast<const float4 *>(rms_s)[2 * v + 1];
+        r[0] = r0.x; r[1] = r0.y; r[2] = r0.z; r[3] = r0.w;
+        r[4] = r1.x; r[5] = r1.y; r[6] = r1.z; r[7] = r1.w;
+    }
+    anima_bf16 *dst = a.out + img + s_tile + v * 8;
+    for (int c = threadIdx.x / kVecs; c < a.C; c += T / kVecs) {
+        const Vec8 xv = *reinterpret_cast<const Vec8 *>(tile + c * P + v * 8);
+        const float gm = kPixel ? 1.0f : gam[c];
+        Vec8 o;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const float2 t2 = __fmul2_rn(make_float2(bf_lo(xv.w[j]), bf_hi(xv.w[j])), make_float2(r[2 * j], r[2 * j + 1]));
+            const float2 u = __fmul2_rn(t2, make_float2(gm, gm));
+            o.w[j] = pack_bf2(u.x, u.y);
+        }
+        if constexpr (kSilu) o = fast_chunk<SiluF>(o);
+        st_vec(dst + (int64_t)c * a.spatial, o);
+    }
+}
+
 // Cluster variant: a 64-pixel tile is spread over a cluster of kCnCluster CTAs, CTA r staging
 // channels [r*Cq, (r+1)*Cq) (Cq = ceil(C / kCnCluster)) into its own shared memory, so loading
 // and the epilogue run on kCnCluster times more threads -- what the small VAE shapes (few tiles
@@ -420,8 +548,39 @@ int channel_norm(const anima_bf16 *x, const anima_bf16 *gamma, anima_bf16 *out, 
     // epilogue needs the threads). Many tiles keep every SM busy already, and the cluster's
     // hand-offs would then only serialise each tile (measured); the norm alone runs the tile
     // kernel at every size (13.0 against 14.7 us on the cluster at [512, 128^2]).
-    if (kSilu && spatial % 8 == 0 && aligned16(x) && aligned16(out) && C >= 64 &&
-        (int64_t)Cq * per_ch <= kCnMaxSmem && cl_tiles <= 2 * (int64_t)sm_count()) {
+    const bool cluster = kSilu && spatial % 8 == 0 && aligned16(x) && aligned16(out) && C >= 64 &&
+                         (int64_t)Cq * per_ch <= kCnMaxSmem && cl_tiles <= 2 * (int64_t)sm_count();
+    // The TMA tile kernel where it measured faster than the cp.async one (see cn_tma_shape);
+    // the conv-bias form keeps cp.async (its bias pass needs the whole tile before the chain).
+    const CnTmaShape tshape = cn_tma_shape(C, kSilu);
+    if (!kBias && !cluster && tshape.P > 0 && spatial % 8 == 0 && aligned16(x) && aligned16(out) &&
+        C % tshape.CG == 0 && (int64_t)B * ((spatial + tshape.P - 1) / tshape.P) < 2147483647) {
+        CUtensorMap xmap;
+        if (encode_bf16_map_3d(&xmap, x, (uint64_t)spatial, (uint64_t)C, (uint64_t)B, (uint64_t)spatial * 2,
+                               (uint64_t)C * spatial * 2, (uint32_t)tshape.P, (uint32_t)tshape.CG)) {
+            a.tiles_per_image = (spatial + tshape.P - 1) / tshape.P;
+            const int64_t tsmem = 1024 + (int64_t)C * tshape.P * 2 + (int64_t)((C + 3) & ~3) * 4 + tshape.P * 4 +
+                                  (int64_t)(C / tshape.CG) * 8;
+            if (tsmem <= kCnMaxSmem + 4096) {
+                const unsigned grid = (unsigned)((int64_t)B * a.tiles_per_image);
+                const int form = kPixel ? 2 : kSilu ? 1 : 0;
+                const int slot = 44 + 3 * tshape.id + form;
+#define ANIMA_CN_TMA(Pv, Tv, CGv)                                                                          \
+    {                                                                                                      \
+        auto kern = channel_norm_tma<Pv, Tv, kSilu, kPixel, CGv>;                                          \
+        if (int e = allow_dynamic_smem((const void *)kern, kCnMaxSmem + 4096, slot)) return e;            \
+        launch(kern, grid, Tv, (size_t)tsmem, stream, xmap, a);                                            \
+    }
+                if (tshape.id == 0) ANIMA_CN_TMA(64, 128, 64)
+                else if (tshape.id == 1) ANIMA_CN_TMA(64, 256, 64)
+                else ANIMA_CN_TMA(32, 256, 64)
+#undef ANIMA_CN_TMA
+                return launch_status();
+            }
+        }
+        a.tiles_per_image = (spatial + P - 1) / P;
+    }
+    if (cluster) {
         a.tiles_per_image = (spatial + kCnPix - 1) / kCnPix;
         auto kern = channel_norm_cluster<kSilu, kBias, kPixel>;
         if (int e = allow_dynamic_smem((const void *)kern, kCnMaxSmem, kPixel ? 13 : kBias ? 7 : kSilu ? 5 : 4)) return e;
@@ -481,4 +640,14 @@ extern "C" int anima_conv_bias_rms_norm_channel_silu_bf16(const anima_bf16 *x, c
 extern "C" int anima_pixel_norm_bf16(const anima_bf16 *x, anima_bf16 *out, int B, int C, int spatial, float eps,
                                      anima_stream_t stream) {
     return channel_norm<false, false, true>(x, nullptr, out, B, C, spatial, eps, stream);
+}
+
+extern "C" int anima_wait_timeouts(unsigned int *count, int reset) {
+    if (!count) return ANIMA_ERR_NULL_POINTER;
+    cudaError_t e = cudaMemcpyFromSymbol(count, g_cn_wait_timeouts, sizeof(unsigned int));
+    if (e == cudaSuccess && reset) {
+        const unsigned int zero = 0;
+        e = cudaMemcpyToSymbol(g_cn_wait_timeouts, &zero, sizeof(unsigned int));
+    }
+    return e == cudaSuccess ? ANIMA_OK : (int)e;
 }

@@ -51,6 +51,14 @@ ANIMA_API const char *anima_status_string(int status);
 /* Library version, e.g. "anima_b200 0.1.0 sm_100a". */
 ANIMA_API const char *anima_version(void);
 
+/* Bounded waits that ran out on the current device: the kernels that stage data with the TMA
+ * unit (the channel norm's tile kernel) wait on mbarriers with an iteration limit instead of
+ * forever; a CTA whose wait runs out skips its output and counts here. Never expected in
+ * normal operation. Writes the count to *count (and clears it when reset != 0); call after
+ * synchronizing the streams that ran those kernels. New in this library (the reference's
+ * kernels have no waits). */
+ANIMA_API int anima_wait_timeouts(unsigned int *count, int reset);
+
 /* ------------------------------------------------------------------ row norms */
 
 /* out[n,:] = x[n,:] * rsqrt(mean(x[n,:]^2) + eps) * weight[:]; weight may be NULL.

@@ -518,7 +518,7 @@ def test_embedding_lookup_bad_ids(anima, rng, D):
 # ---------------------------------------------------------------- VAE channel norm
 @pytest.mark.parametrize("B,C,H,W", [(1, 512, 32, 32), (2, 96, 16, 16), (1, 128, 8, 12), (1, 100, 5, 7),
                                      (3, 16, 4, 4), (1, 1536, 8, 8), (2, 100, 5, 8), (1, 3, 16, 16),
-                                     (1, 4000, 2, 4), (1, 64, 160, 160), (1, 65, 8, 8)])
+                                     (1, 4000, 2, 4), (1, 64, 160, 160), (1, 65, 8, 8), (2, 512, 10, 12)])
 def test_rms_norm_channel(anima, ref, rng, B, C, H, W):
     sp = H * W
     x, g = O.randn_bf16(rng, (B, C, sp)), _weight(rng, C)
@@ -536,7 +536,7 @@ def test_rms_norm_channel(anima, ref, rng, B, C, H, W):
 
 
 @pytest.mark.parametrize("B,C,H,W", [(1, 512, 32, 32), (1, 96, 10, 10), (2, 100, 5, 8), (1, 64, 160, 160),
-                                     (2, 128, 64, 64)])
+                                     (2, 128, 64, 64), (2, 512, 10, 12)])
 def test_pixel_norm(anima, ref, rng, B, C, H, W):
     """vae_kernels.cu:15-52 through each channel-norm kernel: cluster (few tiles), tile (many),
     per-pixel (spatial % 8 != 0)."""
@@ -556,8 +556,11 @@ def test_pixel_norm(anima, ref, rng, B, C, H, W):
 
 
 @pytest.mark.parametrize("B,C,H,W", [(1, 512, 32, 32), (1, 96, 10, 10), (2, 100, 5, 8), (1, 256, 64, 64),
-                                     (1, 64, 160, 160)])
+                                     (1, 64, 160, 160), (1, 128, 150, 132), (2, 256, 100, 104),
+                                     (1, 512, 150, 132)])
 def test_rms_norm_channel_silu_matches_reference_chain(anima, ref, rng, B, C, H, W):
+    """Through the cluster kernel (few tiles) and the TMA tile kernel (many tiles; the last
+    three shapes end in a partial tile, which the TMA loads fill with zeros)."""
     sp = H * W
     x, g = O.randn_bf16(rng, (B, C, sp)), _weight(rng, C)
     dx, dg = dev(x), dev(g)
@@ -568,6 +571,7 @@ def test_rms_norm_channel_silu_matches_reference_chain(anima, ref, rng, B, C, H,
     ref.silu_bf16(r.data_ptr(), r.data_ptr(), B * C * sp, stream_ptr())
     torch.cuda.synchronize()
     assert_bit_exact(host(out), host(r), "rms_norm_channel_silu vs rms_norm_channel + silu")
+    assert anima.wait_timeouts() == 0
 
 
 # ---------------------------------------------------------------- fused LN + modulate
