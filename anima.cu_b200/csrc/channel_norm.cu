@@ -280,14 +280,15 @@ __global__ void __launch_bounds__(T) channel_norm_tile(CnArgs a) {
 struct CnTmaShape {
     int P, T, CG, id;
 };
-inline CnTmaShape cn_tma_shape(int C, bool silu) {
+inline CnTmaShape cn_tma_shape(int C, bool silu, bool few_tiles) {
     if (silu) {
         if (C <= 128) return {64, 128, 64, 0};
         if (C <= 256) return {64, 256, 64, 1};
         if (C <= 512) return {32, 256, 64, 2};
         return {0, 0, 64, 0};
     }
-    if (C > 256 && C <= 512) return {64, 256, 64, 1};
+    // at most ~2 tiles per SM: 512 threads per tile (10.5 against 12.2 us at [512, 128^2])
+    if (C > 256 && C <= 512) return few_tiles ? CnTmaShape{64, 512, 64, 3} : CnTmaShape{64, 256, 64, 1};
     return {0, 0, 64, 0};
 }
 
@@ -301,7 +302,7 @@ __device__ unsigned int g_cn_wait_timeouts;
 // runs while the rest of the tile is still arriving, and no thread spends issue slots on
 // per-chunk copy addresses. Same chain order, epilogue and rounding as channel_norm_tile.
 // Shared memory: the tile [C][P] at a 1024-byte boundary, gamma fp32 [C], rms [P], barriers.
-template <int P, int T, bool kSilu, bool kPixel, int CG>
+template <int P, int T, bool kSilu, bool kBias, bool kPixel, int CG>
 __global__ void __launch_bounds__(T) channel_norm_tma(const __grid_constant__ CUtensorMap xmap, CnArgs a) {
     constexpr int kVecs = P / 8;
     extern __shared__ unsigned char cn_raw[];
@@ -311,6 +312,7 @@ __global__ void __launch_bounds__(T) channel_norm_tma(const __grid_constant__ CU
     float *rms_s = gam + ((a.C + 3) & ~3);                                      // [P]
     uint64_t *bars = reinterpret_cast<uint64_t *>(rms_s + P);                  // [C / CG]
     const int groups = a.C / CG;
+    uint32_t *bias_s = reinterpret_cast<uint32_t *>(bars + groups);            // [C] (b, b) pairs (kBias)
     const int b = blockIdx.x / a.tiles_per_image;
     const int s_tile = (blockIdx.x - b * a.tiles_per_image) * P;
     const int live_vecs = min(P, a.spatial - s_tile) / 8;  // spatial % 8 == 0
@@ -329,6 +331,13 @@ __global__ void __launch_bounds__(T) channel_norm_tma(const __grid_constant__ CU
     }
     if constexpr (!kPixel) {
         for (int c = threadIdx.x; c < a.C; c += T) gam[c] = ldb(a.gamma + c);
+    }
+    if constexpr (kBias) {
+        // the conv bias is added to each value where it is read (the chain, the epilogue), with
+        // the in-place pass's rounding (add_bias8), so no pass over the whole tile precedes the
+        // chain and the chain can still start on the first group
+        for (int c = threadIdx.x; c < a.C; c += T) bias_s[c] = bias_pair(a.bias + c);
+        __syncthreads();
     }
     bool ok = true;
     // vae_kernels.cu:68-74 as in channel_norm_tile: lane t walks pixels 2t, 2t+1 over the channels
@@ -351,7 +360,9 @@ __global__ void __launch_bounds__(T) channel_norm_tma(const __grid_constant__ CU
                 }
 #pragma unroll
                 for (int j = 0; j < 8; ++j) {
-                    const float2 f = make_float2(bf_lo(cur[j]), bf_hi(cur[j]));
+                    uint32_t w = cur[j];
+                    if constexpr (kBias) asm("add.rn.bf16x2 %0, %0, %1;" : "+r"(w) : "r"(bias_s[c + j]));
+                    const float2 f = make_float2(bf_lo(w), bf_hi(w));
                     q2 = __ffma2_rn(f, f, q2);
                 }
                 if (more) {
@@ -382,7 +393,12 @@ __global__ void __launch_bounds__(T) channel_norm_tma(const __grid_constant__ CU
     }
     anima_bf16 *dst = a.out + img + s_tile + v * 8;
     for (int c = threadIdx.x / kVecs; c < a.C; c += T / kVecs) {
-        const Vec8 xv = *reinterpret_cast<const Vec8 *>(tile + c * P + v * 8);
+        Vec8 xv = *reinterpret_cast<const Vec8 *>(tile + c * P + v * 8);
+        if constexpr (kBias) {
+            const uint32_t b2 = bias_s[c];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) asm("add.rn.bf16x2 %0, %0, %1;" : "+r"(xv.w[j]) : "r"(b2));
+        }
         const float gm = kPixel ? 1.0f : gam[c];
         Vec8 o;
 #pragma unroll
@@ -550,30 +566,39 @@ int channel_norm(const anima_bf16 *x, const anima_bf16 *gamma, anima_bf16 *out, 
     // kernel at every size (13.0 against 14.7 us on the cluster at [512, 128^2]).
     const bool cluster = kSilu && spatial % 8 == 0 && aligned16(x) && aligned16(out) && C >= 64 &&
                          (int64_t)Cq * per_ch <= kCnMaxSmem && cl_tiles <= 2 * (int64_t)sm_count();
-    // The TMA tile kernel where it measured faster than the cp.async one (see cn_tma_shape);
-    // the conv-bias form keeps cp.async (its bias pass needs the whole tile before the chain).
-    const CnTmaShape tshape = cn_tma_shape(C, kSilu);
-    if (!kBias && !cluster && tshape.P > 0 && spatial % 8 == 0 && aligned16(x) && aligned16(out) &&
+    // The TMA tile kernel where it measured faster than the cp.async one (see cn_tma_shape).
+    const bool few_tiles = cl_tiles <= 2 * (int64_t)sm_count();
+    // Few tiles, large tensor, C in (256, 512]: the fused SiLU forms run the TMA norm (512
+    // threads per tile) and then the SiLU table kernel in place, 14 us against 17 us for the
+    // one-launch cluster kernel at [512, 128^2]: with 1.7 tiles per SM the fused epilogue's
+    // decided-path SiLU runs on too few warps, the table kernel on every SM. Same bits.
+    if (kSilu && !kPixel && cluster && C > 256 && C <= 512 && C % 64 == 0 && n >= (int64_t)1 << 22) {
+        if (int e = channel_norm<false, kBias, kPixel>(x, gamma, out, B, C, spatial, eps, stream, bias)) return e;
+        return anima_silu_bf16(out, out, n, stream);
+    }
+    const CnTmaShape tshape = cn_tma_shape(C, kSilu, few_tiles);
+    if (!cluster && tshape.P > 0 && spatial % 8 == 0 && aligned16(x) && aligned16(out) &&
         C % tshape.CG == 0 && (int64_t)B * ((spatial + tshape.P - 1) / tshape.P) < 2147483647) {
         CUtensorMap xmap;
         if (encode_bf16_map_3d(&xmap, x, (uint64_t)spatial, (uint64_t)C, (uint64_t)B, (uint64_t)spatial * 2,
                                (uint64_t)C * spatial * 2, (uint32_t)tshape.P, (uint32_t)tshape.CG)) {
             a.tiles_per_image = (spatial + tshape.P - 1) / tshape.P;
             const int64_t tsmem = 1024 + (int64_t)C * tshape.P * 2 + (int64_t)((C + 3) & ~3) * 4 + tshape.P * 4 +
-                                  (int64_t)(C / tshape.CG) * 8;
+                                  (int64_t)(C / tshape.CG) * 8 + (kBias ? (int64_t)C * 4 : 0);
             if (tsmem <= kCnMaxSmem + 4096) {
                 const unsigned grid = (unsigned)((int64_t)B * a.tiles_per_image);
-                const int form = kPixel ? 2 : kSilu ? 1 : 0;
-                const int slot = 44 + 3 * tshape.id + form;
+                const int form = kPixel ? 3 : kBias ? 2 : kSilu ? 1 : 0;
+                const int slot = 44 + 4 * tshape.id + form;
 #define ANIMA_CN_TMA(Pv, Tv, CGv)                                                                          \
     {                                                                                                      \
-        auto kern = channel_norm_tma<Pv, Tv, kSilu, kPixel, CGv>;                                          \
+        auto kern = channel_norm_tma<Pv, Tv, kSilu, kBias, kPixel, CGv>;                                   \
         if (int e = allow_dynamic_smem((const void *)kern, kCnMaxSmem + 4096, slot)) return e;            \
         launch(kern, grid, Tv, (size_t)tsmem, stream, xmap, a);                                            \
     }
                 if (tshape.id == 0) ANIMA_CN_TMA(64, 128, 64)
                 else if (tshape.id == 1) ANIMA_CN_TMA(64, 256, 64)
-                else ANIMA_CN_TMA(32, 256, 64)
+                else if (tshape.id == 2) ANIMA_CN_TMA(32, 256, 64)
+                else ANIMA_CN_TMA(64, 512, 64)
 #undef ANIMA_CN_TMA
                 return launch_status();
             }

@@ -557,10 +557,11 @@ def test_pixel_norm(anima, ref, rng, B, C, H, W):
 
 @pytest.mark.parametrize("B,C,H,W", [(1, 512, 32, 32), (1, 96, 10, 10), (2, 100, 5, 8), (1, 256, 64, 64),
                                      (1, 64, 160, 160), (1, 128, 150, 132), (2, 256, 100, 104),
-                                     (1, 512, 150, 132)])
+                                     (1, 512, 150, 132), (1, 512, 96, 96)])
 def test_rms_norm_channel_silu_matches_reference_chain(anima, ref, rng, B, C, H, W):
-    """Through the cluster kernel (few tiles) and the TMA tile kernel (many tiles; the last
-    three shapes end in a partial tile, which the TMA loads fill with zeros)."""
+    """Through the cluster kernel (few tiles), the TMA tile kernel (many tiles; three shapes end
+    in a partial tile, which the TMA loads fill with zeros) and, for few tiles of a large tensor
+    at C = 512, the TMA norm followed by the SiLU table kernel."""
     sp = H * W
     x, g = O.randn_bf16(rng, (B, C, sp)), _weight(rng, C)
     dx, dg = dev(x), dev(g)
@@ -638,7 +639,7 @@ def test_channel_scale_shift(anima, ref, rng, B, C, sp):
 # (spatial % 8 != 0), and for the fused norm each of its three kernels: cluster (few tiles),
 # tile (many tiles) and the per-pixel kernel.
 CONV_SHAPES = [(1, 512, 32, 32), (1, 96, 10, 10), (2, 100, 5, 8), (1, 256, 64, 64), (1, 64, 160, 160),
-               (1, 128, 256, 256), (2, 3, 3, 6)]
+               (1, 128, 256, 256), (2, 3, 3, 6), (2, 256, 100, 104), (1, 512, 150, 132), (1, 512, 96, 96)]
 
 
 def _ref_conv_bias(ref, dx, db, B, C, sp):
@@ -704,6 +705,7 @@ def test_conv_bias_rms_norm_channel_silu_matches_reference_chain(anima, ref, rng
     torch.cuda.synchronize()
     assert_bit_exact(host(out), host(r), "conv_bias_rms_norm_channel_silu vs bias + rms_norm_channel + silu")
     assert_bit_exact(host(xi), host(r), "conv_bias_rms_norm_channel_silu in place")
+    assert anima.wait_timeouts() == 0
 
 
 PATCH_SHAPES = [(1, 16, 1, 128, 128, 1, 2, 2), (2, 4, 3, 8, 6, 1, 2, 2), (1, 3, 4, 6, 9, 2, 3, 3),
