@@ -1063,6 +1063,11 @@ def main():
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=device)
     n_gpus = world if dist is not None else 1
+    if n_gpus > 1:
+        # the headline sweep, the other configs and the CPU baseline are single-GPU figures
+        # (the N=1 line carries them); at N > 1 the other ranks would only wait at the final
+        # barrier while rank 0 ran them
+        args.no_headline = args.no_other_ops = args.no_cpu_baseline = True
     if args.workload == "cfg5":
         # 8 images at 1536x1536 -> 192x192 latent -> 96x96 patches = 9216 tokens, x CFG 2; the
         # image pairs are shared out over the GPUs as extra batch rows (rows are independent)
