@@ -87,6 +87,22 @@ __device__ __forceinline__ void add_bias8(anima_bf16 *chunk, uint32_t b2) {
     for (int j = 0; j < 4; ++j) asm("add.rn.bf16x2 %0, %0, %1;" : "+r"(v.w[j]) : "r"(b2));
 }
 
+// vae_kernels.cu:71, q += x*x for the two pixels of a packed bf16 pair: sm_100's mixed-precision
+// fma takes the bf16 halves as multiplicands and the fp32 sum as addend and rounds once, which
+// is fmaf(float(x), float(x), q) exactly (the conversion is exact), in two instructions where
+// unpacking and a packed fp32x2 fma take three -- this serial chain is the kernels' critical
+// path.
+__device__ __forceinline__ float sq_acc_bf16(unsigned short x, float q) {
+    float r;
+    asm("{\n .reg .b16 t;\n mov.b16 t, %1;\n fma.rn.f32.bf16 %0, t, t, %2;\n}\n" : "=f"(r) : "h"(x), "f"(q));
+    return r;
+}
+__device__ __forceinline__ void sq_acc_bf16x2(uint32_t w, float2 &q) {
+    asm("{\n .reg .b16 l, h;\n mov.b32 {l, h}, %2;\n fma.rn.f32.bf16 %0, l, l, %0;\n fma.rn.f32.bf16 %1, h, h, %1;\n}\n"
+        : "+f"(q.x), "+f"(q.y)
+        : "r"(w));
+}
+
 struct CnArgs {
     const anima_bf16 *x, *gamma;
     anima_bf16 *out;
@@ -103,43 +119,6 @@ template <bool kPixel>
 __device__ __forceinline__ float norm_scale(float q, int C, float eps) {
     const float m = __fdiv_rn(q, (float)C) + eps;
     return kPixel ? __fdiv_rn(1.0f, __fsqrt_rn(m)) : rsqrtf(m);
-}
-
-// vae_kernels.cu:68-73: pixel p's serial sum of squares over the C channels of a staged tile
-// ([C][kCnPix] in shared memory), in channel order, with the next 8 channels' loads issued
-// before the current 8 fmas; returns rsqrt(mean + eps). Pixels beyond the tile's live width
-// return the value for a zero sum (unused).
-template <bool kPixel>
-__device__ __forceinline__ float pixel_rms(const anima_bf16 *tile, int p, int live_vecs, int C, float eps) {
-    float q = 0.0f;
-    if (p < live_vecs * 8) {
-        const __nv_bfloat16 *col = reinterpret_cast<const __nv_bfloat16 *>(tile) + p;
-        const int full = C & ~7;
-        float cur[8];
-        if (full > 0) {
-#pragma unroll
-            for (int j = 0; j < 8; ++j) cur[j] = __bfloat162float(col[j * kCnPix]);
-        }
-        for (int c = 0; c < full; c += 8) {
-            float nxt[8];
-            const bool more = c + 8 < full;
-            if (more) {
-#pragma unroll
-                for (int j = 0; j < 8; ++j) nxt[j] = __bfloat162float(col[(c + 8 + j) * kCnPix]);
-            }
-#pragma unroll
-            for (int j = 0; j < 8; ++j) q = __fmaf_rn(cur[j], cur[j], q);
-            if (more) {
-#pragma unroll
-                for (int j = 0; j < 8; ++j) cur[j] = nxt[j];
-            }
-        }
-        for (int c = full; c < C; ++c) {
-            const float f = __bfloat162float(col[c * kCnPix]);
-            q = __fmaf_rn(f, f, q);
-        }
-    }
-    return norm_scale<kPixel>(q, C, eps);
 }
 
 // vae_kernels.cu:75-80 on one staged 16-byte chunk (8 pixels of one channel): (x * rms) * gamma,
@@ -222,19 +201,14 @@ __global__ void __launch_bounds__(T) channel_norm_tile(CnArgs a) {
                 for (int j = 0; j < 8; ++j) nxt[j] = col[(c + 8 + j) * (P / 2)];
             }
 #pragma unroll
-            for (int j = 0; j < 8; ++j) {
-                const float2 f = make_float2(bf_lo(cur[j]), bf_hi(cur[j]));
-                q2 = __ffma2_rn(f, f, q2);
-            }
+            for (int j = 0; j < 8; ++j) sq_acc_bf16x2(cur[j], q2);
             if (more) {
 #pragma unroll
                 for (int j = 0; j < 8; ++j) cur[j] = nxt[j];
             }
         }
         for (int c = full; c < a.C; ++c) {
-            const uint32_t w = col[c * (P / 2)];
-            const float2 f = make_float2(bf_lo(w), bf_hi(w));
-            q2 = __ffma2_rn(f, f, q2);
+            sq_acc_bf16x2(col[c * (P / 2)], q2);
         }
         // pixels beyond the tile's live width hold no data: their values are never used
         reinterpret_cast<float2 *>(rms_s)[threadIdx.x] =
@@ -362,8 +336,7 @@ __global__ void __launch_bounds__(T) channel_norm_tma(const __grid_constant__ CU
                 for (int j = 0; j < 8; ++j) {
                     uint32_t w = cur[j];
                     if constexpr (kBias) asm("add.rn.bf16x2 %0, %0, %1;" : "+r"(w) : "r"(bias_s[c + j]));
-                    const float2 f = make_float2(bf_lo(w), bf_hi(w));
-                    q2 = __ffma2_rn(f, f, q2);
+                    sq_acc_bf16x2(w, q2);
                 }
                 if (more) {
 #pragma unroll
@@ -465,19 +438,16 @@ __global__ void __launch_bounds__(kCnBlock) channel_norm_cluster(CnArgs a, int C
             const int p = threadIdx.x;
             float q = r == 0 ? 0.0f : part_s[p];
             if (p < live_vecs * 8) {
-                const __nv_bfloat16 *col = reinterpret_cast<const __nv_bfloat16 *>(tile) + p;
+                const unsigned short *col = reinterpret_cast<const unsigned short *>(tile) + p;
                 const int n = c1 - c0, full = n & ~7;
                 for (int c = 0; c < full; c += 8) {
-                    float f[8];
+                    unsigned short f[8];
 #pragma unroll
-                    for (int j = 0; j < 8; ++j) f[j] = __bfloat162float(col[(c + j) * kCnPix]);
+                    for (int j = 0; j < 8; ++j) f[j] = col[(c + j) * kCnPix];
 #pragma unroll
-                    for (int j = 0; j < 8; ++j) q = __fmaf_rn(f[j], f[j], q);
+                    for (int j = 0; j < 8; ++j) q = sq_acc_bf16(f[j], q);
                 }
-                for (int c = full; c < n; ++c) {
-                    const float f = __bfloat162float(col[c * kCnPix]);
-                    q = __fmaf_rn(f, f, q);
-                }
+                for (int c = full; c < n; ++c) q = sq_acc_bf16(col[c * kCnPix], q);
             }
             if (r + 1 < kCnCluster) {
                 cluster.map_shared_rank(part_s, r + 1)[p] = q;
