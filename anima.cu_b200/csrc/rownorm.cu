@@ -182,20 +182,53 @@ __device__ __forceinline__ void bvec8(const float *bc, int b, int D, int seg, in
 // per instruction, so results equal the scalar ops bit for bit at half the issue cost.
 __device__ __forceinline__ float2 f2(float a, float b) { return make_float2(a, b); }
 
-// out[e] = fma((x[e] - mean) * inv, mul[e], add[e]) for e < 8, optionally rounding the
-// normalised value to bf16 first.
+// sm_100 mixed-precision fp32 arithmetic with bf16 operands taken straight from a packed pair:
+// each converts its bf16 operand to fp32 exactly and rounds the fp32 result once, so the bits
+// are those of the unpacked scalar op, without the unpacking instructions.
+__device__ __forceinline__ float2 bf2_sub(uint32_t w, float c) {  // (lo - c, hi - c)
+    float2 r;
+    asm("{\n .reg .b16 l, h;\n mov.b32 {l, h}, %2;\n sub.rn.f32.bf16 %0, l, %3;\n sub.rn.f32.bf16 %1, h, %3;\n}\n"
+        : "=f"(r.x), "=f"(r.y)
+        : "r"(w), "f"(c));
+    return r;
+}
+__device__ __forceinline__ float2 bf2_add(uint32_t w, float c) {  // (lo + c, hi + c)
+    float2 r;
+    asm("{\n .reg .b16 l, h;\n mov.b32 {l, h}, %2;\n add.rn.f32.bf16 %0, l, %3;\n add.rn.f32.bf16 %1, h, %3;\n}\n"
+        : "=f"(r.x), "=f"(r.y)
+        : "r"(w), "f"(c));
+    return r;
+}
+__device__ __forceinline__ float2 bf2_fma(uint32_t a, uint32_t b, float2 c) {  // (a.lo*b.lo + c.x, a.hi*b.hi + c.y)
+    float2 r;
+    asm("{\n .reg .b16 al, ah, bl, bh;\n mov.b32 {al, ah}, %2;\n mov.b32 {bl, bh}, %3;\n"
+        " fma.rn.f32.bf16 %0, al, bl, %4;\n fma.rn.f32.bf16 %1, ah, bh, %5;\n}\n"
+        : "=f"(r.x), "=f"(r.y)
+        : "r"(a), "r"(b), "f"(c.x), "f"(c.y));
+    return r;
+}
+
+// The adaLN modulation on packed bf16 words: out = fma((x - mean) * inv, 1 + scale, shift),
+// rounded to bf16 (the normalised value rounded to bf16 first for kRoundFirst; nvcc contracts
+// the reference's n * (1.0f + scale) + shift into this fma, layer_norm.cu:121-122,192-193); x - mean and
+// 1 + scale by the mixed-precision ops above, in the reference's fp32 roundings.
 template <bool kRoundFirst>
-__device__ __forceinline__ void ln_modulate8(const float (&x)[8], float mean, float inv, const float (&mul)[8],
-                                             const float (&add)[8], float (&out)[8]) {
-    const float2 nm = f2(-mean, -mean), iv = f2(inv, inv);
+__device__ __forceinline__ Vec8 ln_modulate_w(const Vec8 &x, float mean, float inv, const Vec8 &scale,
+                                              const Vec8 &shift) {
+    Vec8 o;
 #pragma unroll
-    for (int e = 0; e < 8; e += 2) {
-        float2 n = __fmul2_rn(__fadd2_rn(f2(x[e], x[e + 1]), nm), iv);
+    for (int j = 0; j < 4; ++j) {
+        float2 n = __fmul2_rn(bf2_sub(x.w[j], mean), f2(inv, inv));
         if constexpr (kRoundFirst) n = f2(bf16_round(n.x), bf16_round(n.y));
-        const float2 o = __ffma2_rn(n, f2(mul[e], mul[e + 1]), f2(add[e], add[e + 1]));
-        out[e] = o.x;
-        out[e + 1] = o.y;
+        const float2 r = __ffma2_rn(n, bf2_add(scale.w[j], 1.0f), f2(bf_lo(shift.w[j]), bf_hi(shift.w[j])));
+        o.w[j] = pack_bf2(r.x, r.y);
     }
+    return o;
+}
+
+// Broadcast vector b's staged bf16 chunk k of segment `seg` (the layout bvec8 reads).
+__device__ __forceinline__ const Vec8 &bchunk(const float *bc, int b, int D, int seg, int k) {
+    return reinterpret_cast<const Vec8 *>(bc)[b * (D >> 3) + swz(8 * seg + k)];
 }
 
 __device__ __forceinline__ float bf(const anima_bf16 *p, int i) {
@@ -224,16 +257,13 @@ struct LayerNormOp {  // layer_norm.cu:26-59
         const float inv = rsqrtf(ln_var_p2<64 * NW>(sq, mean) + eps);
 #pragma unroll
         for (int k = 0; k < 8; ++k) {
-            float f[8];
-            unpack8(v[k], f);
-            const float2 nm = f2(-mean, -mean), iv = f2(inv, inv);
+            Vec8 o;
 #pragma unroll
-            for (int e = 0; e < 8; e += 2) {
-                const float2 n = __fmul2_rn(__fadd2_rn(f2(f[e], f[e + 1]), nm), iv);
-                f[e] = n.x;
-                f[e + 1] = n.y;
+            for (int j = 0; j < 4; ++j) {
+                const float2 n = __fmul2_rn(bf2_sub(v[k].w[j], mean), f2(inv, inv));
+                o.w[j] = pack_bf2(n.x, n.y);
             }
-            slot[swz(8 * lane + k)] = pack8(f);
+            slot[swz(8 * lane + k)] = o;
         }
     }
 };
@@ -263,14 +293,9 @@ struct AdaLNOp {
         const float mean = div_pow2<64 * NW>(sum);
         const float inv = rsqrtf(ln_var_p2<64 * NW>(sq, mean) + eps);
 #pragma unroll
-        for (int k = 0; k < 8; ++k) {
-            float f[8], sc[8], sh[8];
-            unpack8(v[k], f);
-            bvec8(bc, 0, D, seg, k, true, sc);
-            bvec8(bc, 1, D, seg, k, false, sh);
-            ln_modulate8<kRoundFirst>(f, mean, inv, sc, sh, f);
-            slot[swz(8 * lane + k)] = pack8(f);
-        }
+        for (int k = 0; k < 8; ++k)
+            slot[swz(8 * lane + k)] =
+                ln_modulate_w<kRoundFirst>(v[k], mean, inv, bchunk(bc, 0, D, seg, k), bchunk(bc, 1, D, seg, k));
     }
 };
 
@@ -297,15 +322,12 @@ struct ResGateAdaLNOp {  // layer_norm.cu:146-196
         float h[8][8];
 #pragma unroll
         for (int k = 0; k < 8; ++k) {
-            float g[8], fx[8], fy[8];
-            bvec8(bc, 0, D, seg, k, false, g);
-            unpack8(x[k], fx);
-            unpack8(y[k], fy);
+            const Vec8 &g = bchunk(bc, 0, D, seg, k);
 #pragma unroll
-            for (int e = 0; e < 8; e += 2) {
-                const float2 hv = __ffma2_rn(f2(fy[e], fy[e + 1]), f2(g[e], g[e + 1]), f2(fx[e], fx[e + 1]));
-                h[k][e] = hv.x;
-                h[k][e + 1] = hv.y;
+            for (int j = 0; j < 4; ++j) {
+                const float2 hv = bf2_fma(y[k].w[j], g.w[j], f2(bf_lo(x[k].w[j]), bf_hi(x[k].w[j])));
+                h[k][2 * j] = hv.x;
+                h[k][2 * j + 1] = hv.y;
             }
         }
         // pairs (h[k][4i], h[k][4i+1]) and (h[k][4i+2], h[k][4i+3]); resid_sq_pair packed
@@ -323,13 +345,9 @@ struct ResGateAdaLNOp {  // layer_norm.cu:146-196
 #pragma unroll
         for (int k = 0; k < 8; ++k) {
             const Vec8 hb = pack8(h[k]);
-            float f[8], sc[8], sh[8];
-            unpack8(hb, f);
-            bvec8(bc, 1, D, seg, k, true, sc);
-            bvec8(bc, 2, D, seg, k, false, sh);
-            ln_modulate8<false>(f, mean, inv, sc, sh, f);
             slot[swz(8 * lane + k)] = hb;
-            slot[kUnitChunks + swz(8 * lane + k)] = pack8(f);
+            slot[kUnitChunks + swz(8 * lane + k)] =
+                ln_modulate_w<false>(hb, mean, inv, bchunk(bc, 1, D, seg, k), bchunk(bc, 2, D, seg, k));
         }
     }
 };
