@@ -67,6 +67,32 @@ __device__ __forceinline__ float2 sq_pair2(uint32_t w0, uint32_t w1) {
     return __ffma2_rn(b, b, __fmul2_rn(a, a));
 }
 
+// sm_100 mixed-precision fp32 arithmetic with bf16 operands taken straight from a packed pair:
+// each converts its bf16 operand to fp32 exactly and rounds the fp32 result once, so the bits
+// are those of the unpacked scalar op, without the unpacking instructions.
+__device__ __forceinline__ float2 bf2_sub(uint32_t w, float c) {  // (lo - c, hi - c)
+    float2 r;
+    asm("{\n .reg .b16 l, h;\n mov.b32 {l, h}, %2;\n sub.rn.f32.bf16 %0, l, %3;\n sub.rn.f32.bf16 %1, h, %3;\n}\n"
+        : "=f"(r.x), "=f"(r.y)
+        : "r"(w), "f"(c));
+    return r;
+}
+__device__ __forceinline__ float2 bf2_add(uint32_t w, float c) {  // (lo + c, hi + c)
+    float2 r;
+    asm("{\n .reg .b16 l, h;\n mov.b32 {l, h}, %2;\n add.rn.f32.bf16 %0, l, %3;\n add.rn.f32.bf16 %1, h, %3;\n}\n"
+        : "=f"(r.x), "=f"(r.y)
+        : "r"(w), "f"(c));
+    return r;
+}
+__device__ __forceinline__ float2 bf2_fma(uint32_t a, uint32_t b, float2 c) {  // (a.lo*b.lo + c.x, a.hi*b.hi + c.y)
+    float2 r;
+    asm("{\n .reg .b16 al, ah, bl, bh;\n mov.b32 {al, ah}, %2;\n mov.b32 {bl, bh}, %3;\n"
+        " fma.rn.f32.bf16 %0, al, bl, %4;\n fma.rn.f32.bf16 %1, ah, bh, %5;\n}\n"
+        : "=f"(r.x), "=f"(r.y)
+        : "r"(a), "r"(b), "f"(c.x), "f"(c.y));
+    return r;
+}
+
 // Round two floats to a packed bf16 pair (RNE), like __floats2bfloat162_rn.
 __device__ __forceinline__ uint32_t pack_bf2(float lo, float hi) {
     __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);

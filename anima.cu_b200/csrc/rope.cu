@@ -38,12 +38,18 @@ __device__ __forceinline__ void rot_f32(float x1, float x2, float c, float s, fl
     o2 = __fmaf_rn(x1, s, x2 * c);
 }
 
-// rot_bf16 on two element pairs at once; each lane of the packed ops rounds as the scalar
-// op does.
-__device__ __forceinline__ void rot_bf16_x2(float2 xr, float2 xi, float2 c, float2 s, float2 &o_r, float2 &o_i) {
-    const float2 t = __fmul2_rn(xi, s);
-    o_r = __ffma2_rn(xr, c, make_float2(-t.x, -t.y));
-    o_i = __ffma2_rn(xi, c, __fmul2_rn(xr, s));
+// rot_bf16 on packed bf16 words (two element pairs): every operand is a bf16 value, so
+// sm_100's mixed-precision fma takes them unpacked-free. xi*s and xr*s are exact products
+// (16 significant bits), formed as fma(a, b, -0.0), which returns the product with its own
+// sign of zero; the outer fmas then round once each, as fmaf(xr, c, -(xi*s)) and
+// fmaf(xi, c, xr*s) do. -(xi*s) is xi*(-s), with the sign flipped on the bf16 word.
+__device__ __forceinline__ void rot_bf16_w(uint32_t xr, uint32_t xi, uint32_t c, uint32_t s, uint32_t &o_r,
+                                           uint32_t &o_i) {
+    const float2 nz = make_float2(-0.0f, -0.0f);
+    const float2 r = bf2_fma(xr, c, bf2_fma(xi, s ^ 0x80008000u, nz));
+    const float2 i = bf2_fma(xi, c, bf2_fma(xr, s, nz));
+    o_r = pack_bf2(r.x, r.y);
+    o_i = pack_bf2(i.x, i.y);
 }
 
 struct CosmosArgs {
@@ -102,15 +108,7 @@ __global__ void __launch_bounds__(kRopeBlock) rope_cosmos_vec(CosmosArgs a) {
         if (!ok[u]) continue;
         Vec8 o_r, o_i;
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            float2 r, m;
-            rot_bf16_x2(make_float2(bf_lo(xr[u].w[j]), bf_hi(xr[u].w[j])),
-                        make_float2(bf_lo(xi[u].w[j]), bf_hi(xi[u].w[j])),
-                        make_float2(bf_lo(cv[u].w[j]), bf_hi(cv[u].w[j])),
-                        make_float2(bf_lo(sv[u].w[j]), bf_hi(sv[u].w[j])), r, m);
-            o_r.w[j] = pack_bf2(r.x, r.y);
-            o_i.w[j] = pack_bf2(m.x, m.y);
-        }
+        for (int j = 0; j < 4; ++j) rot_bf16_w(xr[u].w[j], xi[u].w[j], cv[u].w[j], sv[u].w[j], o_r.w[j], o_i.w[j]);
         st_vec(p[u], o_r);
         st_vec(p[u] + half, o_i);
     }
@@ -268,11 +266,7 @@ __global__ void __launch_bounds__(kRopeBlock) qk_norm_rope_128(QkArgs a) {
         const float2 n1 = __fmul2_rn(__fmul2_rn(make_float2(bf_lo(v[1].w[j]), bf_hi(v[1].w[j])), rr),
                                      make_float2(bf_lo(w[1].w[j]), bf_hi(w[1].w[j])));
         const uint32_t p0 = pack_bf2(n0.x, n0.y), p1 = pack_bf2(n1.x, n1.y);
-        float2 a, b;
-        rot_bf16_x2(make_float2(bf_lo(p0), bf_hi(p0)), make_float2(bf_lo(p1), bf_hi(p1)),
-                    make_float2(bf_lo(cv.w[j]), bf_hi(cv.w[j])), make_float2(bf_lo(sv.w[j]), bf_hi(sv.w[j])), a, b);
-        o0.w[j] = pack_bf2(a.x, a.y);
-        o1.w[j] = pack_bf2(b.x, b.y);
+        rot_bf16_w(p0, p1, cv.w[j], sv.w[j], o0.w[j], o1.w[j]);
     }
     st_vec(p, o0);
     st_vec(p + 64, o1);

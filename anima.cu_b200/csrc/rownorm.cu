@@ -182,32 +182,6 @@ __device__ __forceinline__ void bvec8(const float *bc, int b, int D, int seg, in
 // per instruction, so results equal the scalar ops bit for bit at half the issue cost.
 __device__ __forceinline__ float2 f2(float a, float b) { return make_float2(a, b); }
 
-// sm_100 mixed-precision fp32 arithmetic with bf16 operands taken straight from a packed pair:
-// each converts its bf16 operand to fp32 exactly and rounds the fp32 result once, so the bits
-// are those of the unpacked scalar op, without the unpacking instructions.
-__device__ __forceinline__ float2 bf2_sub(uint32_t w, float c) {  // (lo - c, hi - c)
-    float2 r;
-    asm("{\n .reg .b16 l, h;\n mov.b32 {l, h}, %2;\n sub.rn.f32.bf16 %0, l, %3;\n sub.rn.f32.bf16 %1, h, %3;\n}\n"
-        : "=f"(r.x), "=f"(r.y)
-        : "r"(w), "f"(c));
-    return r;
-}
-__device__ __forceinline__ float2 bf2_add(uint32_t w, float c) {  // (lo + c, hi + c)
-    float2 r;
-    asm("{\n .reg .b16 l, h;\n mov.b32 {l, h}, %2;\n add.rn.f32.bf16 %0, l, %3;\n add.rn.f32.bf16 %1, h, %3;\n}\n"
-        : "=f"(r.x), "=f"(r.y)
-        : "r"(w), "f"(c));
-    return r;
-}
-__device__ __forceinline__ float2 bf2_fma(uint32_t a, uint32_t b, float2 c) {  // (a.lo*b.lo + c.x, a.hi*b.hi + c.y)
-    float2 r;
-    asm("{\n .reg .b16 al, ah, bl, bh;\n mov.b32 {al, ah}, %2;\n mov.b32 {bl, bh}, %3;\n"
-        " fma.rn.f32.bf16 %0, al, bl, %4;\n fma.rn.f32.bf16 %1, ah, bh, %5;\n}\n"
-        : "=f"(r.x), "=f"(r.y)
-        : "r"(a), "r"(b), "f"(c.x), "f"(c.y));
-    return r;
-}
-
 // The adaLN modulation on packed bf16 words: out = fma((x - mean) * inv, 1 + scale, shift),
 // rounded to bf16 (the normalised value rounded to bf16 first for kRoundFirst; nvcc contracts
 // the reference's n * (1.0f + scale) + shift into this fma, layer_norm.cu:121-122,192-193); x - mean and
