@@ -639,10 +639,14 @@ extern "C" int anima_pixel_norm_bf16(const anima_bf16 *x, anima_bf16 *out, int B
 
 extern "C" int anima_wait_timeouts(unsigned int *count, int reset) {
     if (!count) return ANIMA_ERR_NULL_POINTER;
-    cudaError_t e = cudaMemcpyFromSymbol(count, g_cn_wait_timeouts, sizeof(unsigned int));
+    unsigned int cn = 0, ew = 0;
+    cudaError_t e = cudaMemcpyFromSymbol(&cn, g_cn_wait_timeouts, sizeof(unsigned int));
     if (e == cudaSuccess && reset) {
         const unsigned int zero = 0;
         e = cudaMemcpyToSymbol(g_cn_wait_timeouts, &zero, sizeof(unsigned int));
     }
-    return e == cudaSuccess ? ANIMA_OK : (int)e;
+    if (e != cudaSuccess) return (int)e;
+    if (int st = ew_wait_timeouts(&ew, reset)) return st;
+    *count = cn + ew;
+    return ANIMA_OK;
 }

@@ -270,6 +270,11 @@ __device__ __forceinline__ void pdl_launch() { asm volatile("griddepcontrol.laun
 // Number of SMs of the current device (cached per device ordinal).
 int sm_count();
 
+// Bounded device waits of the elementwise table kernel that ran out on the current device
+// (elementwise.cu; cleared when reset != 0). anima_wait_timeouts reports them with the
+// channel norm's.
+int ew_wait_timeouts(unsigned int *count, int reset);
+
 // Raises a kernel's dynamic shared-memory limit to `bytes` on the current device, once
 // per (device, slot); `slot` names the kernel (0..63). Returns ANIMA_OK or a cudaError_t.
 int allow_dynamic_smem(const void *kernel, int bytes, int slot);

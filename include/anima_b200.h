@@ -52,8 +52,8 @@ ANIMA_API const char *anima_status_string(int status);
 ANIMA_API const char *anima_version(void);
 
 /* Bounded waits that ran out on the current device: the kernels that stage data with the TMA
- * unit (the channel norm's tile kernel) wait on mbarriers with an iteration limit instead of
- * forever; a CTA whose wait runs out skips its output and counts here. Never expected in
+ * unit (the channel norm's tile kernel, the GELU / SiLU table kernel) wait on mbarriers with an
+ * iteration limit instead of forever; a CTA whose wait runs out skips its output and counts here. Never expected in
  * normal operation. Writes the count to *count (and clears it when reset != 0); call after
  * synchronizing the streams that ran those kernels. New in this library (the reference's
  * kernels have no waits). */

@@ -277,16 +277,16 @@ def test_unary_extreme_inputs(anima, ref, op):
 
 
 @pytest.mark.parametrize("op", ["gelu_tanh", "silu"])
-@pytest.mark.parametrize("reps", [1, 8, 9])
+@pytest.mark.parametrize("reps", [1, 8, 9, 513])
 def test_unary_exhaustive(anima, ref, op, reps):
     """GELU and SiLU map one bf16 input to one bf16 output, so all 65536 inputs (both
     zeros, subnormals, Inf, every NaN payload) settle parity completely. 131072 elements
     take the table-free kernel (approximation + exact-formula fallback); 2^20 and more take
-    the shared-memory table kernel, whose table the exact formula filled; the extra 6
-    elements at reps = 9 exercise its scalar tail."""
+    the shared-memory table kernel, whose table the exact formula filled (from 2^26, as at
+    reps = 513, its TMA-fed form); the extra 6 elements at odd reps exercise the scalar tail."""
     x = np.arange(65536, dtype=np.uint32).astype(np.uint16)
     x = np.tile(np.concatenate([x, x[::-1]]), reps)  # both halves of a bf16 pair see every value
-    if reps == 9:
+    if reps > 1 and reps % 2:
         x = np.concatenate([x, x[:6]])
     dx = dev(x)
     n = x.size
@@ -295,6 +295,7 @@ def test_unary_exhaustive(anima, ref, op, reps):
     getattr(ref, op + "_bf16")(dx.data_ptr(), out_ref.data_ptr(), n, stream_ptr())
     torch.cuda.synchronize()
     assert np.array_equal(host(out), host(out_ref)), f"{op}: {int((host(out) != host(out_ref)).sum())} of {n} differ"
+    assert anima.wait_timeouts() == 0
 
 
 def test_swiglu_exhaustive_gate(anima, ref, rng):
