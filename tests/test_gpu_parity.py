@@ -295,6 +295,11 @@ def test_unary_exhaustive(anima, ref, op, reps):
     getattr(ref, op + "_bf16")(dx.data_ptr(), out_ref.data_ptr(), n, stream_ptr())
     torch.cuda.synchronize()
     assert np.array_equal(host(out), host(out_ref)), f"{op}: {int((host(out) != host(out_ref)).sum())} of {n} differ"
+    if reps == 513:  # in place, as the DiT FFN calls it (llm_adapter.cpp:301), through the TMA-fed form
+        xi = dev(x)
+        getattr(anima, op)(xi, xi, n)
+        torch.cuda.synchronize()
+        assert np.array_equal(host(xi), host(out_ref)), f"{op} in place"
     assert anima.wait_timeouts() == 0
 
 
