@@ -589,9 +589,9 @@ __global__ void __launch_bounds__(kRowBlock) rms_small(const anima_bf16 *x, cons
             const float a = bf_lo(v[k].w[j]), b = bf_hi(v[k].w[j]);
             q[k][j] = fmaf(b, b, a * a);
         }
-    // Scalar squares and the division kept on purpose: packed squares (sq_pair2) and the
-    // exact multiply by 1/D (div_pow2) each made this load-latency-bound kernel slower
-    // (6.61 -> 6.81 us at [4096 x 16, 128], 11.46 -> 11.65 at [8192 x 16, 128]).
+    // Scalar squares and the division kept on purpose: packed squares (sq_pair2), squares on
+    // the mixed-precision bf16 fma and the exact multiply by 1/D (div_pow2) each made this
+    // load-latency-bound kernel slower (6.61 -> 6.80-6.84 us at [4096 x 16, 128]).
     const float r = rsqrtf(__fdiv_rn(ref_pair_tree_sum<LPR, K>(q, l, kFull), (float)D) + eps);
     pdl_launch();
     if (!live) return;
