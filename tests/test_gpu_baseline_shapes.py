@@ -9,7 +9,7 @@ import pytest
 import torch
 
 import oracle as O
-from gpu_util import assert_bit_exact, assert_bit_exact_or_reference_race, empty_bf16, host, stream_ptr
+from gpu_util import assert_bit_exact, assert_bit_exact_or_reference_race, empty_bf16, fresh_run, host, stream_ptr
 
 pytestmark = pytest.mark.gpu
 
@@ -37,13 +37,16 @@ def test_row_norms_at_dit_rows(anima, ref, N):
     anima.adaln_layernorm(x, sc, sh, out, N, D, 1e-6)
     ref.adaln_layernorm_bf16(P(x), P(sc), P(sh), P(out_ref), N, D, 1e-6, stream_ptr())
     torch.cuda.synchronize()
-    assert_bit_exact_or_reference_race(host(out), host(out_ref),
-                                       lambda: O.adaln_layernorm(xs, host(sc), host(sh), N, D), "adaln_layernorm")
+    assert_bit_exact_or_reference_race(
+        host(out), host(out_ref), lambda: O.adaln_layernorm(xs, host(sc), host(sh), N, D), "adaln_layernorm",
+        fresh_run(lambda r: ref.adaln_layernorm_bf16(P(x), P(sc), P(sh), P(r), N, D, 1e-6, stream_ptr()), (N, D)))
 
     anima.layer_norm(x, out, N, D, 1e-6)
     ref.layer_norm_bf16(P(x), P(out_ref), N, D, 1e-6, stream_ptr())
     torch.cuda.synchronize()
-    assert_bit_exact_or_reference_race(host(out), host(out_ref), lambda: O.layer_norm(xs, N, D), "layer_norm")
+    assert_bit_exact_or_reference_race(
+        host(out), host(out_ref), lambda: O.layer_norm(xs, N, D), "layer_norm",
+        fresh_run(lambda r: ref.layer_norm_bf16(P(x), P(r), N, D, 1e-6, stream_ptr()), (N, D)))
 
     anima.rms_norm(x, w, out, N, D, 1e-6)
     ref.rms_norm_bf16(P(x), P(w), P(out_ref), N, D, 1e-6, stream_ptr())
@@ -63,7 +66,9 @@ def test_row_norms_at_dit_rows(anima, ref, N):
     assert_bit_exact(host(h), host(h_ref), "residual_gate_adaln hidden")
     assert_bit_exact_or_reference_race(
         host(out), host(out_ref), lambda: O.residual_gate_adaln(hx(), host(y), host(g), host(sc), host(sh), N, D)[1],
-        "residual_gate_adaln normed")
+        "residual_gate_adaln normed",
+        fresh_run(lambda r, hid=h_ref: (hid.copy_(x), ref.residual_gate_adaln_bf16(  # hidden from x each run
+            P(hid), P(y), P(g), P(sc), P(sh), P(r), N, D, 1e-6, stream_ptr())), (N, D)))
 
 
 def test_rope_cosmos_cfg5_grid(anima, ref):
