@@ -571,13 +571,19 @@ def test_pixel_norm(anima, ref, rng, B, C, H, W):
         assert_one_ulp(host(out), O.pixel_norm(x, B, C, sp), "pixel_norm vs oracle")
 
 
+# Large fused-SiLU tensors (>= 2^24 elements) at C = 128 / 256 that end in a partial tile,
+# with several images (B > 1) in one launch.
+CN_LARGE_SHAPES = [(2, 128, 260, 260), (3, 256, 150, 152)]
+
+
 @pytest.mark.parametrize("B,C,H,W", [(1, 512, 32, 32), (1, 96, 10, 10), (2, 100, 5, 8), (1, 256, 64, 64),
                                      (1, 64, 160, 160), (1, 128, 150, 132), (2, 256, 100, 104),
-                                     (1, 512, 150, 132), (1, 512, 96, 96)])
+                                     (1, 512, 150, 132), (1, 512, 96, 96)] + CN_LARGE_SHAPES)
 def test_rms_norm_channel_silu_matches_reference_chain(anima, ref, rng, B, C, H, W):
     """Through the cluster kernel (few tiles), the TMA tile kernel (many tiles; three shapes end
-    in a partial tile, which the TMA loads fill with zeros) and, for few tiles of a large tensor
-    at C = 512, the TMA norm followed by the SiLU table kernel."""
+    in a partial tile, which the TMA loads fill with zeros; CN_LARGE_SHAPES at full size) and,
+    for few tiles of a large tensor at C = 512, the TMA norm followed by the SiLU table
+    kernel."""
     sp = H * W
     x, g = O.randn_bf16(rng, (B, C, sp)), _weight(rng, C)
     dx, dg = dev(x), dev(g)
@@ -706,7 +712,7 @@ def test_conv_bias_residual_add_matches_reference_chain(anima, ref, rng, B, C, H
         assert_bit_exact(host(out), O.conv_bias_add(x, b, B, C, sp, residual=res), "conv_bias_residual_add vs oracle")
 
 
-@pytest.mark.parametrize("B,C,H,W", CONV_SHAPES)
+@pytest.mark.parametrize("B,C,H,W", CONV_SHAPES + CN_LARGE_SHAPES)
 def test_conv_bias_rms_norm_channel_silu_matches_reference_chain(anima, ref, rng, B, C, H, W):
     sp = H * W
     x, b, g = O.randn_bf16(rng, (B, C, sp)), O.randn_bf16(rng, C, std=0.5), _weight(rng, C)
